@@ -1,0 +1,164 @@
+/*
+ * logitfill_b200 -- C ABI of the B200 packed KV-cache hot path.
+ *
+ * Drop-in replacement for the device side of LogitFill's `packed` backend
+ * (GASSFY/Logitfill, src/logitfill/packed/).  Every entry point takes plain
+ * device pointers, sizes and a cudaStream_t, allocates nothing, launches on
+ * the given stream and returns an lf_status (0 = success).  No torch types.
+ *
+ * History layout in HBM (one layer):
+ *   rows   int32 [batch][kv_heads][row_cap][row_words]   one row per token:
+ *            INT2 | INT4 | INT8 Key codes (packed along tier channels, slot 0
+ *            in the low bits, as layout.py:21-35 packs them), Value codes
+ *            (packed along head_dim), then an fp16 region holding the FP16
+ *            Key tier, the Value scales and the Value mins.
+ *   kmeta  fp16  [batch][kv_heads][group_cap][meta_halves]  one row per Key
+ *            group (k_group tokens): scale and min of every INT2/INT4/INT8
+ *            tier channel.
+ * Every per-sequence array of the reference (layout.py:71-129, stored as
+ * cache.py:64-81 concatenates it) is a strided view of these two buffers, so
+ * the reference's shapes and bytes are recovered without copying.
+ *
+ * Thread safety: entry points are reentrant; kernels on one stream run in
+ * order.  Calls that share an output buffer must be ordered by the caller.
+ */
+#ifndef LOGITFILL_B200_H
+#define LOGITFILL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define LF_API __attribute__((visibility("default")))
+#else
+#define LF_API
+#endif
+
+typedef struct CUstream_st* lf_stream_t; /* == cudaStream_t */
+
+enum lf_status {
+  LF_OK = 0,
+  LF_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, inconsistent layout  */
+  LF_ERR_UNSUPPORTED = 2,      /* geometry this build does not implement           */
+  LF_ERR_LAUNCH = 3,           /* the CUDA launch failed (see lf_last_error)       */
+  LF_ERR_DEVICE_TIMEOUT = 4,   /* a bounded device-side wait gave up               */
+  LF_ERR_OUT_OF_RANGE = 5      /* a device-side bounds check rejected a job        */
+};
+
+enum lf_dtype { LF_F32 = 0, LF_F16 = 1, LF_BF16 = 2 };
+
+typedef struct lf_layout {
+  int32_t kv_heads;     /* H                                                     */
+  int32_t head_dim;     /* D                                                     */
+  int32_t page_size;    /* tokens per packed page (flush unit)                   */
+  int32_t k_group;      /* Key scale/min group along tokens, divides page_size   */
+  int32_t v_group;      /* Value scale/min group along channels, divides D       */
+  int32_t bit_v;        /* Value code bits                                       */
+  int32_t width[4];     /* channels per tier, max over heads: INT2 INT4 INT8 FP16 */
+  int32_t words[3];     /* int32 words per token of the INT2 INT4 INT8 codes     */
+  int32_t code_off[3];  /* word offset of each tier's codes in a row             */
+  int32_t vcode_off;    /* word offset of the Value codes                        */
+  int32_t vcode_words;  /* D * bit_v / 32                                        */
+  int32_t half_off;     /* word offset of the fp16 region                        */
+  int32_t row_words;    /* words per row, multiple of 4                          */
+  int32_t meta_halves;  /* fp16 per Key-group meta row, multiple of 8            */
+  int32_t scale_off[3]; /* fp16 offset of each tier's scales in a meta row       */
+  int32_t min_off[3];   /* fp16 offset of each tier's mins in a meta row         */
+  int64_t row_cap;      /* rows reserved per (sequence, head), multiple of page  */
+  int64_t group_cap;    /* meta rows reserved per (sequence, head)               */
+} lf_layout;
+
+/*
+ * Channel tables (device int32, built once per layer from the [H][D] level
+ * map of layout.py:49-68):
+ *   chan_code [H][D]    (tier << 16) | position of the channel inside its tier
+ *   slot_chan [4][H][D] channel held by tier slot i, -1 past the head's count
+ */
+
+/* Fill *out from the per-head tier channel counts (host int32 [4][H]:
+ * INT2, INT4, INT8, FP16).  Replaces the width bookkeeping of
+ * layout.py:57,82-85 and the concatenation layout of cache.py:64-81. */
+LF_API int lf_layout_init(lf_layout* out, int kv_heads, int head_dim, int page_size, int k_group,
+                   int v_group, int bit_v, const int32_t* tier_counts, int64_t row_cap,
+                   int64_t group_cap);
+
+/*
+ * K1: quantize and pack whole pages (layout.py:71-129 quantize_key_page +
+ * quantize_value_page, written where cache.py:64-81 would concatenate them).
+ * Bit-exact with the reference: IEEE fp32 divide, round-half-even, fp16 RNE.
+ * src_k/src_v: [seq][head][token][D] with the given element strides (channel
+ * stride 1), dtype src_dtype.  jobs (device int32 [n_jobs][4]):
+ * {src_seq, src_token0, dst_seq, dst_page}.  dst_batch bounds dst_seq; a job
+ * outside [0, dst_batch) x [0, row_cap/page_size) is skipped and
+ * LF_ERR_OUT_OF_RANGE is or-ed into *status (device int32, may be NULL).
+ */
+LF_API int lf_pack_pages(const lf_layout* layout, const void* src_k, const void* src_v, int src_dtype,
+                  int64_t src_seq_stride, int64_t src_head_stride, int64_t src_tok_stride,
+                  const int32_t* jobs, int n_jobs, int dst_batch, const int32_t* chan_code,
+                  int32_t* rows, uint16_t* kmeta, int32_t* status, lf_stream_t stream);
+
+/*
+ * Dequantize tokens [0, tokens) of one sequence to fp32 [H][tokens][D]
+ * (layout.py:132-182; code * scale + min as separately rounded multiply and
+ * add, so the round trip is bit-exact with the reference).
+ */
+LF_API int lf_dequantize(const lf_layout* layout, const int32_t* rows, const uint16_t* kmeta,
+                  const int32_t* chan_code, int seq, int64_t tokens, float* out_k, float* out_v,
+                  lf_stream_t stream);
+
+/* Bytes of fp32 split partials K2 writes and K3 reads. */
+LF_API size_t lf_decode_workspace_bytes(int batch, int kv_heads, int n_q, int head_dim, int max_splits);
+
+/* Number of splits (page splits + 1 residual split) for a history of
+ * max_pages pages cut into pages_per_split. */
+LF_API int lf_decode_max_splits(int64_t max_pages, int pages_per_split);
+
+/*
+ * K2: split-K GQA decode attention over the packed history plus the
+ * original-dtype residual page and the new token (replaces kernel.cu:112-190
+ * launched from reference.py:59-109).  One work item per (sequence, KV head,
+ * split); split s < ceil(pages/pages_per_split) covers pages
+ * [s*pps, min((s+1)*pps, pages)), the next split covers the residual tokens
+ * (tail_len[b] tail rows followed by the new token when k_new is not NULL).
+ * Writes an unnormalised partial (running max m, sum l, accumulator) per
+ * (item, q-head) into workspace.
+ *   hist_tokens [batch] device int32, multiple of page_size
+ *   tail_k/tail_v [batch][H][page_size][D] (strides tail_seq_stride,
+ *     tail_head_stride elements; token stride D), dtype resid_dtype
+ *   tail_len [batch] device int32 in [0, page_size)
+ *   k_new/v_new [batch][H][D] (strides new_seq_stride, new_head_stride), resid_dtype, or NULL
+ *   q [batch][n_q][D] (strides q_seq_stride, q_head_stride), dtype q_dtype
+ * q-head j of KV head h is h * (n_q / H) + j (repeat_kv, reference.py:10-15).
+ */
+LF_API int lf_decode_partial(const lf_layout* layout, const int32_t* rows, const uint16_t* kmeta,
+                      const int32_t* slot_chan, const int32_t* hist_tokens, const void* tail_k,
+                      const void* tail_v, int64_t tail_seq_stride, int64_t tail_head_stride,
+                      const int32_t* tail_len, int resid_dtype, const void* k_new,
+                      const void* v_new, int64_t new_seq_stride, int64_t new_head_stride,
+                      const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
+                      int batch, int n_q, float scaling, int pages_per_split, int max_splits,
+                      float* workspace, lf_stream_t stream);
+
+/*
+ * K3: merge the split partials into the attention output
+ * out [batch][n_q][D] (strides out_seq_stride, out_head_stride), dtype out_dtype.
+ * Softmax-exact: out = sum_s e^(m_s - M) acc_s / sum_s e^(m_s - M) l_s.
+ */
+LF_API int lf_decode_merge(const float* workspace, const int32_t* hist_tokens, int batch, int kv_heads,
+                    int n_q, int head_dim, int page_size, int pages_per_split, int max_splits,
+                    void* out, int out_dtype, int64_t out_seq_stride, int64_t out_head_stride,
+                    lf_stream_t stream);
+
+/* Human-readable text of a status code; detail of the last failure on this thread. */
+LF_API const char* lf_status_string(int status);
+LF_API const char* lf_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LOGITFILL_B200_H */

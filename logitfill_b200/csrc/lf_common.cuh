@@ -1,0 +1,74 @@
+// Shared device helpers of the logitfill_b200 kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "logitfill_b200.h"
+
+namespace lf {
+
+// Per-thread error text for lf_last_error().
+void set_error(const char* fmt, ...);
+int launch_status(const char* what);
+
+template <typename T> struct Scalar;
+template <> struct Scalar<float> {
+  static __device__ __forceinline__ float load(const float* p) { return *p; }
+  static __device__ __forceinline__ void store(float* p, float v) { *p = v; }
+};
+template <> struct Scalar<__half> {
+  static __device__ __forceinline__ float load(const __half* p) { return __half2float(*p); }
+  static __device__ __forceinline__ void store(__half* p, float v) { *p = __float2half_rn(v); }
+};
+template <> struct Scalar<__nv_bfloat16> {
+  static __device__ __forceinline__ float load(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+  static __device__ __forceinline__ void store(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+};
+
+__device__ __forceinline__ float half_bits_to_float(uint16_t bits) {
+  return __half2float(__ushort_as_half(bits));
+}
+__device__ __forceinline__ uint16_t float_to_half_bits(float v) {
+  return __half_as_ushort(__float2half_rn(v));
+}
+
+// Reference asymmetric min-max step (layout.py:12-18), bit-exact with torch
+// CPU fp32: IEEE subtract and divide, clamp to [1e-5, 1e5].
+__device__ __forceinline__ float asym_scale(float hi, float lo, int bits) {
+  const float qmax = static_cast<float>((1 << bits) - 1);
+  float s = __fdiv_rn(__fsub_rn(hi, lo), qmax);
+  s = fmaxf(s, 1e-5f);
+  s = fminf(s, 1e5f);
+  return s;
+}
+__device__ __forceinline__ uint32_t asym_code(float x, float lo, float scale, int bits) {
+  float c = rintf(__fdiv_rn(__fsub_rn(x, lo), scale));  // round half to even
+  const float qmax = static_cast<float>((1 << bits) - 1);
+  c = fmaxf(c, 0.0f);
+  c = fminf(c, qmax);
+  return static_cast<uint32_t>(c);
+}
+
+template <typename F>
+__device__ __forceinline__ void dispatch_noop(F) {}
+
+}  // namespace lf
+
+#define LF_CHECK_ARG(cond, ...)                 \
+  do {                                          \
+    if (!(cond)) {                              \
+      lf::set_error(__VA_ARGS__);               \
+      return LF_ERR_INVALID_ARGUMENT;           \
+    }                                           \
+  } while (0)
+
+#define LF_CHECK_SUPPORTED(cond, ...)           \
+  do {                                          \
+    if (!(cond)) {                              \
+      lf::set_error(__VA_ARGS__);               \
+      return LF_ERR_UNSUPPORTED;                \
+    }                                           \
+  } while (0)

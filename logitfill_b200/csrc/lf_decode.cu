@@ -1,0 +1,553 @@
+// K2 (split-K GQA decode over packed pages + residual) and K3 (split merge).
+//
+// Work item = (split s, KV head h, sequence b); one 128-thread CTA each.
+// All q-heads of the GQA group are computed together, so each packed page is
+// read from HBM once per KV head (the reference kernel re-reads it once per
+// q-head, kernel.cu:112-190).
+//
+// The packed history is affine per page: a Key channel's scale/min is
+// constant over its k_group tokens and a token's Value scale/min is constant
+// over its v_group channels.  So
+//   q.k_t = sum_c (q_c s_c) code_tc + sum_c q_c m_c        (per-page q' and bias)
+//   sum_t p_t v_t = sum_t (p_t s_t) code_t + (sum_t p_t m_t) 1
+// and the inner loops multiply raw integer codes by precomputed fp32 factors.
+#include <atomic>
+
+#include "lf_common.cuh"
+
+namespace lf {
+
+constexpr int kDecThreads = 128;
+constexpr int kGQ = 8;        // q-heads per KV head handled by one CTA
+constexpr int kResChunk = 32; // residual tokens per chunk
+
+struct DecodeParams {
+  lf_layout L;
+  const int32_t* rows;
+  const uint16_t* kmeta;
+  const int32_t* slot_chan;
+  const int32_t* hist_tokens;
+  const void* tail_k;
+  const void* tail_v;
+  int64_t tail_seq_stride, tail_head_stride;
+  const int32_t* tail_len;
+  const void* k_new;
+  const void* v_new;
+  int64_t new_seq_stride, new_head_stride;
+  const void* q;
+  int64_t q_seq_stride, q_head_stride;
+  int batch, n_q, gq, pps, max_splits, n_slots;
+  float scaling;
+  float* ws;
+};
+
+struct DecodeSmem {
+  int q, qp, p, red, slot, slot16, region, rows_bytes, total;
+};
+
+__host__ __device__ inline DecodeSmem decode_smem(const lf_layout& L, int n_slots) {
+  const int D = L.head_dim, P = L.page_size;
+  DecodeSmem s;
+  int off = 0;
+  s.q = off; off += kGQ * D * 4;
+  s.qp = off; off += ((n_slots + 3) / 4 * 4) * kGQ * 4;
+  s.p = off; off += (P > kResChunk ? P : kResChunk) * kGQ * 4;
+  s.red = off; off += 2 * (kDecThreads / 32) * kGQ * 4;
+  s.slot = off; off += ((n_slots + 3) / 4 * 4) * 4;
+  s.slot16 = off; off += ((L.width[3] + 3) / 4 * 4) * 4;
+  off = (off + 15) / 16 * 16;
+  s.region = off;
+  const int page_bytes = P * L.row_words * 4 + (L.meta_halves * 2 + 15) / 16 * 16;
+  const int resid_bytes = 2 * kResChunk * D * 4 + kResChunk * kGQ * 4;
+  s.rows_bytes = page_bytes;
+  off += page_bytes > resid_bytes ? page_bytes : resid_bytes;
+  s.total = (off + 15) / 16 * 16;
+  return s;
+}
+
+// Sum (or max) of kGQ values over the CTA; every thread receives the result.
+template <bool kMax>
+__device__ __forceinline__ void block_reduce8(float (&v)[kGQ], float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int j = 0; j < kGQ; ++j) {
+    float x = v[j];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float y = __shfl_xor_sync(0xffffffffu, x, o);
+      x = kMax ? fmaxf(x, y) : x + y;
+    }
+    v[j] = x;
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int j = 0; j < kGQ; ++j) red[warp * kGQ + j] = v[j];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < kGQ; ++j) {
+    float x = red[j];
+#pragma unroll
+    for (int w = 1; w < kDecThreads / 32; ++w) x = kMax ? fmaxf(x, red[w * kGQ + j]) : x + red[w * kGQ + j];
+    v[j] = x;
+  }
+  __syncthreads();
+}
+
+template <typename RT, typename QT>
+__global__ void __launch_bounds__(kDecThreads)
+decode_partial_simt(DecodeParams p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const lf_layout& L = p.L;
+  const DecodeSmem S = decode_smem(L, p.n_slots);
+  float* q_s = reinterpret_cast<float*>(smem + S.q);
+  float* qp_s = reinterpret_cast<float*>(smem + S.qp);
+  float* p_s = reinterpret_cast<float*>(smem + S.p);
+  float* red = reinterpret_cast<float*>(smem + S.red);
+  int* slot_s = reinterpret_cast<int*>(smem + S.slot);
+  int* slot16_s = reinterpret_cast<int*>(smem + S.slot16);
+  unsigned char* region = smem + S.region;
+
+  const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
+  const int P = L.page_size, D = L.head_dim, R = L.row_words, H = L.kv_heads;
+  const int GQ = p.gq;
+  const int pages = p.hist_tokens[b] / P;
+  const int n_page_splits = (pages + p.pps - 1) / p.pps;
+  if (s > n_page_splits) return;
+
+  // Query group, q-heads h*GQ .. h*GQ+GQ-1 (repeat_kv order, reference.py:10-15).
+  const QT* qb = static_cast<const QT*>(p.q) + b * p.q_seq_stride;
+  for (int i = tid; i < kGQ * D; i += kDecThreads) {
+    const int j = i / D, d = i - j * D;
+    q_s[i] = j < GQ ? Scalar<QT>::load(qb + (h * GQ + j) * p.q_head_stride + d) : 0.0f;
+  }
+  // Tier slot -> channel, in history-row order.
+  for (int i = tid; i < p.n_slots; i += kDecThreads) {
+    int tier = 0, base = 0;
+    while (tier < 2 && i >= base + (32 / (2 << tier)) * L.words[tier]) {
+      base += (32 / (2 << tier)) * L.words[tier];
+      ++tier;
+    }
+    const int local = i - base;
+    const int ch = local < L.width[tier] ? p.slot_chan[(tier * H + h) * D + local] : -1;
+    // channel | tier << 16 | position << 18, or -1 for a padding slot (code 0).
+    slot_s[i] = ch < 0 ? -1 : (ch | (tier << 16) | (local << 18));
+  }
+  for (int i = tid; i < L.width[3]; i += kDecThreads) slot16_s[i] = p.slot_chan[(3 * H + h) * D + i];
+
+  float m[kGQ], acc[kGQ], lt[kGQ], lvt[kGQ];
+#pragma unroll
+  for (int j = 0; j < kGQ; ++j) {
+    m[j] = -INFINITY;
+    acc[j] = 0.f;
+    lt[j] = 0.f;
+    lvt[j] = 0.f;
+  }
+
+  if (s < n_page_splits) {
+    int32_t* row_s = reinterpret_cast<int32_t*>(region);
+    uint16_t* meta_s = reinterpret_cast<uint16_t*>(region + P * R * 4);
+    const uint16_t* row16_s = reinterpret_cast<const uint16_t*>(row_s);
+    const int pg0 = s * p.pps;
+    const int pg1 = min(pages, pg0 + p.pps);
+    const int64_t head_row = (static_cast<int64_t>(b) * H + h) * L.row_cap;
+    const int64_t head_meta = (static_cast<int64_t>(b) * H + h) * L.group_cap;
+    for (int pg = pg0; pg < pg1; ++pg) {
+      __syncthreads();
+      const int4* src = reinterpret_cast<const int4*>(p.rows + (head_row + static_cast<int64_t>(pg) * P) * R);
+      int4* dst = reinterpret_cast<int4*>(row_s);
+      for (int i = tid; i < P * R / 4; i += kDecThreads) dst[i] = __ldg(src + i);
+      const int4* msrc = reinterpret_cast<const int4*>(p.kmeta + (head_meta + pg) * L.meta_halves);
+      for (int i = tid; i < L.meta_halves / 8; i += kDecThreads)
+        reinterpret_cast<int4*>(meta_s)[i] = __ldg(msrc + i);
+      __syncthreads();
+
+      // Per-page q' = q * scale (per slot) and bias = sum_c q_c * min_c.
+      float bias[kGQ];
+#pragma unroll
+      for (int j = 0; j < kGQ; ++j) bias[j] = 0.f;
+      for (int i = tid; i < p.n_slots; i += kDecThreads) {
+        const int e = slot_s[i];
+        float* dstq = qp_s + i * kGQ;
+        if (e < 0) {
+#pragma unroll
+          for (int j = 0; j < kGQ; ++j) dstq[j] = 0.f;
+          continue;
+        }
+        const int ch = e & 0xFFFF, tier = (e >> 16) & 3, local = (e >> 18) & 0x1FFF;
+        const float sc = half_bits_to_float(meta_s[L.scale_off[tier] + local]);
+        const float mn = half_bits_to_float(meta_s[L.min_off[tier] + local]);
+#pragma unroll
+        for (int j = 0; j < kGQ; ++j) {
+          const float qv = q_s[j * D + ch];
+          dstq[j] = qv * sc;
+          bias[j] = fmaf(qv, mn, bias[j]);
+        }
+      }
+      block_reduce8<false>(bias, red);
+
+      float sc_t[kGQ];
+      if (tid < P) {
+#pragma unroll
+        for (int j = 0; j < kGQ; ++j) sc_t[j] = bias[j];
+        const uint32_t* row = reinterpret_cast<const uint32_t*>(row_s + tid * R);
+        int slot = 0;
+#pragma unroll
+        for (int tier = 0; tier < 3; ++tier) {
+          const int bits = 2 << tier, per = 32 / bits;
+          const uint32_t mask = (1u << bits) - 1u;
+          for (int w = 0; w < L.words[tier]; ++w) {
+            const uint32_t x = row[L.code_off[tier] + w];
+            for (int k = 0; k < per; ++k, ++slot) {
+              const float c = static_cast<float>((x >> (k * bits)) & mask);
+              const float4 a = *reinterpret_cast<const float4*>(qp_s + slot * kGQ);
+              const float4 bq = *reinterpret_cast<const float4*>(qp_s + slot * kGQ + 4);
+              sc_t[0] = fmaf(a.x, c, sc_t[0]);
+              sc_t[1] = fmaf(a.y, c, sc_t[1]);
+              sc_t[2] = fmaf(a.z, c, sc_t[2]);
+              sc_t[3] = fmaf(a.w, c, sc_t[3]);
+              sc_t[4] = fmaf(bq.x, c, sc_t[4]);
+              sc_t[5] = fmaf(bq.y, c, sc_t[5]);
+              sc_t[6] = fmaf(bq.z, c, sc_t[6]);
+              sc_t[7] = fmaf(bq.w, c, sc_t[7]);
+            }
+          }
+        }
+        const uint16_t* r16 = row16_s + tid * 2 * R + 2 * L.half_off;
+        for (int i = 0; i < L.width[3]; ++i) {
+          const int ch = slot16_s[i];
+          if (ch < 0) continue;
+          const float kv = half_bits_to_float(r16[i]);
+#pragma unroll
+          for (int j = 0; j < kGQ; ++j) sc_t[j] = fmaf(q_s[j * D + ch], kv, sc_t[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < kGQ; ++j) sc_t[j] = j < GQ ? sc_t[j] * p.scaling : -INFINITY;
+      } else {
+#pragma unroll
+        for (int j = 0; j < kGQ; ++j) sc_t[j] = -INFINITY;
+      }
+      float pm[kGQ];
+#pragma unroll
+      for (int j = 0; j < kGQ; ++j) pm[j] = sc_t[j];
+      block_reduce8<true>(pm, red);
+      float alpha[kGQ];
+#pragma unroll
+      for (int j = 0; j < kGQ; ++j) {
+        const float mn = fmaxf(m[j], pm[j]);
+        alpha[j] = m[j] == -INFINITY ? 0.f : expf(m[j] - mn);
+        m[j] = mn;
+      }
+      if (tid < P) {
+        const uint16_t* r16 = row16_s + tid * 2 * R + 2 * L.half_off + L.width[3];
+        const float vs = half_bits_to_float(r16[0]);
+        const float vm = half_bits_to_float(r16[1]);
+#pragma unroll
+        for (int j = 0; j < kGQ; ++j) {
+          const float pj = m[j] == -INFINITY ? 0.f : expf(sc_t[j] - m[j]);
+          lt[j] = fmaf(lt[j], alpha[j], pj);
+          lvt[j] = fmaf(lvt[j], alpha[j], pj * vm);
+          p_s[tid * kGQ + j] = pj * vs;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < kGQ; ++j) {
+          lt[j] *= alpha[j];
+          lvt[j] *= alpha[j];
+        }
+      }
+      __syncthreads();
+      if (tid < D) {
+#pragma unroll
+        for (int j = 0; j < kGQ; ++j) acc[j] *= alpha[j];
+        const int wd = L.vcode_off + tid / 16, sh = 2 * (tid % 16);
+        for (int t = 0; t < P; ++t) {
+          const float c = static_cast<float>((static_cast<uint32_t>(row_s[t * R + wd]) >> sh) & 3u);
+          const float4 a = *reinterpret_cast<const float4*>(p_s + t * kGQ);
+          const float4 bq = *reinterpret_cast<const float4*>(p_s + t * kGQ + 4);
+          acc[0] = fmaf(a.x, c, acc[0]);
+          acc[1] = fmaf(a.y, c, acc[1]);
+          acc[2] = fmaf(a.z, c, acc[2]);
+          acc[3] = fmaf(a.w, c, acc[3]);
+          acc[4] = fmaf(bq.x, c, acc[4]);
+          acc[5] = fmaf(bq.y, c, acc[5]);
+          acc[6] = fmaf(bq.z, c, acc[6]);
+          acc[7] = fmaf(bq.w, c, acc[7]);
+        }
+      }
+    }
+  } else {
+    // Residual split: tail rows in the caller's dtype, then the new token.
+    float* k_s = reinterpret_cast<float*>(region);
+    float* v_s = k_s + kResChunk * D;
+    float* sc_s = v_s + kResChunk * D;
+    const int tl = p.tail_len[b];
+    const int has_new = p.k_new != nullptr ? 1 : 0;
+    const int ntok = tl + has_new;
+    const RT* tk = static_cast<const RT*>(p.tail_k) + b * p.tail_seq_stride + h * p.tail_head_stride;
+    const RT* tv = static_cast<const RT*>(p.tail_v) + b * p.tail_seq_stride + h * p.tail_head_stride;
+    const RT* nk = has_new ? static_cast<const RT*>(p.k_new) + b * p.new_seq_stride + h * p.new_head_stride : nullptr;
+    const RT* nv = has_new ? static_cast<const RT*>(p.v_new) + b * p.new_seq_stride + h * p.new_head_stride : nullptr;
+    for (int t0 = 0; t0 < ntok; t0 += kResChunk) {
+      __syncthreads();
+      for (int i = tid; i < kResChunk * D; i += kDecThreads) {
+        const int t = t0 + i / D, d = i % D;
+        float kv = 0.f, vv = 0.f;
+        if (t < tl) {
+          kv = Scalar<RT>::load(tk + t * D + d);
+          vv = Scalar<RT>::load(tv + t * D + d);
+        } else if (t < ntok) {
+          kv = Scalar<RT>::load(nk + d);
+          vv = Scalar<RT>::load(nv + d);
+        }
+        k_s[i] = kv;
+        v_s[i] = vv;
+      }
+      __syncthreads();
+      for (int pair = tid; pair < kResChunk * kGQ; pair += kDecThreads) {
+        const int t = pair / kGQ, j = pair % kGQ;
+        float sc = -INFINITY;
+        if (t0 + t < ntok && j < GQ) {
+          float dot = 0.f;
+          for (int d = 0; d < D; ++d) dot = fmaf(q_s[j * D + d], k_s[t * D + d], dot);
+          sc = dot * p.scaling;
+        }
+        sc_s[pair] = sc;
+      }
+      __syncthreads();
+      float alpha[kGQ];
+#pragma unroll
+      for (int j = 0; j < kGQ; ++j) {
+        float pm = -INFINITY;
+        for (int t = 0; t < kResChunk; ++t) pm = fmaxf(pm, sc_s[t * kGQ + j]);
+        const float mn = fmaxf(m[j], pm);
+        alpha[j] = m[j] == -INFINITY ? 0.f : expf(m[j] - mn);
+        m[j] = mn;
+      }
+      if (tid < kResChunk) {
+#pragma unroll
+        for (int j = 0; j < kGQ; ++j) {
+          const float sc = sc_s[tid * kGQ + j];
+          const float pj = (sc == -INFINITY || m[j] == -INFINITY) ? 0.f : expf(sc - m[j]);
+          lt[j] = fmaf(lt[j], alpha[j], pj);
+          p_s[tid * kGQ + j] = pj;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < kGQ; ++j) lt[j] *= alpha[j];
+      }
+      __syncthreads();
+      if (tid < D) {
+#pragma unroll
+        for (int j = 0; j < kGQ; ++j) acc[j] *= alpha[j];
+        for (int t = 0; t < kResChunk; ++t) {
+          const float vv = v_s[t * D + tid];
+#pragma unroll
+          for (int j = 0; j < kGQ; ++j) acc[j] = fmaf(p_s[t * kGQ + j], vv, acc[j]);
+        }
+      }
+    }
+  }
+
+  block_reduce8<false>(lt, red);
+  block_reduce8<false>(lvt, red);
+  float* item = p.ws + ((static_cast<int64_t>(b) * H + h) * p.max_splits + s) * (GQ * (D + 2));
+  if (tid < D) {
+#pragma unroll
+    for (int j = 0; j < kGQ; ++j)
+      if (j < GQ) item[j * D + tid] = acc[j] + lvt[j];
+  }
+  if (tid == 0) {
+#pragma unroll
+    for (int j = 0; j < kGQ; ++j) {
+      if (j < GQ) {
+        item[GQ * D + j] = m[j];
+        item[GQ * D + GQ + j] = lt[j];
+      }
+    }
+  }
+}
+
+template <typename OT>
+__global__ void __launch_bounds__(128)
+decode_merge_kernel(const float* __restrict__ ws, const int32_t* __restrict__ hist_tokens,
+                    int kv_heads, int n_q, int D, int P, int pps, int max_splits, OT* __restrict__ out,
+                    int64_t out_seq_stride, int64_t out_head_stride) {
+  const int b = blockIdx.x, qh = blockIdx.y;
+  const int GQ = n_q / kv_heads, h = qh / GQ, j = qh - h * GQ;
+  const int pages = hist_tokens[b] / P;
+  const int n_s = (pages + pps - 1) / pps + 1;
+  const float* base = ws + (static_cast<int64_t>(b) * kv_heads + h) * max_splits * (GQ * (D + 2));
+  const int item = GQ * (D + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < n_s; ++s) M = fmaxf(M, base[s * item + GQ * D + j]);
+  float L = 0.f;
+  for (int s = 0; s < n_s; ++s) {
+    const float ms = base[s * item + GQ * D + j];
+    if (ms != -INFINITY) L += expf(ms - M) * base[s * item + GQ * D + GQ + j];
+  }
+  const float inv = L > 0.f ? 1.0f / L : 0.f;
+  OT* o = out + b * out_seq_stride + qh * out_head_stride;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float a = 0.f;
+    for (int s = 0; s < n_s; ++s) {
+      const float ms = base[s * item + GQ * D + j];
+      if (ms != -INFINITY) a = fmaf(expf(ms - M), base[s * item + j * D + d], a);
+    }
+    Scalar<OT>::store(o + d, a * inv);
+  }
+}
+
+static int n_slots_of(const lf_layout& L) { return 16 * L.words[0] + 8 * L.words[1] + 4 * L.words[2]; }
+
+template <typename RT, typename QT>
+static int launch_partial(const DecodeParams& p, cudaStream_t stream) {
+  const DecodeSmem S = decode_smem(p.L, p.n_slots);
+  auto kern = decode_partial_simt<RT, QT>;
+  // Raise the kernel's dynamic shared-memory limit once per size, outside
+  // any later stream capture of the launch.
+  static std::atomic<int> configured{48 * 1024};
+  if (S.total > configured.load()) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S.total);
+    if (e == cudaSuccess) configured.store(S.total);
+    if (e != cudaSuccess) {
+      set_error("lf_decode_partial: shared memory %d B: %s", S.total, cudaGetErrorString(e));
+      return LF_ERR_UNSUPPORTED;
+    }
+  }
+  dim3 grid(p.max_splits, p.L.kv_heads, p.batch);
+  kern<<<grid, kDecThreads, S.total, stream>>>(p);
+  return launch_status("lf_decode_partial");
+}
+
+template <typename RT>
+static int dispatch_q(const DecodeParams& p, int q_dtype, cudaStream_t stream) {
+  switch (q_dtype) {
+    case LF_F32: return launch_partial<RT, float>(p, stream);
+    case LF_F16: return launch_partial<RT, __half>(p, stream);
+    case LF_BF16: return launch_partial<RT, __nv_bfloat16>(p, stream);
+  }
+  set_error("lf_decode_partial: q dtype %d", q_dtype);
+  return LF_ERR_INVALID_ARGUMENT;
+}
+
+}  // namespace lf
+
+extern "C" size_t lf_decode_workspace_bytes(int batch, int kv_heads, int n_q, int head_dim,
+                                            int max_splits) {
+  if (batch <= 0 || kv_heads <= 0 || n_q <= 0 || head_dim <= 0 || max_splits <= 0) return 0;
+  const size_t gq = static_cast<size_t>(n_q / kv_heads);
+  return static_cast<size_t>(batch) * kv_heads * max_splits * gq * (head_dim + 2) * sizeof(float);
+}
+
+extern "C" int lf_decode_max_splits(int64_t max_pages, int pages_per_split) {
+  if (max_pages < 0 || pages_per_split <= 0) return 0;
+  return static_cast<int>((max_pages + pages_per_split - 1) / pages_per_split) + 1;
+}
+
+extern "C" int lf_decode_partial(const lf_layout* layout, const int32_t* rows, const uint16_t* kmeta,
+                                 const int32_t* slot_chan, const int32_t* hist_tokens,
+                                 const void* tail_k, const void* tail_v, int64_t tail_seq_stride,
+                                 int64_t tail_head_stride, const int32_t* tail_len, int resid_dtype,
+                                 const void* k_new, const void* v_new, int64_t new_seq_stride,
+                                 int64_t new_head_stride, const void* q, int q_dtype,
+                                 int64_t q_seq_stride, int64_t q_head_stride, int batch, int n_q,
+                                 float scaling, int pages_per_split, int max_splits,
+                                 float* workspace, lf_stream_t stream) {
+  LF_CHECK_ARG(layout != nullptr, "lf_decode_partial: null layout");
+  const lf_layout& L = *layout;
+  LF_CHECK_ARG(rows && slot_chan && hist_tokens && tail_k && tail_v && tail_len && q && workspace,
+               "lf_decode_partial: null pointer");
+  LF_CHECK_ARG((k_new == nullptr) == (v_new == nullptr), "lf_decode_partial: k_new/v_new mismatch");
+  LF_CHECK_ARG(batch > 0 && batch <= 65535 && n_q > 0 && n_q % L.kv_heads == 0,
+               "lf_decode_partial: batch %d, n_q %d, kv_heads %d", batch, n_q, L.kv_heads);
+  LF_CHECK_ARG(pages_per_split > 0 && max_splits >= 1 && max_splits <= 65535,
+               "lf_decode_partial: pages_per_split %d, max_splits %d", pages_per_split, max_splits);
+  LF_CHECK_ARG(max_splits >= lf_decode_max_splits(L.row_cap / L.page_size, pages_per_split),
+               "lf_decode_partial: max_splits %d cannot cover row_cap %lld", max_splits,
+               (long long)L.row_cap);
+  LF_CHECK_SUPPORTED(L.bit_v == 2, "decode supports bit_v 2, got %d", L.bit_v);
+  LF_CHECK_SUPPORTED(L.k_group == L.page_size, "decode needs k_group == page_size (%d vs %d)",
+                     L.k_group, L.page_size);
+  LF_CHECK_SUPPORTED(L.v_group == L.head_dim, "decode needs v_group == head_dim (%d vs %d)",
+                     L.v_group, L.head_dim);
+  LF_CHECK_SUPPORTED(L.head_dim % 16 == 0 && L.head_dim <= lf::kDecThreads,
+                     "decode head_dim %d not supported", L.head_dim);
+  LF_CHECK_SUPPORTED(L.page_size <= lf::kDecThreads, "decode page_size %d > %d", L.page_size,
+                     lf::kDecThreads);
+  LF_CHECK_SUPPORTED(n_q / L.kv_heads <= lf::kGQ, "decode GQA group %d > %d", n_q / L.kv_heads,
+                     lf::kGQ);
+  lf::DecodeParams p{};
+  p.L = L;
+  p.rows = rows;
+  p.kmeta = kmeta;
+  p.slot_chan = slot_chan;
+  p.hist_tokens = hist_tokens;
+  p.tail_k = tail_k;
+  p.tail_v = tail_v;
+  p.tail_seq_stride = tail_seq_stride;
+  p.tail_head_stride = tail_head_stride;
+  p.tail_len = tail_len;
+  p.k_new = k_new;
+  p.v_new = v_new;
+  p.new_seq_stride = new_seq_stride;
+  p.new_head_stride = new_head_stride;
+  p.q = q;
+  p.q_seq_stride = q_seq_stride;
+  p.q_head_stride = q_head_stride;
+  p.batch = batch;
+  p.n_q = n_q;
+  p.gq = n_q / L.kv_heads;
+  p.pps = pages_per_split;
+  p.max_splits = max_splits;
+  p.n_slots = lf::n_slots_of(L);
+  p.scaling = scaling;
+  p.ws = workspace;
+  LF_CHECK_SUPPORTED(lf::decode_smem(L, p.n_slots).total <= 227 * 1024,
+                     "decode shared memory %d B too large", lf::decode_smem(L, p.n_slots).total);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (resid_dtype) {
+    case LF_F32: return lf::dispatch_q<float>(p, q_dtype, s);
+    case LF_F16: return lf::dispatch_q<__half>(p, q_dtype, s);
+    case LF_BF16: return lf::dispatch_q<__nv_bfloat16>(p, q_dtype, s);
+  }
+  lf::set_error("lf_decode_partial: residual dtype %d", resid_dtype);
+  return LF_ERR_INVALID_ARGUMENT;
+}
+
+extern "C" int lf_decode_merge(const float* workspace, const int32_t* hist_tokens, int batch,
+                               int kv_heads, int n_q, int head_dim, int page_size,
+                               int pages_per_split, int max_splits, void* out, int out_dtype,
+                               int64_t out_seq_stride, int64_t out_head_stride,
+                               lf_stream_t stream) {
+  LF_CHECK_ARG(workspace && hist_tokens && out, "lf_decode_merge: null pointer");
+  LF_CHECK_ARG(batch > 0 && batch <= 65535 && kv_heads > 0 && n_q % kv_heads == 0 && n_q <= 65535,
+               "lf_decode_merge: batch %d n_q %d kv_heads %d", batch, n_q, kv_heads);
+  LF_CHECK_ARG(page_size > 0 && pages_per_split > 0 && max_splits > 0 && head_dim > 0,
+               "lf_decode_merge: bad sizes");
+  dim3 grid(batch, n_q);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (out_dtype) {
+    case LF_F32:
+      lf::decode_merge_kernel<float><<<grid, 128, 0, s>>>(workspace, hist_tokens, kv_heads, n_q, head_dim,
+                                                          page_size, pages_per_split, max_splits,
+                                                          static_cast<float*>(out), out_seq_stride,
+                                                          out_head_stride);
+      break;
+    case LF_F16:
+      lf::decode_merge_kernel<__half><<<grid, 128, 0, s>>>(workspace, hist_tokens, kv_heads, n_q, head_dim,
+                                                           page_size, pages_per_split, max_splits,
+                                                           static_cast<__half*>(out), out_seq_stride,
+                                                           out_head_stride);
+      break;
+    case LF_BF16:
+      lf::decode_merge_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(
+          workspace, hist_tokens, kv_heads, n_q, head_dim, page_size, pages_per_split, max_splits,
+          static_cast<__nv_bfloat16*>(out), out_seq_stride, out_head_stride);
+      break;
+    default:
+      lf::set_error("lf_decode_merge: out dtype %d", out_dtype);
+      return LF_ERR_INVALID_ARGUMENT;
+  }
+  return lf::launch_status("lf_decode_merge");
+}

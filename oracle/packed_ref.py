@@ -275,17 +275,20 @@ def attention_over(key: np.ndarray, value: np.ndarray, query: np.ndarray, scalin
     n_kv, T, D = key.shape
     n_q, q_len, _ = query.shape
     rep = n_q // n_kv
-    k = np.repeat(key.astype(np.float64), rep, axis=0)
-    v = np.repeat(value.astype(np.float64), rep, axis=0)
-    s = np.einsum("hqd,htd->hqt", query.astype(np.float64), k) * float(scaling)
+    # q-head h*rep + j reads KV head h: the repeat_kv expansion as a grouped product.
+    qg = query.astype(np.float64).reshape(n_kv, rep, q_len, D).reshape(n_kv, rep * q_len, D)
+    k = key.astype(np.float64)
+    v = value.astype(np.float64)
+    s = (qg @ k.transpose(0, 2, 1)).reshape(n_kv, rep, q_len, T) * float(scaling)
     if q_len > 1:
         for i in range(q_len):
             visible = T - q_len + i + 1
-            s[:, i, visible:] = -np.inf
+            s[:, :, i, visible:] = -np.inf
     s -= s.max(axis=-1, keepdims=True)
     p = np.exp(s)
     p /= p.sum(axis=-1, keepdims=True)
-    return np.einsum("hqt,htd->hqd", p, v)
+    out = p.reshape(n_kv, rep * q_len, T) @ v
+    return out.reshape(n_kv, rep, q_len, D).reshape(n_q, q_len, D)
 
 
 def reference_attention(layer: OracleLayer, query: np.ndarray, key_new: np.ndarray,

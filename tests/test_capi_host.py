@@ -1,0 +1,124 @@
+"""CPU tests of the C ABI and the host logic (no GPU calls).
+
+* the shared library loads and exports every ``LF_API`` symbol of
+  ``include/logitfill_b200.h``;
+* ``lf_layout_init`` agrees with an independent restatement of the layout
+  rules and with the reference's tier widths (layout.py:57,82);
+* argument validation returns the documented status codes without touching
+  the GPU;
+* host tier tables equal the oracle's (layout.py:49-68).
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from logitfill_b200 import _lib
+from logitfill_b200.packed.layout import LayerLayout, tier_tables
+from logitfill_b200.synthetic import synthetic_levels
+from oracle import packed_ref as orc
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def header_symbols() -> list[str]:
+    text = (ROOT / "include" / "logitfill_b200.h").read_text()
+    return re.findall(r"LF_API\s+[\w\s\*]+?\b(lf_\w+)\s*\(", text)
+
+
+def test_library_exports_every_header_symbol():
+    so = _lib.lib()
+    names = header_symbols()
+    assert len(names) >= 9
+    for name in names:
+        assert hasattr(so, name), name
+    assert set(names) == set(_lib.EXPORTS)
+
+
+def _layout_restated(counts, D, P, kg, vg, bit_v):
+    bits = (2, 4, 8)
+    width = [int(max(counts[t])) for t in range(4)]
+    words = [(width[t] + 32 // bits[t] - 1) // (32 // bits[t]) for t in range(3)]
+    code_off = [0, words[0], words[0] + words[1]]
+    vcode_off = sum(words)
+    vcode_words = (D + 32 // bit_v - 1) // (32 // bit_v)
+    half_off = vcode_off + vcode_words
+    halves = width[3] + 2 * (D // vg)
+    row_words = -(-(half_off + (halves + 1) // 2) // 4) * 4
+    meta = -(-(2 * sum(width[:3])) // 8) * 8
+    return width, words, code_off, vcode_off, half_off, row_words, meta
+
+
+@pytest.mark.parametrize("target_bit", [2.25, 2.5, 3.0, 4.0])
+def test_layout_init_matches_restatement(target_bit):
+    levels = synthetic_levels(1, 4, 128, target_bit, seed=3)[0]
+    lay = LayerLayout(levels, head_dim=128, page_size=128, k_group_size=128, v_group_size=128, bit_v=2,
+                      row_cap=512, device="cpu")
+    table = orc.tier_tables(levels)
+    counts = np.stack([table[c]["count"] for c in range(4)])
+    width, words, code_off, vcode_off, half_off, row_words, meta = _layout_restated(counts, 128, 128, 128, 128, 2)
+    c = lay.c
+    assert list(c.width) == width == [table[t]["width"] for t in range(4)]
+    assert list(c.words) == words
+    assert list(c.code_off) == code_off
+    assert (c.vcode_off, c.half_off, c.row_words, c.meta_halves) == (vcode_off, half_off, row_words, meta)
+    assert c.row_words % 4 == 0 and c.meta_halves % 8 == 0
+    assert (c.row_cap, c.group_cap) == (512, 4)
+
+
+def test_layout_init_rejects_bad_arguments():
+    so = _lib.lib()
+    out = _lib.LfLayout()
+    counts = np.array([[64], [32], [16], [16]], np.int32)
+    assert so.lf_layout_init(ctypes.byref(out), 1, 128, 128, 96, 128, 2, counts.ctypes.data, 128, 1) \
+        == _lib.LF_ERR_INVALID_ARGUMENT   # page not a multiple of k_group
+    assert so.lf_layout_init(ctypes.byref(out), 1, 128, 128, 128, 128, 3, counts.ctypes.data, 128, 1) \
+        == _lib.LF_ERR_UNSUPPORTED        # bit_v 3 is not a packed width
+    bad = np.array([[64], [32], [16], [15]], np.int32)
+    assert so.lf_layout_init(ctypes.byref(out), 1, 128, 128, 128, 128, 2, bad.ctypes.data, 128, 1) \
+        == _lib.LF_ERR_INVALID_ARGUMENT   # counts do not cover head_dim
+    assert b"head" in so.lf_last_error()
+    with pytest.raises(ValueError):
+        _lib.check(_lib.LF_ERR_INVALID_ARGUMENT, "x")
+    with pytest.raises(NotImplementedError):
+        _lib.check(_lib.LF_ERR_UNSUPPORTED, "x")
+
+
+def test_entry_points_validate_before_launch():
+    """Null or inconsistent arguments are rejected on the host, no GPU needed."""
+    so = _lib.lib()
+    assert so.lf_pack_pages(None, None, None, 2, 0, 0, 0, None, 1, 1, None, None, None, None, None) \
+        == _lib.LF_ERR_INVALID_ARGUMENT
+    lay = LayerLayout(np.zeros((2, 64), np.int64), head_dim=64, page_size=64, k_group_size=64,
+                      v_group_size=64, bit_v=2, row_cap=256, device="cpu")
+    fake = 1 << 20  # never dereferenced: validation fails first
+    # max_splits too small for the capacity
+    st = so.lf_decode_partial(ctypes.byref(lay.c), fake, fake, fake, fake, fake, fake, 0, 0, fake, 2, None, None,
+                              0, 0, fake, 2, 0, 0, 1, 2, 1.0, 1, 1, fake, None)
+    assert st == _lib.LF_ERR_INVALID_ARGUMENT
+    # GQA group of 16 exceeds what one CTA computes
+    st = so.lf_decode_partial(ctypes.byref(lay.c), fake, fake, fake, fake, fake, fake, 0, 0, fake, 2, None, None,
+                              0, 0, fake, 2, 0, 0, 1, 32, 1.0, 1, 5, fake, None)
+    assert st == _lib.LF_ERR_UNSUPPORTED
+    assert so.lf_decode_merge(None, None, 1, 1, 1, 64, 64, 1, 1, None, 0, 0, 0, None) == _lib.LF_ERR_INVALID_ARGUMENT
+    assert so.lf_decode_max_splits(256, 16) == 17
+    assert so.lf_decode_workspace_bytes(2, 4, 28, 128, 5) == 2 * 4 * 5 * 7 * 130 * 4
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_tier_tables_match_oracle(seed):
+    rng = np.random.default_rng(seed)
+    levels = rng.integers(0, 4, size=(3, 64))
+    levels[1] = 0   # a head with a single tier
+    ours = tier_tables(torch.as_tensor(levels))
+    ref = orc.tier_tables(levels)
+    for code in range(4):
+        for key in ("index", "count", "local"):
+            np.testing.assert_array_equal(ours["tiers"][code][key].numpy(), ref[code][key])
+        assert ours["tiers"][code]["width"] == ref[code]["width"]
+    np.testing.assert_array_equal(ours["tier"].numpy(), ref["tier"])

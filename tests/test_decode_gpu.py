@@ -1,0 +1,162 @@
+"""GPU parity of K2 + K3 (split-K packed decode attention) against the oracle.
+
+Tolerance (north star): max-abs 2e-3 and cosine >= 0.9999 against the
+reference's dense packed path (reference.py:30-56, restated by the oracle)
+with fp32 accumulation.
+"""
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from logitfill_b200.packed import PackedKVCache
+from logitfill_b200.packed.attention import decode_into, packed_attention, packed_attention_batched
+from logitfill_b200.packed.cache import _LayerStore
+from logitfill_b200.synthetic import synthetic_kv, synthetic_levels
+from oracle import packed_ref as orc
+from tests.golden import cases
+from tests.gpu_cases import TORCH_DT, attention_close, manager_for
+from tests.oracle_runner import oracle_layer_for, run_case, small_case
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _decode(mgr, case, q_dtype=torch.float32):
+    dt = TORCH_DT[case["dtype"]]
+    q = torch.as_tensor(case["query"])[None].to("cuda", q_dtype)
+    kn = torch.as_tensor(case["key_new"])[None].to("cuda", dt)
+    vn = torch.as_tensor(case["value_new"])[None].to("cuda", dt)
+    return packed_attention(mgr, 0, q, kn, vn, case["scaling"])
+
+
+@pytest.mark.parametrize("name", sorted(cases.CONFIG0_VARIANTS))
+def test_config0_decode(name):
+    hist, tail = cases.CONFIG0_VARIANTS[name]
+    case = cases.config0_like(hist, tail)
+    want = run_case(case)["attn"]
+    out = _decode(manager_for(case), case)
+    assert out.dtype == torch.float32 and out.shape == (1, 28, 1, 128)
+    ok, err, cos = attention_close(out[0].cpu().numpy(), want)
+    assert ok, (err, cos)
+
+
+def test_config0_decode_matches_golden_fixture():
+    """The CUDA output against the reference's own output stored in the fixture."""
+    big = dict(np.load(GOLDEN / "golden_config0.npz"))
+    case = cases.config0_like(1024, 37)
+    out = _decode(manager_for(case), case)
+    ok, err, cos = attention_close(out[0].cpu().numpy(), big["config0_attn"])
+    assert ok, (err, cos)
+
+
+def test_bf16_query_returns_bf16():
+    case = cases.config0_like(1024, 37)
+    want = run_case(case)["attn"]
+    out = _decode(manager_for(case), case, q_dtype=torch.bfloat16)
+    assert out.dtype == torch.bfloat16
+    ok, err, cos = attention_close(out[0].float().cpu().numpy(), want, atol=1e-2, min_cos=0.9999)
+    assert ok, (err, cos)
+
+
+@pytest.mark.parametrize("name", ["cuda", "mixed"])
+def test_reference_test_shapes(name):
+    """The reference's kernel test shape (tests/test_logitfill_offline.py:187-219)
+    and a mixed-tier GQA-2 case, head_dim 64, page 64, fp32 inputs."""
+    small = dict(np.load(GOLDEN / "golden_small.npz"))
+    case = small_case(small, name)
+    out = _decode(manager_for(case), case)
+    ok, err, cos = attention_close(out[0].cpu().numpy(), small[f"{name}_attn"])
+    assert ok, (err, cos)
+    assert np.allclose(out[0].cpu().numpy(), small[f"{name}_attn"], atol=1e-3, rtol=1e-3)
+
+
+def test_gqa5_ragged_batch():
+    """Config-4 head geometry (40 q / 8 kv, GQA 5) on a small ragged batch,
+    every sequence against the oracle, several split sizes."""
+    B, H, NQ, D = 5, 8, 40, 128
+    levels = synthetic_levels(1, H, D, 2.5, seed=9)[0]
+    lengths = [0 + 5, 128, 700, 1024 + 127, 2000]
+    k, v = synthetic_kv(B, H, max(lengths) + 1, D, seed=9, layer=0, device="cuda")
+    cache = PackedKVCache([levels], B, NQ, H, D, device="cuda", capacity=2048)
+    cache.prefill(0, k, v, lengths)
+    g = torch.Generator(device="cuda").manual_seed(1)
+    q = torch.randn(B, NQ, D, generator=g, device="cuda").to(torch.bfloat16)
+    kn = torch.stack([k[b, :, n] for b, n in enumerate(lengths)])
+    vn = torch.stack([v[b, :, n] for b, n in enumerate(lengths)])
+    for pps in (1, 3, 16):
+        out = torch.empty(B, NQ, D, dtype=torch.float32, device="cuda")
+        decode_into(cache, 0, q, kn, vn, D ** -0.5, out, pps=pps)
+        for b in range(B):
+            ref = orc.OracleLayer(levels, 128, 128, 128, 2)
+            ref.append(k[b, :, :lengths[b]].float().cpu().numpy(), v[b, :, :lengths[b]].float().cpu().numpy())
+            want = orc.reference_attention(ref, q[b, :, None].float().cpu().numpy(),
+                                           kn[b, :, None].float().cpu().numpy(),
+                                           vn[b, :, None].float().cpu().numpy(), D ** -0.5)
+            ok, err, cos = attention_close(out[b].cpu().numpy(), want[:, 0])
+            assert ok, (pps, b, err, cos)
+
+
+@pytest.mark.parametrize("target_bit", [2.25, 2.5, 3.0, 4.0])
+def test_config1_geometry_sampled(target_bit):
+    """Config-1/2 geometry (28 q / 4 kv, 8192-token packed history + ragged
+    0-127 tail): sampled sequences against the oracle at every policy width."""
+    B, H, NQ, D, T = 4, 4, 28, 128, 8192
+    levels = synthetic_levels(1, H, D, target_bit, seed=1)[0]
+    tails = [0, 1, 64, 127]
+    k, v = synthetic_kv(B, H, T + 128, D, seed=1, layer=0, device="cuda")
+    cache = PackedKVCache([levels], B, NQ, H, D, device="cuda", capacity=T + 128)
+    cache.prefill(0, k, v, [T + t for t in tails])
+    g = torch.Generator(device="cuda").manual_seed(2)
+    q = torch.randn(B, NQ, D, generator=g, device="cuda").to(torch.bfloat16)
+    kn = torch.stack([k[b, :, T + t] for b, t in enumerate(tails)])
+    vn = torch.stack([v[b, :, T + t] for b, t in enumerate(tails)])
+    out = packed_attention_batched(cache, 0, q, kn, vn, D ** -0.5, out_dtype=torch.float32)
+    for b in (0, 3):
+        ref = orc.OracleLayer(levels, 128, 128, 128, 2)
+        n = T + tails[b]
+        ref.append(k[b, :, :n].float().cpu().numpy(), v[b, :, :n].float().cpu().numpy())
+        want = orc.reference_attention(ref, q[b, :, None].float().cpu().numpy(), kn[b, :, None].float().cpu().numpy(),
+                                       vn[b, :, None].float().cpu().numpy(), D ** -0.5)
+        ok, err, cos = attention_close(out[b].cpu().numpy(), want[:, 0])
+        assert ok, (b, err, cos)
+
+
+def test_long_context_split_merge_property():
+    """32k-token history (config-2 length): the merged output does not depend
+    on how the history is split (split-merge invariance), and one sampled
+    sequence matches the oracle."""
+    B, H, NQ, D, T = 2, 4, 28, 128, 32768
+    levels = synthetic_levels(1, H, D, 3.0, seed=2)[0]
+    k, v = synthetic_kv(B, H, T + 40, D, seed=2, layer=0, device="cuda")
+    cache = PackedKVCache([levels], B, NQ, H, D, device="cuda", capacity=T + 128)
+    cache.prefill(0, k, v, [T + 39, T])
+    g = torch.Generator(device="cuda").manual_seed(3)
+    q = torch.randn(B, NQ, D, generator=g, device="cuda").to(torch.bfloat16)
+    kn, vn = k[:, :, T + 39].contiguous(), v[:, :, T + 39].contiguous()
+    outs = []
+    for pps in (1, 7, 64, 256):
+        out = torch.empty(B, NQ, D, dtype=torch.float32, device="cuda")
+        decode_into(cache, 0, q, kn, vn, D ** -0.5, out, pps=pps)
+        outs.append(out)
+    for o in outs[1:]:
+        assert float((o - outs[0]).abs().max()) < 1e-4
+    ref = orc.OracleLayer(levels, 128, 128, 128, 2)
+    ref.append(k[1, :, :T].float().cpu().numpy(), v[1, :, :T].float().cpu().numpy())
+    want = orc.reference_attention(ref, q[1, :, None].float().cpu().numpy(), kn[1, :, None].float().cpu().numpy(),
+                                   vn[1, :, None].float().cpu().numpy(), D ** -0.5)
+    ok, err, cos = attention_close(outs[0][1].cpu().numpy(), want[:, 0])
+    assert ok, (err, cos)
+
+
+def test_errors_are_raised_not_swallowed():
+    case = cases.config0_like(128, 1)
+    mgr = manager_for(case)
+    q = torch.zeros(1, 28, 2, 128, device="cuda")  # q_len 2: no kernel, no silent fallback
+    with pytest.raises(NotImplementedError):
+        packed_attention(mgr, 0, q, q[:, :4], q[:, :4], 0.1)
+    with pytest.raises(NotImplementedError):
+        PackedKVCache([None], 1, 28, 4, 128, bit_v=4, device="cuda")
