@@ -110,20 +110,27 @@ LF_API int lf_dequantize(const lf_layout* layout, const int32_t* rows, const uin
                   const int32_t* chan_code, int seq, int64_t tokens, float* out_k, float* out_v,
                   lf_stream_t stream);
 
+/* Resident K2 CTAs per SM for this layer and split size (occupancy of the
+ * kernel lf_decode_partial would launch, capped by tensor-memory columns);
+ * <= 0 on error.  Needs a current CUDA device. */
+LF_API int lf_decode_occupancy(const lf_layout* layout, int n_q, int pages_per_split);
+
 /* Bytes of fp32 split partials K2 writes and K3 reads. */
 LF_API size_t lf_decode_workspace_bytes(int batch, int kv_heads, int n_q, int head_dim, int max_splits);
 
-/* Number of splits (page splits + 1 residual split) for a history of
- * max_pages pages cut into pages_per_split. */
-LF_API int lf_decode_max_splits(int64_t max_pages, int pages_per_split);
+/* Number of work-item splits per (sequence, KV head): page splits for a
+ * history of up to max_pages pages cut into pages_per_split, plus the
+ * residual splits (32 residual tokens each, ceil(page_size / 32)). */
+LF_API int lf_decode_max_splits(int64_t max_pages, int pages_per_split, int page_size);
 
 /*
  * K2: split-K GQA decode attention over the packed history plus the
  * original-dtype residual page and the new token (replaces kernel.cu:112-190
  * launched from reference.py:59-109).  One work item per (sequence, KV head,
- * split); split s < ceil(pages/pages_per_split) covers pages
- * [s*pps, min((s+1)*pps, pages)), the next split covers the residual tokens
- * (tail_len[b] tail rows followed by the new token when k_new is not NULL).
+ * split); split s < n = ceil(pages/pages_per_split) covers pages
+ * [s*pps, min((s+1)*pps, pages)); splits n .. n + ceil(page_size/32) - 1
+ * cover 32 residual tokens each (tail_len[b] tail rows followed by the new
+ * token when k_new is not NULL; rows 16-byte aligned).
  * Writes an unnormalised partial (running max m, sum l, accumulator) per
  * (item, q-head) into workspace.
  *   hist_tokens [batch] device int32, multiple of page_size
@@ -133,6 +140,12 @@ LF_API int lf_decode_max_splits(int64_t max_pages, int pages_per_split);
  *   k_new/v_new [batch][H][D] (strides new_seq_stride, new_head_stride), resid_dtype, or NULL
  *   q [batch][n_q][D] (strides q_seq_stride, q_head_stride), dtype q_dtype
  * q-head j of KV head h is h * (n_q / H) + j (repeat_kv, reference.py:10-15).
+ * status (device int32, may be NULL) is set to LF_ERR_DEVICE_TIMEOUT if a
+ * bounded device-side wait expires; the kernel then returns without hanging.
+ * Geometry head_dim 128 / page 128 / k_group 128 / v_group 128 / GQA <= 8
+ * runs on the tensor cores (tcgen05.mma kind::i8); other supported
+ * geometries (head_dim <= 128, page <= 128, k_group == page, v_group ==
+ * head_dim) on a CUDA-core kernel.
  */
 LF_API int lf_decode_partial(const lf_layout* layout, const int32_t* rows, const uint16_t* kmeta,
                       const int32_t* slot_chan, const int32_t* hist_tokens, const void* tail_k,
@@ -141,7 +154,7 @@ LF_API int lf_decode_partial(const lf_layout* layout, const int32_t* rows, const
                       const void* v_new, int64_t new_seq_stride, int64_t new_head_stride,
                       const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
                       int batch, int n_q, float scaling, int pages_per_split, int max_splits,
-                      float* workspace, lf_stream_t stream);
+                      float* workspace, int32_t* status, lf_stream_t stream);
 
 /*
  * K3: merge the split partials into the attention output

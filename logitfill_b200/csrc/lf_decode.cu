@@ -13,33 +13,14 @@
 // and the inner loops multiply raw integer codes by precomputed fp32 factors.
 #include <atomic>
 
-#include "lf_common.cuh"
+#include "lf_decode_common.cuh"
 
 namespace lf {
 
-constexpr int kDecThreads = 128;
-constexpr int kGQ = 8;        // q-heads per KV head handled by one CTA
-constexpr int kResChunk = 32; // residual tokens per chunk
-
-struct DecodeParams {
-  lf_layout L;
-  const int32_t* rows;
-  const uint16_t* kmeta;
-  const int32_t* slot_chan;
-  const int32_t* hist_tokens;
-  const void* tail_k;
-  const void* tail_v;
-  int64_t tail_seq_stride, tail_head_stride;
-  const int32_t* tail_len;
-  const void* k_new;
-  const void* v_new;
-  int64_t new_seq_stride, new_head_stride;
-  const void* q;
-  int64_t q_seq_stride, q_head_stride;
-  int batch, n_q, gq, pps, max_splits, n_slots;
-  float scaling;
-  float* ws;
-};
+// Tensor-core decode (lf_decode_tc.cu).
+bool tc_supported(const lf_layout& L, int gq, int pps);
+int launch_partial_tc(const DecodeParams& p, int resid_dtype, int q_dtype, cudaStream_t stream);
+int occupancy_tc(const lf_layout& L, int pps);
 
 struct DecodeSmem {
   int q, qp, p, red, slot, slot16, region, rows_bytes, total;
@@ -58,40 +39,11 @@ __host__ __device__ inline DecodeSmem decode_smem(const lf_layout& L, int n_slot
   off = (off + 15) / 16 * 16;
   s.region = off;
   const int page_bytes = P * L.row_words * 4 + (L.meta_halves * 2 + 15) / 16 * 16;
-  const int resid_bytes = 2 * kResChunk * D * 4 + kResChunk * kGQ * 4;
+  const int resid_bytes = resid_smem(D).total;
   s.rows_bytes = page_bytes;
   off += page_bytes > resid_bytes ? page_bytes : resid_bytes;
   s.total = (off + 15) / 16 * 16;
   return s;
-}
-
-// Sum (or max) of kGQ values over the CTA; every thread receives the result.
-template <bool kMax>
-__device__ __forceinline__ void block_reduce8(float (&v)[kGQ], float* red) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-  for (int j = 0; j < kGQ; ++j) {
-    float x = v[j];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float y = __shfl_xor_sync(0xffffffffu, x, o);
-      x = kMax ? fmaxf(x, y) : x + y;
-    }
-    v[j] = x;
-  }
-  if (lane == 0) {
-#pragma unroll
-    for (int j = 0; j < kGQ; ++j) red[warp * kGQ + j] = v[j];
-  }
-  __syncthreads();
-#pragma unroll
-  for (int j = 0; j < kGQ; ++j) {
-    float x = red[j];
-#pragma unroll
-    for (int w = 1; w < kDecThreads / 32; ++w) x = kMax ? fmaxf(x, red[w * kGQ + j]) : x + red[w * kGQ + j];
-    v[j] = x;
-  }
-  __syncthreads();
 }
 
 template <typename RT, typename QT>
@@ -113,14 +65,9 @@ decode_partial_simt(DecodeParams p) {
   const int GQ = p.gq;
   const int pages = p.hist_tokens[b] / P;
   const int n_page_splits = (pages + p.pps - 1) / p.pps;
-  if (s > n_page_splits) return;
+  if (s >= n_page_splits + residual_splits(P)) return;
 
-  // Query group, q-heads h*GQ .. h*GQ+GQ-1 (repeat_kv order, reference.py:10-15).
-  const QT* qb = static_cast<const QT*>(p.q) + b * p.q_seq_stride;
-  for (int i = tid; i < kGQ * D; i += kDecThreads) {
-    const int j = i / D, d = i - j * D;
-    q_s[i] = j < GQ ? Scalar<QT>::load(qb + (h * GQ + j) * p.q_head_stride + d) : 0.0f;
-  }
+  load_query_group<QT>(p, b, h, q_s);
   // Tier slot -> channel, in history-row order.
   for (int i = tid; i < p.n_slots; i += kDecThreads) {
     int tier = 0, base = 0;
@@ -277,95 +224,10 @@ decode_partial_simt(DecodeParams p) {
       }
     }
   } else {
-    // Residual split: tail rows in the caller's dtype, then the new token.
-    float* k_s = reinterpret_cast<float*>(region);
-    float* v_s = k_s + kResChunk * D;
-    float* sc_s = v_s + kResChunk * D;
-    const int tl = p.tail_len[b];
-    const int has_new = p.k_new != nullptr ? 1 : 0;
-    const int ntok = tl + has_new;
-    const RT* tk = static_cast<const RT*>(p.tail_k) + b * p.tail_seq_stride + h * p.tail_head_stride;
-    const RT* tv = static_cast<const RT*>(p.tail_v) + b * p.tail_seq_stride + h * p.tail_head_stride;
-    const RT* nk = has_new ? static_cast<const RT*>(p.k_new) + b * p.new_seq_stride + h * p.new_head_stride : nullptr;
-    const RT* nv = has_new ? static_cast<const RT*>(p.v_new) + b * p.new_seq_stride + h * p.new_head_stride : nullptr;
-    for (int t0 = 0; t0 < ntok; t0 += kResChunk) {
-      __syncthreads();
-      for (int i = tid; i < kResChunk * D; i += kDecThreads) {
-        const int t = t0 + i / D, d = i % D;
-        float kv = 0.f, vv = 0.f;
-        if (t < tl) {
-          kv = Scalar<RT>::load(tk + t * D + d);
-          vv = Scalar<RT>::load(tv + t * D + d);
-        } else if (t < ntok) {
-          kv = Scalar<RT>::load(nk + d);
-          vv = Scalar<RT>::load(nv + d);
-        }
-        k_s[i] = kv;
-        v_s[i] = vv;
-      }
-      __syncthreads();
-      for (int pair = tid; pair < kResChunk * kGQ; pair += kDecThreads) {
-        const int t = pair / kGQ, j = pair % kGQ;
-        float sc = -INFINITY;
-        if (t0 + t < ntok && j < GQ) {
-          float dot = 0.f;
-          for (int d = 0; d < D; ++d) dot = fmaf(q_s[j * D + d], k_s[t * D + d], dot);
-          sc = dot * p.scaling;
-        }
-        sc_s[pair] = sc;
-      }
-      __syncthreads();
-      float alpha[kGQ];
-#pragma unroll
-      for (int j = 0; j < kGQ; ++j) {
-        float pm = -INFINITY;
-        for (int t = 0; t < kResChunk; ++t) pm = fmaxf(pm, sc_s[t * kGQ + j]);
-        const float mn = fmaxf(m[j], pm);
-        alpha[j] = m[j] == -INFINITY ? 0.f : expf(m[j] - mn);
-        m[j] = mn;
-      }
-      if (tid < kResChunk) {
-#pragma unroll
-        for (int j = 0; j < kGQ; ++j) {
-          const float sc = sc_s[tid * kGQ + j];
-          const float pj = (sc == -INFINITY || m[j] == -INFINITY) ? 0.f : expf(sc - m[j]);
-          lt[j] = fmaf(lt[j], alpha[j], pj);
-          p_s[tid * kGQ + j] = pj;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < kGQ; ++j) lt[j] *= alpha[j];
-      }
-      __syncthreads();
-      if (tid < D) {
-#pragma unroll
-        for (int j = 0; j < kGQ; ++j) acc[j] *= alpha[j];
-        for (int t = 0; t < kResChunk; ++t) {
-          const float vv = v_s[t * D + tid];
-#pragma unroll
-          for (int j = 0; j < kGQ; ++j) acc[j] = fmaf(p_s[t * kGQ + j], vv, acc[j]);
-        }
-      }
-    }
+    residual_chunk<RT>(p, b, h, s - n_page_splits, q_s, region, m, acc, lt);
   }
 
-  block_reduce8<false>(lt, red);
-  block_reduce8<false>(lvt, red);
-  float* item = p.ws + ((static_cast<int64_t>(b) * H + h) * p.max_splits + s) * (GQ * (D + 2));
-  if (tid < D) {
-#pragma unroll
-    for (int j = 0; j < kGQ; ++j)
-      if (j < GQ) item[j * D + tid] = acc[j] + lvt[j];
-  }
-  if (tid == 0) {
-#pragma unroll
-    for (int j = 0; j < kGQ; ++j) {
-      if (j < GQ) {
-        item[GQ * D + j] = m[j];
-        item[GQ * D + GQ + j] = lt[j];
-      }
-    }
-  }
+  write_partial(p, b, h, s, tid, acc, m, lt, lvt, red);
 }
 
 template <typename OT>
@@ -376,7 +238,7 @@ decode_merge_kernel(const float* __restrict__ ws, const int32_t* __restrict__ hi
   const int b = blockIdx.x, qh = blockIdx.y;
   const int GQ = n_q / kv_heads, h = qh / GQ, j = qh - h * GQ;
   const int pages = hist_tokens[b] / P;
-  const int n_s = (pages + pps - 1) / pps + 1;
+  const int n_s = (pages + pps - 1) / pps + residual_splits(P);
   const float* base = ws + (static_cast<int64_t>(b) * kv_heads + h) * max_splits * (GQ * (D + 2));
   const int item = GQ * (D + 2);
   float M = -INFINITY;
@@ -433,6 +295,22 @@ static int dispatch_q(const DecodeParams& p, int q_dtype, cudaStream_t stream) {
 
 }  // namespace lf
 
+extern "C" int lf_decode_occupancy(const lf_layout* layout, int n_q, int pages_per_split) {
+  if (layout == nullptr || n_q <= 0 || pages_per_split <= 0 || n_q % layout->kv_heads) return 0;
+  const int gq = n_q / layout->kv_heads;
+  if (lf::tc_supported(*layout, gq, pages_per_split)) return lf::occupancy_tc(*layout, pages_per_split);
+  const lf::DecodeSmem S = lf::decode_smem(*layout, lf::n_slots_of(*layout));
+  if (S.total > 227 * 1024) return 0;
+  auto kern = lf::decode_partial_simt<__nv_bfloat16, __nv_bfloat16>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S.total);
+  int blocks = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kern, lf::kDecThreads, S.total) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  return blocks;
+}
+
 extern "C" size_t lf_decode_workspace_bytes(int batch, int kv_heads, int n_q, int head_dim,
                                             int max_splits) {
   if (batch <= 0 || kv_heads <= 0 || n_q <= 0 || head_dim <= 0 || max_splits <= 0) return 0;
@@ -440,9 +318,9 @@ extern "C" size_t lf_decode_workspace_bytes(int batch, int kv_heads, int n_q, in
   return static_cast<size_t>(batch) * kv_heads * max_splits * gq * (head_dim + 2) * sizeof(float);
 }
 
-extern "C" int lf_decode_max_splits(int64_t max_pages, int pages_per_split) {
-  if (max_pages < 0 || pages_per_split <= 0) return 0;
-  return static_cast<int>((max_pages + pages_per_split - 1) / pages_per_split) + 1;
+extern "C" int lf_decode_max_splits(int64_t max_pages, int pages_per_split, int page_size) {
+  if (max_pages < 0 || pages_per_split <= 0 || page_size <= 0) return 0;
+  return static_cast<int>((max_pages + pages_per_split - 1) / pages_per_split) + lf::residual_splits(page_size);
 }
 
 extern "C" int lf_decode_partial(const lf_layout* layout, const int32_t* rows, const uint16_t* kmeta,
@@ -453,7 +331,7 @@ extern "C" int lf_decode_partial(const lf_layout* layout, const int32_t* rows, c
                                  int64_t new_head_stride, const void* q, int q_dtype,
                                  int64_t q_seq_stride, int64_t q_head_stride, int batch, int n_q,
                                  float scaling, int pages_per_split, int max_splits,
-                                 float* workspace, lf_stream_t stream) {
+                                 float* workspace, int32_t* status, lf_stream_t stream) {
   LF_CHECK_ARG(layout != nullptr, "lf_decode_partial: null layout");
   const lf_layout& L = *layout;
   LF_CHECK_ARG(rows && slot_chan && hist_tokens && tail_k && tail_v && tail_len && q && workspace,
@@ -463,9 +341,20 @@ extern "C" int lf_decode_partial(const lf_layout* layout, const int32_t* rows, c
                "lf_decode_partial: batch %d, n_q %d, kv_heads %d", batch, n_q, L.kv_heads);
   LF_CHECK_ARG(pages_per_split > 0 && max_splits >= 1 && max_splits <= 65535,
                "lf_decode_partial: pages_per_split %d, max_splits %d", pages_per_split, max_splits);
-  LF_CHECK_ARG(max_splits >= lf_decode_max_splits(L.row_cap / L.page_size, pages_per_split),
+  LF_CHECK_ARG(max_splits >= lf_decode_max_splits(L.row_cap / L.page_size, pages_per_split, L.page_size),
                "lf_decode_partial: max_splits %d cannot cover row_cap %lld", max_splits,
                (long long)L.row_cap);
+  {
+    const int esz = resid_dtype == LF_F32 ? 4 : 2;
+    const bool aligned = (reinterpret_cast<uintptr_t>(tail_k) % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(tail_v) % 16 == 0) &&
+                         (tail_seq_stride * esz) % 16 == 0 && (tail_head_stride * esz) % 16 == 0 &&
+                         (k_new == nullptr || ((reinterpret_cast<uintptr_t>(k_new) % 16 == 0) &&
+                                               (reinterpret_cast<uintptr_t>(v_new) % 16 == 0) &&
+                                               (new_seq_stride * esz) % 16 == 0 && (new_head_stride * esz) % 16 == 0));
+    LF_CHECK_ARG(aligned, "lf_decode_partial: residual / new-token rows must be 16-byte aligned");
+  }
+  LF_CHECK_SUPPORTED(L.head_dim % 8 == 0, "decode head_dim %d must be a multiple of 8", L.head_dim);
   LF_CHECK_SUPPORTED(L.bit_v == 2, "decode supports bit_v 2, got %d", L.bit_v);
   LF_CHECK_SUPPORTED(L.k_group == L.page_size, "decode needs k_group == page_size (%d vs %d)",
                      L.k_group, L.page_size);
@@ -503,9 +392,11 @@ extern "C" int lf_decode_partial(const lf_layout* layout, const int32_t* rows, c
   p.n_slots = lf::n_slots_of(L);
   p.scaling = scaling;
   p.ws = workspace;
+  p.status = status;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (lf::tc_supported(L, p.gq, pages_per_split)) return lf::launch_partial_tc(p, resid_dtype, q_dtype, s);
   LF_CHECK_SUPPORTED(lf::decode_smem(L, p.n_slots).total <= 227 * 1024,
                      "decode shared memory %d B too large", lf::decode_smem(L, p.n_slots).total);
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (resid_dtype) {
     case LF_F32: return lf::dispatch_q<float>(p, q_dtype, s);
     case LF_F16: return lf::dispatch_q<__half>(p, q_dtype, s);

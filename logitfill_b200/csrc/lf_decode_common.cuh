@@ -1,0 +1,278 @@
+// Pieces shared by the decode kernels: launch parameters, CTA reductions,
+// the residual split (original-dtype tail rows + new token) and the partial
+// writer read by the merge kernel.
+#pragma once
+
+#include "lf_common.cuh"
+
+namespace lf {
+
+constexpr int kDecThreads = 128;
+constexpr int kGQ = 8;         // q-heads per KV head handled by one CTA
+constexpr int kResChunk = 32;  // residual tokens per chunk
+
+struct DecodeParams {
+  lf_layout L;
+  const int32_t* rows;
+  const uint16_t* kmeta;
+  const int32_t* slot_chan;
+  const int32_t* hist_tokens;
+  const void* tail_k;
+  const void* tail_v;
+  int64_t tail_seq_stride, tail_head_stride;
+  const int32_t* tail_len;
+  const void* k_new;
+  const void* v_new;
+  int64_t new_seq_stride, new_head_stride;
+  const void* q;
+  int64_t q_seq_stride, q_head_stride;
+  int batch, n_q, gq, pps, max_splits, n_slots;
+  float scaling;
+  float* ws;
+  int32_t* status;  // device status word (LF_ERR_DEVICE_TIMEOUT on a timed-out wait), may be null
+};
+
+// Sum (or max) of kGQ values over the CTA; every thread receives the result.
+template <bool kMax>
+__device__ __forceinline__ void block_reduce8(float (&v)[kGQ], float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int j = 0; j < kGQ; ++j) {
+    float x = v[j];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float y = __shfl_xor_sync(0xffffffffu, x, o);
+      x = kMax ? fmaxf(x, y) : x + y;
+    }
+    v[j] = x;
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int j = 0; j < kGQ; ++j) red[warp * kGQ + j] = v[j];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < kGQ; ++j) {
+    float x = red[j];
+#pragma unroll
+    for (int w = 1; w < kDecThreads / 32; ++w)
+      x = kMax ? fmaxf(x, red[w * kGQ + j]) : x + red[w * kGQ + j];
+    v[j] = x;
+  }
+  __syncthreads();
+}
+
+// Query group of KV head h (q-heads h*GQ .. h*GQ+GQ-1, the repeat_kv order
+// of reference.py:10-15) into q_s [kGQ][D] fp32, zero-padded to kGQ heads.
+template <typename QT>
+__device__ __forceinline__ void load_query_group(const DecodeParams& p, int b, int h, float* q_s) {
+  const int D = p.L.head_dim;
+  const QT* qb = static_cast<const QT*>(p.q) + b * p.q_seq_stride;
+  for (int i = threadIdx.x; i < kGQ * D; i += kDecThreads) {
+    const int j = i / D, d = i - j * D;
+    q_s[i] = j < p.gq ? Scalar<QT>::load(qb + (h * p.gq + j) * p.q_head_stride + d) : 0.0f;
+  }
+}
+
+// Residual splits: chunk c of the original-dtype residual (tail_len[b] tail
+// rows followed by the new token; reference.py:38-42) covers tokens
+// [kResChunk*c, kResChunk*(c+1)).  Up to ceil(page/kResChunk) chunks, one work
+// item each, so the residual is spread over several CTAs.
+__host__ __device__ inline int residual_splits(int page_size) { return (page_size + kResChunk - 1) / kResChunk; }
+
+struct ResidSmem {
+  int k, v, part, p, stat, total;  // byte offsets from the region base
+};
+__host__ __device__ inline ResidSmem resid_smem(int D) {
+  ResidSmem r;
+  int off = 0;
+  r.k = off; off += kResChunk * (D + 1) * 4;     // K rows, stride D+1 (conflict-free columns)
+  r.v = off; off += kResChunk * D * 4;           // V rows
+  r.part = off; off += 4 * kResChunk * kGQ * 4;  // per-warp partial scores
+  r.p = off; off += kResChunk * kGQ * 4;         // probabilities
+  r.stat = off; off += 3 * kGQ * 4;              // new max, alpha, chunk sum
+  r.total = off;
+  return r;
+}
+
+template <typename RT>
+__device__ __forceinline__ void load_vec_to_float(const RT* src, float* dst);
+template <>
+__device__ __forceinline__ void load_vec_to_float<__nv_bfloat16>(const __nv_bfloat16* src, float* dst) {
+  const uint4 u = *reinterpret_cast<const uint4*>(src);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    dst[2 * i] = __uint_as_float(w[i] << 16);
+    dst[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+template <>
+__device__ __forceinline__ void load_vec_to_float<__half>(const __half* src, float* dst) {
+  const uint4 u = *reinterpret_cast<const uint4*>(src);
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    dst[2 * i] = f.x;
+    dst[2 * i + 1] = f.y;
+  }
+}
+template <>
+__device__ __forceinline__ void load_vec_to_float<float>(const float* src, float* dst) {
+  const float4 a = *reinterpret_cast<const float4*>(src);
+  const float4 b = *reinterpret_cast<const float4*>(src + 4);
+  dst[0] = a.x; dst[1] = a.y; dst[2] = a.z; dst[3] = a.w;
+  dst[4] = b.x; dst[5] = b.y; dst[6] = b.z; dst[7] = b.w;
+}
+
+// One residual chunk: attention of the query group (q_s [kGQ][D]) over up to
+// kResChunk tokens in fp32.  Thread d < D accumulates channel d in acc; the
+// chunk's probability sum is added to lt of thread 0 only (lt is summed over
+// the CTA afterwards).  Rows are read 8 elements per load (16 B for bf16/fp16;
+// the residual page and the new-token rows are contiguous, D a multiple of 8).
+template <typename RT>
+__device__ void residual_chunk(const DecodeParams& p, int b, int h, int chunk, const float* q_s,
+                               unsigned char* region, float (&m)[kGQ], float (&acc)[kGQ], float (&lt)[kGQ]) {
+  const int D = p.L.head_dim, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, GQ = p.gq;
+  const ResidSmem RS = resid_smem(D);
+  float* k_s = reinterpret_cast<float*>(region + RS.k);
+  float* v_s = reinterpret_cast<float*>(region + RS.v);
+  float* part = reinterpret_cast<float*>(region + RS.part);
+  float* p_s = reinterpret_cast<float*>(region + RS.p);
+  float* stat = reinterpret_cast<float*>(region + RS.stat);
+  const int tl = p.tail_len[b];
+  const int total = tl + (p.k_new != nullptr ? 1 : 0);
+  const int t0 = chunk * kResChunk;
+  const int ntok = min(kResChunk, total - t0);
+  if (ntok <= 0) return;
+  const RT* tk = static_cast<const RT*>(p.tail_k) + b * p.tail_seq_stride + h * p.tail_head_stride;
+  const RT* tv = static_cast<const RT*>(p.tail_v) + b * p.tail_seq_stride + h * p.tail_head_stride;
+  const RT* nk = p.k_new != nullptr ? static_cast<const RT*>(p.k_new) + b * p.new_seq_stride + h * p.new_head_stride : nullptr;
+  const RT* nv = p.v_new != nullptr ? static_cast<const RT*>(p.v_new) + b * p.new_seq_stride + h * p.new_head_stride : nullptr;
+  // 1. Rows -> fp32 in shared memory; every thread issues all its loads first.
+  const int vec_per_row = D / 8;
+  const int nvec = kResChunk * vec_per_row;  // <= 512
+  constexpr int kMaxVec = kResChunk * 128 / 8 / kDecThreads;  // 4
+  float kv[kMaxVec][8], vv[kMaxVec][8];
+#pragma unroll
+  for (int r = 0; r < kMaxVec; ++r) {
+    const int i = tid + r * kDecThreads;
+    const int t = i / vec_per_row, c = i - t * vec_per_row;
+    const int tok = t0 + t;
+    if (i < nvec && t < ntok) {
+      const RT* ks = tok < tl ? tk + tok * D : nk;
+      const RT* vs = tok < tl ? tv + tok * D : nv;
+      load_vec_to_float<RT>(ks + c * 8, kv[r]);
+      load_vec_to_float<RT>(vs + c * 8, vv[r]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) kv[r][e] = vv[r][e] = 0.f;
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < kMaxVec; ++r) {
+    const int i = tid + r * kDecThreads;
+    if (i >= nvec) break;
+    const int t = i / vec_per_row, c = i - t * vec_per_row;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) k_s[t * (D + 1) + c * 8 + e] = kv[r][e];
+    *reinterpret_cast<float4*>(v_s + t * D + c * 8) = make_float4(vv[r][0], vv[r][1], vv[r][2], vv[r][3]);
+    *reinterpret_cast<float4*>(v_s + t * D + c * 8 + 4) = make_float4(vv[r][4], vv[r][5], vv[r][6], vv[r][7]);
+  }
+  __syncthreads();
+  // 2. Partial scores: lane = token, warp = quarter of the head dim.
+  {
+    const int dq = D / 4, d0 = warp * dq;
+    float ps[kGQ];
+#pragma unroll
+    for (int j = 0; j < kGQ; ++j) ps[j] = 0.f;
+    for (int d = d0; d < d0 + dq; ++d) {
+      const float kd = k_s[lane * (D + 1) + d];
+#pragma unroll
+      for (int j = 0; j < kGQ; ++j) ps[j] = fmaf(q_s[j * D + d], kd, ps[j]);
+    }
+    float* dst = part + (warp * kResChunk + lane) * kGQ;
+    *reinterpret_cast<float4*>(dst) = make_float4(ps[0], ps[1], ps[2], ps[3]);
+    *reinterpret_cast<float4*>(dst + 4) = make_float4(ps[4], ps[5], ps[6], ps[7]);
+  }
+  __syncthreads();
+  // 3. Softmax statistics of the chunk in warp 0 (lane = token).
+  if (warp == 0) {
+#pragma unroll
+    for (int j = 0; j < kGQ; ++j) {
+      float sj = -INFINITY;
+      if (lane < ntok && j < GQ) {
+        sj = (part[(0 * kResChunk + lane) * kGQ + j] + part[(1 * kResChunk + lane) * kGQ + j]) +
+             (part[(2 * kResChunk + lane) * kGQ + j] + part[(3 * kResChunk + lane) * kGQ + j]);
+        sj *= p.scaling;
+      }
+      float mx = sj;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float mnew = fmaxf(m[j], mx);
+      const float pj = (sj == -INFINITY) ? 0.f : expf(sj - mnew);
+      p_s[lane * kGQ + j] = pj;
+      float sum = pj;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      if (lane == 0) {
+        stat[j] = mnew;
+        stat[kGQ + j] = (m[j] == -INFINITY || mnew == -INFINITY) ? 0.f : expf(m[j] - mnew);
+        stat[2 * kGQ + j] = sum;
+      }
+    }
+  }
+  __syncthreads();
+  // 4. Rescale and accumulate.
+#pragma unroll
+  for (int j = 0; j < kGQ; ++j) {
+    if (j >= GQ) continue;
+    const float alpha = stat[kGQ + j];
+    m[j] = stat[j];
+    lt[j] = lt[j] * alpha + (tid == 0 ? stat[2 * kGQ + j] : 0.f);
+    acc[j] *= alpha;
+  }
+  if (tid < D) {
+    for (int t = 0; t < ntok; ++t) {
+      const float v = v_s[t * D + tid];
+      const float4 a = *reinterpret_cast<const float4*>(p_s + t * kGQ);
+      const float4 c = *reinterpret_cast<const float4*>(p_s + t * kGQ + 4);
+      acc[0] = fmaf(a.x, v, acc[0]);
+      acc[1] = fmaf(a.y, v, acc[1]);
+      acc[2] = fmaf(a.z, v, acc[2]);
+      acc[3] = fmaf(a.w, v, acc[3]);
+      acc[4] = fmaf(c.x, v, acc[4]);
+      acc[5] = fmaf(c.y, v, acc[5]);
+      acc[6] = fmaf(c.z, v, acc[6]);
+      acc[7] = fmaf(c.w, v, acc[7]);
+    }
+  }
+}
+
+// Write one work item's partial: acc[j][d] + lv[j], m[j] (natural-log units), l[j].
+// lt/lvt are per-thread partial sums, reduced here over the CTA.
+__device__ __forceinline__ void write_partial(const DecodeParams& p, int b, int h, int s, int channel,
+                                              const float (&acc)[kGQ], const float (&m)[kGQ],
+                                              float (&lt)[kGQ], float (&lvt)[kGQ], float* red) {
+  const int D = p.L.head_dim, GQ = p.gq, H = p.L.kv_heads;
+  block_reduce8<false>(lt, red);
+  block_reduce8<false>(lvt, red);
+  float* item = p.ws + ((static_cast<int64_t>(b) * H + h) * p.max_splits + s) * (GQ * (D + 2));
+  if (channel >= 0 && channel < D) {
+#pragma unroll
+    for (int j = 0; j < kGQ; ++j)
+      if (j < GQ) item[j * D + channel] = acc[j] + lvt[j];
+  }
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int j = 0; j < kGQ; ++j) {
+      if (j < GQ) {
+        item[GQ * D + j] = m[j];
+        item[GQ * D + GQ + j] = lt[j];
+      }
+    }
+  }
+}
+
+}  // namespace lf

@@ -14,15 +14,31 @@ import torch
 from logitfill_b200 import _lib
 from logitfill_b200.packed.cache import PackedKVCache, PackedKVManager
 
-TARGET_ITEMS = 4 * 148  # aim for ~4 CTAs per SM across the (seq, head, split) grid
-
-
-def pages_per_split(cache: PackedKVCache) -> int:
-    """Pages per K2 work item for this cache's capacity, sized so the grid
-    covers the 148 SMs several times over."""
-    cap_pages = cache.row_cap // cache.page_size
-    total = cache.batch * cache.n_kv * max(cap_pages, 1)
-    return max(1, min(cap_pages, -(-total // TARGET_ITEMS)))
+def pages_per_split(cache: PackedKVCache, layer_idx: int = 0) -> int:
+    """Pages per K2 work item.  Every (sequence, KV head) history is cut into
+    ceil(pages / pps) items, plus up to ceil(page/32) residual items; the
+    choice minimises (waves of resident CTAs) x (pages per item), i.e. it
+    balances the grid over the SMs instead of just making it large."""
+    layer = cache.layers[layer_idx]
+    P = cache.page_size
+    pages = int(layer.hist_len.max()) // P if layer.hist_len.size else 0
+    if pages <= 1:
+        return 1
+    so = _lib.lib()
+    sms = torch.cuda.get_device_properties(cache.device).multi_processor_count
+    pairs = cache.batch * cache.n_kv
+    resid = sum(-(-(int(t) + 1) // 32) for t in layer.tail_len) * cache.n_kv
+    best, best_cost = 1, None
+    for pps in range(1, pages + 1):
+        occ = so.lf_decode_occupancy(ctypes.byref(layer.layout.c), cache.n_q, pps)
+        if occ <= 0:
+            continue
+        ctas = pairs * (-(-pages // pps))
+        waves = -(-(ctas + resid // 4) // (sms * occ))
+        cost = waves * pps + 0.05 * (-(-pages // pps))
+        if best_cost is None or cost < best_cost:
+            best, best_cost = pps, cost
+    return best
 
 
 class DecodeCall:
@@ -56,8 +72,8 @@ class DecodeCall:
         self.query, self.key_new, self.value_new, self.out = query, key_new, value_new, out
         self.scaling = float(scaling)
         self.resid_dtype = resid_dtype
-        self.pps = pages_per_split(cache) if pps is None else int(pps)
-        self.max_splits = _lib.lib().lf_decode_max_splits(cache.row_cap // cache.page_size, self.pps)
+        self.pps = pages_per_split(cache, layer_idx) if pps is None else int(pps)
+        self.max_splits = _lib.lib().lf_decode_max_splits(cache.row_cap // cache.page_size, self.pps, cache.page_size)
         self.ws = cache.workspace(self.max_splits)
 
     def launch_partial(self) -> None:
@@ -69,7 +85,7 @@ class DecodeCall:
             _lib.ptr(L.dev_tail), _lib.dtype_code(self.resid_dtype), _lib.ptr(kn), _lib.ptr(self.value_new),
             kn.stride(0) if kn is not None else 0, kn.stride(1) if kn is not None else 0,
             _lib.ptr(self.query), _lib.dtype_code(self.query.dtype), self.query.stride(0), self.query.stride(1),
-            c.batch, c.n_q, self.scaling, self.pps, self.max_splits, _lib.ptr(self.ws),
+            c.batch, c.n_q, self.scaling, self.pps, self.max_splits, _lib.ptr(self.ws), _lib.ptr(c.status),
             _lib.stream_handle(self.query.device)), "lf_decode_partial")
 
     def launch_merge(self) -> None:

@@ -175,6 +175,8 @@ class PackedKVCache:
                 else torch.as_tensor(level, dtype=torch.int64).cpu()
             self.layers.append(_Layer(lv, self))
         self._workspace: Optional[torch.Tensor] = None
+        # Device status word written by kernels whose bounded waits expire.
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
 
     @property
     def n_layers(self) -> int:
@@ -212,6 +214,13 @@ class PackedKVCache:
         if self._workspace is None or self._workspace.numel() * 4 < need:
             self._workspace = torch.empty(need // 4, dtype=torch.float32, device=self.device)
         return self._workspace
+
+    def check_status(self) -> None:
+        """Raise if a kernel reported a device-side failure (synchronises)."""
+        code = int(self.status.item())
+        if code:
+            self.status.zero_()
+            _lib.check(code, "packed KV kernel")
 
     def length(self, b: int = 0, layer_idx: int = 0) -> int:
         layer = self.layers[layer_idx]

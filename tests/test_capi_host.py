@@ -99,14 +99,14 @@ def test_entry_points_validate_before_launch():
     fake = 1 << 20  # never dereferenced: validation fails first
     # max_splits too small for the capacity
     st = so.lf_decode_partial(ctypes.byref(lay.c), fake, fake, fake, fake, fake, fake, 0, 0, fake, 2, None, None,
-                              0, 0, fake, 2, 0, 0, 1, 2, 1.0, 1, 1, fake, None)
+                              0, 0, fake, 2, 0, 0, 1, 2, 1.0, 1, 1, fake, None, None)
     assert st == _lib.LF_ERR_INVALID_ARGUMENT
     # GQA group of 16 exceeds what one CTA computes
     st = so.lf_decode_partial(ctypes.byref(lay.c), fake, fake, fake, fake, fake, fake, 0, 0, fake, 2, None, None,
-                              0, 0, fake, 2, 0, 0, 1, 32, 1.0, 1, 5, fake, None)
+                              0, 0, fake, 2, 0, 0, 1, 32, 1.0, 1, 10, fake, None, None)
     assert st == _lib.LF_ERR_UNSUPPORTED
     assert so.lf_decode_merge(None, None, 1, 1, 1, 64, 64, 1, 1, None, 0, 0, 0, None) == _lib.LF_ERR_INVALID_ARGUMENT
-    assert so.lf_decode_max_splits(256, 16) == 17
+    assert so.lf_decode_max_splits(256, 16, 128) == 16 + 4
     assert so.lf_decode_workspace_bytes(2, 4, 28, 128, 5) == 2 * 4 * 5 * 7 * 130 * 4
 
 

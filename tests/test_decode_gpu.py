@@ -142,14 +142,17 @@ def test_long_context_split_merge_property():
         out = torch.empty(B, NQ, D, dtype=torch.float32, device="cuda")
         decode_into(cache, 0, q, kn, vn, D ** -0.5, out, pps=pps)
         outs.append(out)
+    # fp32 accumulation order differs between split sizes (one split sums up
+    # to 32k tokens serially); the results agree far inside the 2e-3 bound.
     for o in outs[1:]:
-        assert float((o - outs[0]).abs().max()) < 1e-4
+        assert float((o - outs[0]).abs().max()) < 1e-3
     ref = orc.OracleLayer(levels, 128, 128, 128, 2)
     ref.append(k[1, :, :T].float().cpu().numpy(), v[1, :, :T].float().cpu().numpy())
     want = orc.reference_attention(ref, q[1, :, None].float().cpu().numpy(), kn[1, :, None].float().cpu().numpy(),
                                    vn[1, :, None].float().cpu().numpy(), D ** -0.5)
-    ok, err, cos = attention_close(outs[0][1].cpu().numpy(), want[:, 0])
-    assert ok, (err, cos)
+    for pps, o in zip((1, 7, 64, 256), outs):
+        ok, err, cos = attention_close(o[1].cpu().numpy(), want[:, 0])
+        assert ok, (pps, err, cos)
 
 
 def test_errors_are_raised_not_swallowed():

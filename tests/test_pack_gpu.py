@@ -90,7 +90,7 @@ def test_capacity_growth_keeps_history():
     """Commits beyond the initial capacity reallocate and keep every byte."""
     case = cases.config0_like(1024, 37)
     mgr = manager_for(case, capacity=128)
-    assert mgr.cache.row_cap >= 1024 + 128
+    assert mgr.cache.row_cap >= 1024  # packed pages only; the tail lives in the residual page
     _check_store(mgr, case)
 
 
