@@ -284,7 +284,7 @@ def run_b200(args, cfg) -> None:
     vn = torch.randn(L, B, H, D, generator=gen, device=dev).to(torch.bfloat16)
     out = torch.empty(L, B, NQ, D, device=dev, dtype=torch.bfloat16)
     scaling = D ** -0.5
-    calls = [DecodeCall(cache, l, q[l], kn[l], vn[l], scaling, out[l]) for l in range(L)]
+    calls = [DecodeCall(cache, l, q[l], kn[l], vn[l], scaling, out[l], pps=args.pps) for l in range(L)]
 
     def step():
         for c in calls:
@@ -382,6 +382,7 @@ def run_b200(args, cfg) -> None:
             "config": workload_config(cfg, world),
             "hbm_gbs": step_gbs * world, "hbm_frac_of_peak_per_gpu": step_gbs / peak,
             "key_mean_bits": mean_key_bits(levels),
+            "pages_per_split": calls[0].pps,
             "roofline": {"kernel": "lf_decode_partial (K2)", "bound": "hbm", "achieved": achieved,
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                          "traffic": None, "bytes_per_launch": k2_bytes_avg, "avg_launch_ms": k2_avg_ms},
@@ -406,6 +407,8 @@ def main() -> None:
     ap.add_argument("--config", type=int, default=1, choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--pps", type=int, default=None,
+                    help="pages per K2 work item (default: the occupancy-aware planner)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -64,7 +64,7 @@ typedef struct lf_layout {
   int32_t vcode_off;    /* word offset of the Value codes                        */
   int32_t vcode_words;  /* D * bit_v / 32                                        */
   int32_t half_off;     /* word offset of the fp16 region                        */
-  int32_t row_words;    /* words per row, multiple of 4                          */
+  int32_t row_words;    /* words per row, odd (bank-conflict-free row reads)     */
   int32_t meta_halves;  /* fp16 per Key-group meta row, multiple of 8            */
   int32_t scale_off[3]; /* fp16 offset of each tier's scales in a meta row       */
   int32_t min_off[3];   /* fp16 offset of each tier's mins in a meta row         */

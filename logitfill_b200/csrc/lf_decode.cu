@@ -20,7 +20,7 @@ namespace lf {
 // Tensor-core decode (lf_decode_tc.cu).
 bool tc_supported(const lf_layout& L, int gq, int pps);
 int launch_partial_tc(const DecodeParams& p, int resid_dtype, int q_dtype, cudaStream_t stream);
-int occupancy_tc(const lf_layout& L, int pps);
+int occupancy_tc(const lf_layout& L, int gq, int pps);
 
 struct DecodeSmem {
   int q, qp, p, red, slot, slot16, region, rows_bytes, total;
@@ -224,7 +224,7 @@ decode_partial_simt(DecodeParams p) {
       }
     }
   } else {
-    residual_chunk<RT>(p, b, h, s - n_page_splits, q_s, region, m, acc, lt);
+    residual_chunk(p, b, h, s - n_page_splits, q_s, region, m, acc, lt);
   }
 
   write_partial(p, b, h, s, tid, acc, m, lt, lvt, red);
@@ -298,7 +298,7 @@ static int dispatch_q(const DecodeParams& p, int q_dtype, cudaStream_t stream) {
 extern "C" int lf_decode_occupancy(const lf_layout* layout, int n_q, int pages_per_split) {
   if (layout == nullptr || n_q <= 0 || pages_per_split <= 0 || n_q % layout->kv_heads) return 0;
   const int gq = n_q / layout->kv_heads;
-  if (lf::tc_supported(*layout, gq, pages_per_split)) return lf::occupancy_tc(*layout, pages_per_split);
+  if (lf::tc_supported(*layout, gq, pages_per_split)) return lf::occupancy_tc(*layout, gq, pages_per_split);
   const lf::DecodeSmem S = lf::decode_smem(*layout, lf::n_slots_of(*layout));
   if (S.total > 227 * 1024) return 0;
   auto kern = lf::decode_partial_simt<__nv_bfloat16, __nv_bfloat16>;
@@ -362,8 +362,8 @@ extern "C" int lf_decode_partial(const lf_layout* layout, const int32_t* rows, c
                      L.v_group, L.head_dim);
   LF_CHECK_SUPPORTED(L.head_dim % 16 == 0 && L.head_dim <= lf::kDecThreads,
                      "decode head_dim %d not supported", L.head_dim);
-  LF_CHECK_SUPPORTED(L.page_size <= lf::kDecThreads, "decode page_size %d > %d", L.page_size,
-                     lf::kDecThreads);
+  LF_CHECK_SUPPORTED(L.page_size <= lf::kDecThreads && L.page_size % 4 == 0,
+                     "decode page_size %d must be a multiple of 4 and at most %d", L.page_size, lf::kDecThreads);
   LF_CHECK_SUPPORTED(n_q / L.kv_heads <= lf::kGQ, "decode GQA group %d > %d", n_q / L.kv_heads,
                      lf::kGQ);
   lf::DecodeParams p{};
@@ -393,6 +393,8 @@ extern "C" int lf_decode_partial(const lf_layout* layout, const int32_t* rows, c
   p.scaling = scaling;
   p.ws = workspace;
   p.status = status;
+  p.resid_dtype = resid_dtype;
+  p.q_dtype = q_dtype;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (lf::tc_supported(L, p.gq, pages_per_split)) return lf::launch_partial_tc(p, resid_dtype, q_dtype, s);
   LF_CHECK_SUPPORTED(lf::decode_smem(L, p.n_slots).total <= 227 * 1024,

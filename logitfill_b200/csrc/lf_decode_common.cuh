@@ -30,6 +30,7 @@ struct DecodeParams {
   float scaling;
   float* ws;
   int32_t* status;  // device status word (LF_ERR_DEVICE_TIMEOUT on a timed-out wait), may be null
+  int q_dtype, resid_dtype;  // lf_dtype of q and of the residual rows
 };
 
 // Sum (or max) of kGQ values over the CTA; every thread receives the result.
@@ -72,6 +73,49 @@ __device__ __forceinline__ void load_query_group(const DecodeParams& p, int b, i
     const int j = i / D, d = i - j * D;
     q_s[i] = j < p.gq ? Scalar<QT>::load(qb + (h * p.gq + j) * p.q_head_stride + d) : 0.0f;
   }
+}
+
+__device__ __forceinline__ float load_dtype(const void* base, int64_t idx, int dtype) {
+  switch (dtype) {
+    case LF_F32: return static_cast<const float*>(base)[idx];
+    case LF_F16: return __half2float(static_cast<const __half*>(base)[idx]);
+    default: return __bfloat162float(static_cast<const __nv_bfloat16*>(base)[idx]);
+  }
+}
+// Query group as load_query_group, dtype chosen at run time (p.q_dtype).
+__device__ __forceinline__ void load_query_group_rt(const DecodeParams& p, int b, int h, float* q_s, int nthreads) {
+  const int D = p.L.head_dim;
+  for (int i = threadIdx.x; i < kGQ * D; i += nthreads) {
+    const int j = i / D, d = i - j * D;
+    q_s[i] = j < p.gq ? load_dtype(p.q, b * p.q_seq_stride + (h * p.gq + j) * p.q_head_stride + d, p.q_dtype)
+                      : 0.0f;
+  }
+}
+
+// Named barrier over the first `count` threads of the CTA (id >= 1).
+__device__ __forceinline__ void named_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Sum of N values over the first 128 threads only, synchronised on barrier `bar_id`.
+template <int N>
+__device__ __forceinline__ void group_sum(float (&v)[N], float* red, int bar_id) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    float x = v[j];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    v[j] = x;
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) red[warp * kGQ + j] = v[j];
+  }
+  named_sync(bar_id, kDecThreads);
+#pragma unroll
+  for (int j = 0; j < N; ++j) v[j] = (red[j] + red[kGQ + j]) + (red[2 * kGQ + j] + red[3 * kGQ + j]);
+  named_sync(bar_id, kDecThreads);
 }
 
 // Residual splits: chunk c of the original-dtype residual (tail_len[b] tail
@@ -131,9 +175,19 @@ __device__ __forceinline__ void load_vec_to_float<float>(const float* src, float
 // chunk's probability sum is added to lt of thread 0 only (lt is summed over
 // the CTA afterwards).  Rows are read 8 elements per load (16 B for bf16/fp16;
 // the residual page and the new-token rows are contiguous, D a multiple of 8).
-template <typename RT>
-__device__ void residual_chunk(const DecodeParams& p, int b, int h, int chunk, const float* q_s,
-                               unsigned char* region, float (&m)[kGQ], float (&acc)[kGQ], float (&lt)[kGQ]) {
+// 8 consecutive elements of dtype `dtype` (16-byte aligned rows) as fp32.
+__device__ __forceinline__ void load_vec_to_float_rt(const void* src, int dtype, float* dst) {
+  switch (dtype) {
+    case LF_F32: load_vec_to_float<float>(static_cast<const float*>(src), dst); break;
+    case LF_F16: load_vec_to_float<__half>(static_cast<const __half*>(src), dst); break;
+    default: load_vec_to_float<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(src), dst); break;
+  }
+}
+
+static __device__ __noinline__ void residual_chunk(const DecodeParams& p, int b, int h, int chunk, const float* q_s,
+                                            unsigned char* region, float (&m)[kGQ], float (&acc)[kGQ],
+                                            float (&lt)[kGQ]) {
+  const int RS_ = p.resid_dtype == LF_F32 ? 4 : 2;  // element size
   const int D = p.L.head_dim, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, GQ = p.gq;
   const ResidSmem RS = resid_smem(D);
   float* k_s = reinterpret_cast<float*>(region + RS.k);
@@ -146,10 +200,14 @@ __device__ void residual_chunk(const DecodeParams& p, int b, int h, int chunk, c
   const int t0 = chunk * kResChunk;
   const int ntok = min(kResChunk, total - t0);
   if (ntok <= 0) return;
-  const RT* tk = static_cast<const RT*>(p.tail_k) + b * p.tail_seq_stride + h * p.tail_head_stride;
-  const RT* tv = static_cast<const RT*>(p.tail_v) + b * p.tail_seq_stride + h * p.tail_head_stride;
-  const RT* nk = p.k_new != nullptr ? static_cast<const RT*>(p.k_new) + b * p.new_seq_stride + h * p.new_head_stride : nullptr;
-  const RT* nv = p.v_new != nullptr ? static_cast<const RT*>(p.v_new) + b * p.new_seq_stride + h * p.new_head_stride : nullptr;
+  const char* tk = static_cast<const char*>(p.tail_k) + (b * p.tail_seq_stride + h * p.tail_head_stride) * RS_;
+  const char* tv = static_cast<const char*>(p.tail_v) + (b * p.tail_seq_stride + h * p.tail_head_stride) * RS_;
+  const char* nk = p.k_new != nullptr
+                       ? static_cast<const char*>(p.k_new) + (b * p.new_seq_stride + h * p.new_head_stride) * RS_
+                       : nullptr;
+  const char* nv = p.v_new != nullptr
+                       ? static_cast<const char*>(p.v_new) + (b * p.new_seq_stride + h * p.new_head_stride) * RS_
+                       : nullptr;
   // 1. Rows -> fp32 in shared memory; every thread issues all its loads first.
   const int vec_per_row = D / 8;
   const int nvec = kResChunk * vec_per_row;  // <= 512
@@ -161,10 +219,10 @@ __device__ void residual_chunk(const DecodeParams& p, int b, int h, int chunk, c
     const int t = i / vec_per_row, c = i - t * vec_per_row;
     const int tok = t0 + t;
     if (i < nvec && t < ntok) {
-      const RT* ks = tok < tl ? tk + tok * D : nk;
-      const RT* vs = tok < tl ? tv + tok * D : nv;
-      load_vec_to_float<RT>(ks + c * 8, kv[r]);
-      load_vec_to_float<RT>(vs + c * 8, vv[r]);
+      const char* ks = tok < tl ? tk + static_cast<int64_t>(tok) * D * RS_ : nk;
+      const char* vs = tok < tl ? tv + static_cast<int64_t>(tok) * D * RS_ : nv;
+      load_vec_to_float_rt(ks + c * 8 * RS_, p.resid_dtype, kv[r]);
+      load_vec_to_float_rt(vs + c * 8 * RS_, p.resid_dtype, vv[r]);
     } else {
 #pragma unroll
       for (int e = 0; e < 8; ++e) kv[r][e] = vv[r][e] = 0.f;
@@ -180,7 +238,7 @@ __device__ void residual_chunk(const DecodeParams& p, int b, int h, int chunk, c
     *reinterpret_cast<float4*>(v_s + t * D + c * 8) = make_float4(vv[r][0], vv[r][1], vv[r][2], vv[r][3]);
     *reinterpret_cast<float4*>(v_s + t * D + c * 8 + 4) = make_float4(vv[r][4], vv[r][5], vv[r][6], vv[r][7]);
   }
-  __syncthreads();
+  named_sync(1, kDecThreads);
   // 2. Partial scores: lane = token, warp = quarter of the head dim.
   {
     const int dq = D / 4, d0 = warp * dq;
@@ -196,7 +254,7 @@ __device__ void residual_chunk(const DecodeParams& p, int b, int h, int chunk, c
     *reinterpret_cast<float4*>(dst) = make_float4(ps[0], ps[1], ps[2], ps[3]);
     *reinterpret_cast<float4*>(dst + 4) = make_float4(ps[4], ps[5], ps[6], ps[7]);
   }
-  __syncthreads();
+  named_sync(1, kDecThreads);
   // 3. Softmax statistics of the chunk in warp 0 (lane = token).
   if (warp == 0) {
 #pragma unroll
@@ -223,7 +281,7 @@ __device__ void residual_chunk(const DecodeParams& p, int b, int h, int chunk, c
       }
     }
   }
-  __syncthreads();
+  named_sync(1, kDecThreads);
   // 4. Rescale and accumulate.
 #pragma unroll
   for (int j = 0; j < kGQ; ++j) {
@@ -246,6 +304,31 @@ __device__ void residual_chunk(const DecodeParams& p, int b, int h, int chunk, c
       acc[5] = fmaf(c.y, v, acc[5]);
       acc[6] = fmaf(c.z, v, acc[6]);
       acc[7] = fmaf(c.w, v, acc[7]);
+    }
+  }
+}
+
+// Partial writer for the first 128 threads only (barrier `bar_id`), N >= p.gq.
+template <int N>
+__device__ __forceinline__ void write_partial_group(const DecodeParams& p, int b, int h, int s, int channel,
+                                                    const float (&acc)[N], const float (&m)[N],
+                                                    float (&lt)[N], float (&lvt)[N], float* red, int bar_id) {
+  const int D = p.L.head_dim, GQ = p.gq, H = p.L.kv_heads;
+  group_sum<N>(lt, red, bar_id);
+  group_sum<N>(lvt, red, bar_id);
+  float* item = p.ws + ((static_cast<int64_t>(b) * H + h) * p.max_splits + s) * (GQ * (D + 2));
+  if (channel >= 0 && channel < D) {
+#pragma unroll
+    for (int j = 0; j < N; ++j)
+      if (j < GQ) item[j * D + channel] = acc[j] + lvt[j];
+  }
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      if (j < GQ) {
+        item[GQ * D + j] = m[j];
+        item[GQ * D + GQ + j] = lt[j];
+      }
     }
   }
 }

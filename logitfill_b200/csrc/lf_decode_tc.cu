@@ -1,33 +1,33 @@
 // K2 on the 5th-generation tensor cores (sm_100a, tcgen05.mma kind::i8).
 //
 // Geometry: head_dim 128, page 128 = Key group 128, Value group 128, bit_v 2
-// (the LogitFill defaults, deepseek_qwen.py:24-46).  One 128-thread CTA per
-// (split, KV head, sequence) work item; thread t owns token t of the current
-// page, TMEM lane t and, for the PV result, head-dim position t.
+// (the LogitFill defaults, deepseek_qwen.py:24-46).  One CTA per (split, KV
+// head, sequence) work item: four compute warps (thread t owns token t of the
+// current page, TMEM lane t and head-dim position t of the PV result) and one
+// control warp that issues the 1-D bulk copies of the page row blocks and the
+// tensor-core MMAs.
 //
-// Per page (128 tokens) of packed history:
-//   [A] the row block (all tiers' Key codes, Value codes, FP16 Key tier,
-//       Value scale/min of 128 tokens) arrives by one 1-D bulk copy;
-//       each thread unpacks its token's Key codes to u8 straight into TMEM
-//       (A operand of QK, K-major) and its Value codes to u8 into shared memory
-//       (A operand of PV, MN-major), and writes the B row of QK for its tier
-//       slots: 24-bit fixed point X = q_j * scale_c * 2^-E_j offset by 2^23,
-//       three unsigned limbs, plus a column of ones.
-//   QK = codes . B  (5 x M128 N32 K32 MMAs for 160 slots)
-//       score_tj = 2^E_j (acc0 + 256 acc1 + 65536 (acc2 - 128 ones))
-//                  + sum_c q_j[c] min_c + FP16-tier part,
-//   [B] online softmax over the page (one CTA max per q-head), then the B
-//       row of PV for token t: 23-bit fixed point p_tj * vscale_t, 3 limbs.
-//   PV = Vcodes^T . B  (4 x M128 N32 K32 MMAs)
-//   [C] o_j = o_j alpha_j + 2^Ev_j (acc0 + 256 acc1 + 65536 acc2).
-// The Value-min term sum_t p_tj vmin_t and the normaliser are per-thread
-// partial sums reduced once per work item.
+// Per page (128 tokens) of packed history, with X = 24-bit fixed point:
+//   U_K  Key codes -> u8 in TMEM (A of QK, K-major); the B row of QK for the
+//        thread's tier slots: X(q_j[c] * scale_c) + 2^23 as three unsigned
+//        limbs plus a column of ones; FP16-tier partial scores (CUDA cores).
+//   QK   5 x M128 N32 K32:  acc0 + 256 acc1 + 65536 (acc2 - 128 ones)
+//        = sum_c code_tc X_jc, exact in int32.
+//   S    scores (+ sum_c q_j[c] min_c + FP16 part), page max per q-head over
+//        the four compute warps, online-softmax update, B row of PV for token
+//        t: 23-bit X(p_tj * vscale_t), three limbs.
+//   U_V  Value codes -> u8 in shared memory (A of PV, MN-major).
+//   PV   4 x M128 N32 K32;  C: o_j = o_j alpha_j + 2^Ev_j (acc0 + 256 acc1 + 65536 acc2).
+// Compute warps run S(i), U_K(i+1), C(i), U_V(i+1): PV(i) overlaps U_K(i+1)
+// and QK(i+1) overlaps C(i) and U_V(i+1).  The Value-min term sum_t p_tj
+// vmin_t and the normaliser are per-thread partial sums reduced per item.
 //
 // The integer products are exact; the fixed-point rounding is 2^-22 (QK) and
 // 2^-23 (PV) of the per-page block maximum (tests/kernel_model.py models it).
-// Every mbarrier wait is bounded (2 s): on expiry the CTA sets
-// LF_ERR_DEVICE_TIMEOUT in the status word, drains its own copies and MMAs,
-// frees its TMEM and returns.
+// Every mbarrier wait is bounded (2 s).  On expiry the CTA records
+// LF_ERR_DEVICE_TIMEOUT, stops waiting (every warp still passes the same
+// barriers, so nothing deadlocks), drains its own copies and MMAs, frees its
+// TMEM and returns.
 #include <atomic>
 
 #include "lf_decode_common.cuh"
@@ -46,9 +46,13 @@ constexpr uint32_t kIdescQK = idesc_u8(128, 32, false, true);  // A: TMEM (K-maj
 constexpr uint32_t kIdescPV = idesc_u8(128, 32, true, true);   // A, B: MN-major smem
 constexpr uint32_t kM2 = 0x03030303u, kM4 = 0x0F0F0F0Fu;
 
+constexpr int kStages = 2;
+constexpr int kThreads = kDecThreads + 32;  // 4 compute warps + 1 control warp
+constexpr int kMaxPagesPerItem = 16;        // bounds the per-item meta buffer
+
 struct TcSmem {
-  int bars, red, kpos, esc, qs, q16, stage0, stage1, meta, apv, bqk, bpv, total;
-  int kpad, a_col, tm_qk, tm_pv, tm_cols, bqk_sbo;
+  int bars, red, kpos, esc, q16, stage0, meta, apv, qs, bqk, bpv, total;
+  int kpad, a_col, tm_qk, tm_pv, tm_cols, bqk_sbo, stage_bytes;
 };
 
 __host__ __device__ inline int n_slots_of(const lf_layout& L) {
@@ -67,24 +71,21 @@ __host__ __device__ inline TcSmem tc_smem(const lf_layout& L, int pps) {
   while (cols < need) cols *= 2;
   s.tm_cols = cols;
   s.bqk_sbo = s.kpad * 16;
+  s.stage_bytes = kP * L.row_words * 4;
   int off = 0;
-  s.bars = off; off += 64;
-  s.red = off; off += 256 * 4;
+  s.bars = off; off += 128;
+  s.red = off; off += 320 * 4;
   s.kpos = off; off += s.kpad * 4;
   s.esc = off; off += ((pps + 3) / 4 * 4) * 4;
-  s.qs = off; off += kGQ * kD * 4;
   s.q16 = off; off += (L.width[3] > 0 ? L.width[3] : 1) * kGQ * 4;
   off = (off + 127) / 128 * 128;
-  s.stage0 = off; off += kP * L.row_words * 4;
-  s.stage1 = off; off += kP * L.row_words * 4;
+  s.stage0 = off; off += kStages * s.stage_bytes;
   s.meta = off; off += (pps * L.meta_halves * 2 + 15) / 16 * 16;
   off = (off + 1023) / 1024 * 1024;
-  s.apv = off; off += kP * kD;
+  s.apv = off; off += 2 * kP * kD;   // two Value tiles (page parity)
+  s.qs = s.apv + kP * kD;           // the query group aliases the second tile in the prologue
   s.bqk = off; off += s.kpad * 32;
   s.bpv = off; off += kP * 32;
-  // The residual split reuses the region from stage0 for fp32 K/V rows.
-  const int resid_end = s.stage0 + resid_smem(kD).total;
-  if (resid_end > off) off = resid_end;
   s.total = (off + 1023) / 1024 * 1024;
   return s;
 }
@@ -179,307 +180,392 @@ __device__ __forceinline__ int exp2_ceil(float x) {
 // 2^e as a float, e in [-126, 127].
 __device__ __forceinline__ float exp2i(int e) { return __int_as_float((e + 127) << 23); }
 
-template <typename RT, typename QT>
-__global__ void __launch_bounds__(kDecThreads, 3) decode_partial_tc(DecodeParams p) {
+// Barrier slots in shared memory.
+enum { kBarFull = 0, kBarKReady = kStages, kBarVReady, kBarQK, kBarPV, kNumBars };
+
+template <int GQ>
+__global__ void __launch_bounds__(kThreads, 3) decode_partial_tc(DecodeParams p) {
   extern __shared__ __align__(1024) unsigned char smem[];
   const lf_layout& L = p.L;
   const TcSmem S = tc_smem(L, p.pps);
   const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
-  const int H = L.kv_heads, R = L.row_words, M = L.meta_halves, GQ = p.gq;
+  const int H = L.kv_heads, R = L.row_words, M = L.meta_halves;
   const int pages = p.hist_tokens[b] / kP;
   const int n_page_splits = (pages + p.pps - 1) / p.pps;
   if (s >= n_page_splits + residual_splits(kP)) return;
 
   float* q_s = reinterpret_cast<float*>(smem + S.qs);
   float* red = reinterpret_cast<float*>(smem + S.red);
-  float m[kGQ], o[kGQ], lt[kGQ], lvt[kGQ];
-#pragma unroll
-  for (int j = 0; j < kGQ; ++j) {
-    m[j] = -INFINITY;
-    o[j] = 0.f;
-    lt[j] = 0.f;
-    lvt[j] = 0.f;
-  }
-  load_query_group<QT>(p, b, h, q_s);
 
-  if (s >= n_page_splits) {  // residual splits: tail rows + new token, fp32
-    residual_chunk<RT>(p, b, h, s - n_page_splits, q_s, smem + S.stage0, m, o, lt);
-    write_partial(p, b, h, s, tid, o, m, lt, lvt, red);
+  if (s >= n_page_splits) {  // residual splits: tail rows + new token, fp32 (compute warps)
+    if (warp >= 4) return;
+    float m[kGQ], o[kGQ], lt[kGQ], lvt[kGQ];
+#pragma unroll
+    for (int j = 0; j < kGQ; ++j) {
+      m[j] = -INFINITY;
+      o[j] = lt[j] = lvt[j] = 0.f;
+    }
+    load_query_group_rt(p, b, h, q_s, kDecThreads);
+    const int c = s - n_page_splits;
+    unsigned char* region = smem + S.stage0;
+    residual_chunk(p, b, h, c, q_s, region, m, o, lt);
+    write_partial_group<kGQ>(p, b, h, s, tid, o, m, lt, lvt, red, 1);
     return;
   }
 
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S.bars);  // full[0], full[1], qk, pv
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S.bars + 32);
-  volatile int* abort_s = reinterpret_cast<volatile int*>(smem + S.bars + 36);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S.bars);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S.bars + 8 * kNumBars);
+  volatile int* abort_s = reinterpret_cast<volatile int*>(smem + S.bars + 8 * kNumBars + 4);
   int* kpos_s = reinterpret_cast<int*>(smem + S.kpos);
   int* esc_s = reinterpret_cast<int*>(smem + S.esc);
   float* q16_s = reinterpret_cast<float*>(smem + S.q16);
-  uint32_t* const stage0 = reinterpret_cast<uint32_t*>(smem + S.stage0);
-  const int stage_words = kP * L.row_words;  // stage1 follows stage0
+  unsigned char* stage0 = smem + S.stage0;
   const uint16_t* meta_s = reinterpret_cast<const uint16_t*>(smem + S.meta);
   unsigned char* apv = smem + S.apv;
   unsigned char* bqk = smem + S.bqk;
   unsigned char* bpv = smem + S.bpv;
-  float* red_b = red;            // [4 warps][8] bias partials
-  uint32_t* red_m = reinterpret_cast<uint32_t*>(red + 64);  // [4 warps][16] max keys
+  float* red_b = red;                                         // [2][4 warps][8] bias partials
+  uint32_t* red_m = reinterpret_cast<uint32_t*>(red + 64);    // [2][4 warps][16] max keys
+  float* red_w = red + 192;                                   // item-end reductions
 
   const int pg0 = s * p.pps;
   const int npg = min(pages, pg0 + p.pps) - pg0;
   const int64_t head_row = (static_cast<int64_t>(b) * H + h) * L.row_cap;
   const int64_t head_meta = (static_cast<int64_t>(b) * H + h) * L.group_cap;
-  const uint32_t row_bytes = kP * R * 4;
+  const uint32_t row_bytes = static_cast<uint32_t>(S.stage_bytes);
   const uint32_t meta_bytes = static_cast<uint32_t>(npg * M * 2);
 
-  if (tid == 0) {
+  if (tid == kDecThreads) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < kStages; ++i) mbar_init(&bars[kBarFull + i], 1);
+    mbar_init(&bars[kBarKReady], kDecThreads);
+    mbar_init(&bars[kBarVReady], kDecThreads);
+    mbar_init(&bars[kBarQK], 1);
+    mbar_init(&bars[kBarPV], 1);
     *abort_s = 0;
     fence_mbar_init();
   }
-  if (warp == 0) {
+  if (warp == 4) {
     tmem_alloc(tmem_slot, S.tm_cols);
     tmem_relinquish();
   }
-  for (int pp = tid; pp < S.kpad; pp += kDecThreads) kpos_s[pp] = kpos_entry(L, p.slot_chan, h, pp);
-  for (int q = tid; q < npg; q += kDecThreads) esc_s[q] = 0;
+  if (tid < kDecThreads) {
+    load_query_group_rt(p, b, h, q_s, kDecThreads);
+    for (int pp = tid; pp < S.kpad; pp += kDecThreads) kpos_s[pp] = kpos_entry(L, p.slot_chan, h, pp);
+    for (int q = tid; q < npg; q += kDecThreads) esc_s[q] = 0;
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
 
-  // Kick off the item's Key meta rows and the first two pages.
-  if (tid == 0) {
-    mbar_arrive_expect_tx(&bars[0], row_bytes + meta_bytes);
-    if (meta_bytes) bulk_g2s(smem + S.meta, p.kmeta + (head_meta + pg0) * M, meta_bytes, &bars[0]);
-    bulk_g2s(stage0, p.rows + (head_row + static_cast<int64_t>(pg0) * kP) * R, row_bytes, &bars[0]);
-    if (npg > 1) {
-      mbar_arrive_expect_tx(&bars[1], row_bytes);
-      bulk_g2s(stage0 + stage_words, p.rows + (head_row + static_cast<int64_t>(pg0 + 1) * kP) * R, row_bytes, &bars[1]);
+  // ------------------------------------------------------------ control warp
+  if (warp == 4) {
+    if (lane == 0) {
+      const uint64_t kLimit = kWaitLimitNs;
+      int issued[kStages] = {0, 0};
+      for (int i = 0; i < kStages && i < npg; ++i) {
+        uint64_t* full = &bars[kBarFull + i];
+        mbar_arrive_expect_tx(full, row_bytes + (i == 0 ? meta_bytes : 0u));
+        if (i == 0 && meta_bytes) bulk_g2s(smem + S.meta, p.kmeta + (head_meta + pg0) * M, meta_bytes, full);
+        bulk_g2s(stage0 + i * S.stage_bytes, p.rows + (head_row + static_cast<int64_t>(pg0 + i) * kP) * R,
+                 row_bytes, full);
+        ++issued[i];
+      }
+      // Descriptors: QK B per K step, PV A/B per K step and Value-tile parity.
+      const uint32_t n_ks = static_cast<uint32_t>(S.kpad / 32);
+      const uint64_t bqk_desc0 = smem_desc(bqk, 128, S.bqk_sbo);
+      const uint64_t apv_desc0 = smem_desc(apv, 128, 2048);
+      const uint64_t bpv_desc0 = smem_desc(bpv, 128, 2048);
+      int qk_open = 0, pv_open = 0;
+      for (int i = 0; i < npg; ++i) {
+        if (!*abort_s && !mbar_wait_bounded(&bars[kBarKReady], i & 1, kLimit)) *abort_s = 1;
+        tc_fence_after();
+        for (uint32_t ks = 0; ks < n_ks; ++ks)  // +512 B per K step = +32 in descriptor units
+          mma_u8_ts(tmem + S.tm_qk, tmem + S.a_col + 8 * ks, bqk_desc0 + 32 * ks, kIdescQK, ks > 0 ? 1u : 0u);
+        mma_commit(&bars[kBarQK]);
+        qk_open = i + 1;
+        if (!*abort_s && !mbar_wait_bounded(&bars[kBarVReady], i & 1, kLimit)) *abort_s = 1;
+        tc_fence_after();
+        const uint64_t a_tile = apv_desc0 + static_cast<uint64_t>((i & 1) * (kP * kD / 16));
+#pragma unroll
+        for (int ks = 0; ks < kP / 32; ++ks)
+          mma_u8_ss(tmem + S.tm_pv, a_tile + 32 * ks, bpv_desc0 + 32 * ks, kIdescPV, ks > 0 ? 1u : 0u);
+        mma_commit(&bars[kBarPV]);
+        pv_open = i + 1;
+        // Stage i % kStages has been read by U(i) and S(i): it takes page i + kStages.
+        if (i + kStages < npg && !*abort_s) {
+          const int st = i % kStages;
+          uint64_t* full = &bars[kBarFull + st];
+          mbar_arrive_expect_tx(full, row_bytes);
+          bulk_g2s(stage0 + st * S.stage_bytes,
+                   p.rows + (head_row + static_cast<int64_t>(pg0 + i + kStages) * kP) * R, row_bytes, full);
+          ++issued[st];
+        }
+      }
+      if (*abort_s) {
+        // Drain this CTA's copies and MMAs before its shared memory and TMEM go away.
+        for (int st = 0; st < kStages; ++st)
+          if (issued[st]) mbar_wait_bounded(&bars[kBarFull + st], (issued[st] - 1) & 1, kLimit);
+        if (qk_open) mbar_wait_bounded(&bars[kBarQK], (qk_open - 1) & 1, kLimit);
+        if (pv_open) mbar_wait_bounded(&bars[kBarPV], (pv_open - 1) & 1, kLimit);
+        if (p.status != nullptr) atomicExch(p.status, LF_ERR_DEVICE_TIMEOUT);
+      }
     }
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();  // compute warps finished (their partial is written)
+    tc_fence_after();
+    tmem_dealloc(tmem, S.tm_cols);
+    return;
   }
+
+  // ----------------------------------------------------------- compute warps
+  float mg[GQ], og[GQ], ltg[GQ], lvtg[GQ];
+#pragma unroll
+  for (int j = 0; j < GQ; ++j) {
+    mg[j] = -INFINITY;
+    og[j] = ltg[j] = lvtg[j] = 0.f;
+  }
+  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+  const uint64_t kLimit = kWaitLimitNs;
+  auto wait = [&](uint64_t* bar, uint32_t parity) {
+    if (*abort_s) return;
+    if (!mbar_wait_bounded(bar, parity, kLimit)) *abort_s = 1;
+  };
 
   // Per-q-head block exponent of the query: max_c |q_j[c]| <= 2^eq_j.
-  int eq[kGQ];
-  {
+  int eq[GQ];
 #pragma unroll
-    for (int j = 0; j < kGQ; ++j) {
-      const uint32_t a = __float_as_uint(fabsf(q_s[j * kD + tid]));
-      const uint32_t mx = __reduce_max_sync(0xffffffffu, a);
-      if (lane == 0) red_m[warp * 16 + j] = mx;
-    }
-    for (int i = tid; i < L.width[3] * kGQ; i += kDecThreads) {
-      const int ii = i / kGQ, j = i % kGQ;
-      const int ch = p.slot_chan[(3 * H + h) * kD + ii];
-      q16_s[i] = ch < 0 ? 0.f : q_s[j * kD + ch];
-    }
-    __syncthreads();
-#pragma unroll
-    for (int j = 0; j < kGQ; ++j) {
-      uint32_t mx = red_m[j];
-#pragma unroll
-      for (int w = 1; w < 4; ++w) mx = max(mx, red_m[w * 16 + j]);
-      eq[j] = exp2_ceil(__uint_as_float(mx));
-    }
+  for (int j = 0; j < GQ; ++j) {
+    const uint32_t mx = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(q_s[j * kD + tid])));
+    if (lane == 0) red_m[warp * 16 + j] = mx;
   }
-  // This thread's QK B rows: K positions tid, tid+128, tid+256.
-  float qq[3][kGQ];
-  int soff[3], moff[3];
+  for (int i = tid; i < L.width[3] * kGQ; i += kDecThreads) {
+    const int ii = i / kGQ, j = i % kGQ;
+    const int ch = p.slot_chan[(3 * H + h) * kD + ii];
+    q16_s[i] = ch < 0 ? 0.f : q_s[j * kD + ch];
+  }
+  named_sync(1, kDecThreads);
 #pragma unroll
-  for (int k = 0; k < 3; ++k) {
+  for (int j = 0; j < GQ; ++j) {
+    const uint32_t mx = max(max(red_m[j], red_m[16 + j]), max(red_m[32 + j], red_m[48 + j]));
+    eq[j] = max(-60, min(60, exp2_ceil(__uint_as_float(mx))));
+  }
+  // This thread's QK B rows: K positions tid and tid+128 (scaled query values).
+  float qq[2][GQ];
+  int soff[2], moff[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
     const int pp = tid + k * kDecThreads;
     const int e = pp < S.kpad ? kpos_s[pp] : -1;
     soff[k] = moff[k] = -1;
     if (e >= 0) {
-      const int ch = e & 0xFFFF, tier = (e >> 16) & 3, slot = e >> 18;
+      const int tier = (e >> 16) & 3, slot = e >> 18;
       soff[k] = L.scale_off[tier] + slot;
       moff[k] = L.min_off[tier] + slot;
     }
 #pragma unroll
-    for (int j = 0; j < kGQ; ++j) qq[k][j] = e >= 0 ? q_s[j * kD + (e & 0xFFFF)] * exp2i(22 - eq[j]) : 0.f;
+    for (int j = 0; j < GQ; ++j) qq[k][j] = e >= 0 ? q_s[j * kD + (e & 0xFFFF)] * exp2i(22 - eq[j]) : 0.f;
   }
   // A columns past the packed slots stay zero for the whole item.
   for (int c = n_slots_of(L) / 4; c < S.kpad / 4; ++c) tmem_st_x1(tmem + lane_base + S.a_col + c, 0u);
-
   const float c2 = p.scaling * kLog2e;
-  bool ok = true;
-  int issued[2] = {1, npg > 1 ? 1 : 0}, waited[2] = {0, 0};
-  int mma_open = 0;  // committed-but-unwaited MMA barriers: bit0 qk, bit1 pv
-  int i = 0;
-  for (; i < npg; ++i) {
-    const int st = i & 1;
-    if (!mbar_wait_bounded(&bars[st], (i >> 1) & 1, kWaitLimitNs)) { *abort_s = 1; ok = false; }
-    else ++waited[st];
-    if (i == 0) {
-      // Per-page block exponent of the Key scales, from the item's meta rows:
-      // max over this thread's slots, warp max, then one shared atomic per warp.
-      for (int q = 0; q < npg; ++q) {
-        float mx = 0.f;
+
+  // Page-0 data (with the item's meta rows) -> per-page Key-scale exponents.
+  wait(&bars[kBarFull + 0], 0);
+  for (int q = 0; q < npg; ++q) {
+    float mx = 0.f;
 #pragma unroll
-        for (int k = 0; k < 3; ++k)
-          if (soff[k] >= 0) mx = fmaxf(mx, half_bits_to_float(meta_s[q * M + soff[k]]));
-        const uint32_t wmax = __reduce_max_sync(0xffffffffu, __float_as_uint(mx));
-        if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(esc_s) + q, wmax);
-      }
-      __syncthreads();
-      for (int q = tid; q < npg; q += kDecThreads) esc_s[q] = exp2_ceil(__uint_as_float(esc_s[q]));
-      __syncthreads();
+    for (int k = 0; k < 2; ++k)
+      if (soff[k] >= 0) mx = fmaxf(mx, half_bits_to_float(meta_s[q * M + soff[k]]));
+    const uint32_t wmax = __reduce_max_sync(0xffffffffu, __float_as_uint(mx));
+    if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(esc_s) + q, wmax);
+  }
+  named_sync(1, kDecThreads);  // also: every read of the query staging (second Value tile) is done
+  for (int q = tid; q < npg; q += kDecThreads) esc_s[q] = max(-60, min(60, exp2_ceil(__uint_as_float(esc_s[q]))));
+  named_sync(1, kDecThreads);
+
+  // U(i): one pass over the token's row -- Key codes -> TMEM, Value codes ->
+  // Value tile (i & 1), QK B rows for this thread's slots, bias partials.
+  auto unpack = [&](int i) {
+    const uint32_t* rowp = reinterpret_cast<const uint32_t*>(stage0 + (i % kStages) * S.stage_bytes) + tid * R;
+    uint32_t vw[kD / 16];
+#pragma unroll
+    for (int w = 0; w < kD / 16; ++w) vw[w] = rowp[L.vcode_off + w];
+    const uint16_t* mrow = meta_s + i * M;
+    float msc[2], mmn[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      msc[k] = soff[k] >= 0 ? half_bits_to_float(mrow[soff[k]]) : 0.f;
+      mmn[k] = soff[k] >= 0 ? half_bits_to_float(mrow[moff[k]]) : 0.f;
     }
-    const uint32_t* rowp = stage0 + st * stage_words + tid * R;
-    const uint16_t* row16 = reinterpret_cast<const uint16_t*>(rowp);
-    // [A1] Key codes -> TMEM (this thread's lane), u8 per slot.
+    uint32_t col = tmem + lane_base + S.a_col;
     {
-      uint32_t col = tmem + lane_base + S.a_col;
-      for (int w = 0; w < L.words[0]; ++w, col += 4) {
-        const uint32_t x = rowp[L.code_off[0] + w];
-        tmem_st_x4(col, x & kM2, (x >> 2) & kM2, (x >> 4) & kM2, (x >> 6) & kM2);
+      const uint32_t* src = rowp + L.code_off[0];
+#pragma unroll 4
+      for (int w = 0; w < L.words[0]; ++w) {
+        const uint32_t x = src[w];
+        tmem_st_x4(col + 4 * w, x & kM2, (x >> 2) & kM2, (x >> 4) & kM2, (x >> 6) & kM2);
       }
-      for (int w = 0; w < L.words[1]; ++w, col += 2) {
-        const uint32_t x = rowp[L.code_off[1] + w];
-        tmem_st_x2(col, x & kM4, (x >> 4) & kM4);
-      }
-      for (int w = 0; w < L.words[2]; ++w, col += 1) tmem_st_x1(col, rowp[L.code_off[2] + w]);
+      col += 4 * L.words[0];
     }
-    // [A2] Value codes -> A operand of PV (MN-major: 16 channels x 8 tokens cores).
     {
-      unsigned char* dst = apv + (tid & 7) * 16 + (tid >> 3) * 128;
+      const uint32_t* src = rowp + L.code_off[1];
+#pragma unroll 4
+      for (int w = 0; w < L.words[1]; ++w) {
+        const uint32_t x = src[w];
+        tmem_st_x2(col + 2 * w, x & kM4, (x >> 4) & kM4);
+      }
+      col += 2 * L.words[1];
+    }
+    {
+      const uint32_t* src = rowp + L.code_off[2];
+#pragma unroll 4
+      for (int w = 0; w < L.words[2]; ++w) tmem_st_x1(col + w, src[w]);
+    }
+    {
+      unsigned char* dst = apv + (i & 1) * (kP * kD) + (tid & 7) * 16 + (tid >> 3) * 128;
 #pragma unroll
       for (int w = 0; w < kD / 16; ++w) {
-        const uint32_t x = rowp[L.vcode_off + w];
-        *reinterpret_cast<uint4*>(dst + w * 2048) =
-            make_uint4(x & kM2, (x >> 2) & kM2, (x >> 4) & kM2, (x >> 6) & kM2);
+        const uint32_t x = vw[w];
+        *reinterpret_cast<uint4*>(dst + w * 2048) = make_uint4(x & kM2, (x >> 2) & kM2, (x >> 4) & kM2, (x >> 6) & kM2);
       }
     }
-    // [A3] FP16 Key tier on the CUDA cores; Value scale / min of the token.
-    float s16[kGQ];
-#pragma unroll
-    for (int j = 0; j < kGQ; ++j) s16[j] = 0.f;
-    const int h0 = 2 * L.half_off;
-    for (int c = 0; c < L.width[3]; ++c) {
-      const float kv = half_bits_to_float(row16[h0 + c]);
-      const float4 a = *reinterpret_cast<const float4*>(q16_s + c * kGQ);
-      const float4 bq = *reinterpret_cast<const float4*>(q16_s + c * kGQ + 4);
-      s16[0] = fmaf(a.x, kv, s16[0]);
-      s16[1] = fmaf(a.y, kv, s16[1]);
-      s16[2] = fmaf(a.z, kv, s16[2]);
-      s16[3] = fmaf(a.w, kv, s16[3]);
-      s16[4] = fmaf(bq.x, kv, s16[4]);
-      s16[5] = fmaf(bq.y, kv, s16[5]);
-      s16[6] = fmaf(bq.z, kv, s16[6]);
-      s16[7] = fmaf(bq.w, kv, s16[7]);
-    }
-    const float vs = half_bits_to_float(row16[h0 + L.width[3]]);
-    const float vm = half_bits_to_float(row16[h0 + L.width[3] + 1]);
-    // [A4] B rows of QK for this thread's slots; bias partials sum_c q_c min_c.
     float bias[kGQ];
 #pragma unroll
     for (int j = 0; j < kGQ; ++j) bias[j] = 0.f;
-    {
-      const float fsc = exp2i(-esc_s[i]);
-      const uint16_t* mrow = meta_s + i * M;
+    const float fsc = exp2i(-esc_s[i]);
 #pragma unroll
-      for (int k = 0; k < 3; ++k) {
-        const int pp = tid + k * kDecThreads;
-        if (pp >= S.kpad) break;
-        uint4 c0 = make_uint4(0u, 0u, 0u, 0u), c1 = c0;
-        if (soff[k] >= 0) {
-          const float sc = half_bits_to_float(mrow[soff[k]]) * fsc;
-          const float mn = half_bits_to_float(mrow[moff[k]]);
-          uint32_t U[kGQ];
+    for (int k = 0; k < 2; ++k) {
+      const int pp = tid + k * kDecThreads;
+      if (pp >= S.kpad) break;
+      uint4 c0 = make_uint4(0u, 0u, 0u, 0u), c1 = c0;
+      if (soff[k] >= 0) {
+        const float sc = msc[k] * fsc;
+        uint32_t U[kGQ];
 #pragma unroll
-          for (int j = 0; j < kGQ; ++j) {
+        for (int j = 0; j < kGQ; ++j) {
+          if (j < GQ) {
             // rint(qq * sc) + 2^23 via the fp32 magic constant 1.5 * 2^23.
             U[j] = __float_as_uint(fmaf(qq[k][j], sc, 12582912.0f)) - 0x4AC00000u;
-            bias[j] = fmaf(qq[k][j], mn, bias[j]);
+            bias[j] = fmaf(qq[k][j], mmn[k], bias[j]);
+          } else {
+            U[j] = 0x800000u;  // X = 0
           }
-          pack_limbs(U, c0, c1, 1u);
         }
-        unsigned char* dst = bqk + (pp & 7) * 16 + (pp >> 3) * 128;
-        *reinterpret_cast<uint4*>(dst) = c0;
-        *reinterpret_cast<uint4*>(dst + S.bqk_sbo) = c1;
+        pack_limbs(U, c0, c1, 1u);
       }
+      unsigned char* dst = bqk + (pp & 7) * 16 + (pp >> 3) * 128;
+      *reinterpret_cast<uint4*>(dst) = c0;
+      *reinterpret_cast<uint4*>(dst + S.bqk_sbo) = c1;
     }
-    {
-      const float part = warp_sum8_scatter(bias, lane);
-      if ((lane & 3) == 0) red_b[warp * kGQ + (((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1))] = part;
-    }
+    const float part = warp_sum8_scatter(bias, lane);
+    if ((lane & 3) == 0)
+      red_b[(i & 1) * 32 + warp * kGQ + (((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1))] = part;
     tmem_wait_st();
     fence_proxy_async_smem();
     tc_fence_before();
-    __syncthreads();
-    if (*abort_s) break;
-    if (tid == 0) {
-      tc_fence_after();
-      for (int ks = 0; ks < S.kpad / 32; ++ks)
-        mma_u8_ts(tmem + S.tm_qk, tmem + S.a_col + 8 * ks, smem_desc(bqk + 512 * ks, 128, S.bqk_sbo), kIdescQK,
-                  ks > 0 ? 1u : 0u);
-      mma_commit(&bars[2]);
-      if (i + 2 < npg) {  // the stage just consumed takes page i+2
-        mbar_arrive_expect_tx(&bars[st], row_bytes);
-        bulk_g2s(stage0 + st * stage_words, p.rows + (head_row + static_cast<int64_t>(pg0 + i + 2) * kP) * R, row_bytes,
-                 &bars[st]);
-        ++issued[st];
-      }
-    }
-    mma_open |= 1;
+    mbar_arrive(&bars[kBarKReady]);
+  };
 
-    // [B] scores, page max, probabilities and the PV B rows.
-    if (!mbar_wait_bounded(&bars[2], i & 1, kWaitLimitNs)) { *abort_s = 1; ok = false; }
-    else mma_open &= ~1;
+  float alpha[GQ];
+  int ev[GQ];
+  // Iteration i runs S(i), U(i+1), C(i); iteration -1 only U(0).
+  for (int i = -1; i < npg; ++i) {
+    if (i < 0) {
+      unpack(0);
+      continue;
+    }
+    // S(i): scores, page max, online softmax, PV B rows.  The FP16 Key tier
+    // (CUDA cores) and the token's Value scale / min come from the page's
+    // stage, resident until this page's V-ready arrive.
+    const uint16_t* row16 =
+        reinterpret_cast<const uint16_t*>(stage0 + (i % kStages) * S.stage_bytes) + 2 * tid * R + 2 * L.half_off;
+    float s16[GQ];
+#pragma unroll
+    for (int j = 0; j < GQ; ++j) s16[j] = 0.f;
+#pragma unroll 4
+    for (int c = 0; c < L.width[3]; ++c) {
+      const float kv = half_bits_to_float(row16[c]);
+      const float4 qa = *reinterpret_cast<const float4*>(q16_s + c * kGQ);
+      const float4 qb = *reinterpret_cast<const float4*>(q16_s + c * kGQ + 4);
+      const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+      for (int j = 0; j < GQ; ++j) s16[j] = fmaf(qv[j], kv, s16[j]);
+    }
+    const float vs_i = half_bits_to_float(row16[L.width[3]]);
+    const float vm_i = half_bits_to_float(row16[L.width[3] + 1]);
+    const int esc = esc_s[i];
+    wait(&bars[kBarQK], i & 1);
     tc_fence_after();
     uint32_t acc[32];
-    tmem_ld_x32(tmem + lane_base + S.tm_qk, acc);
-    tmem_wait_ld();
-    float sc[kGQ];
-    {
-      const int esc = esc_s[i];
-      const int ones = static_cast<int>(acc[24]);
+    tmem_ld_x32_sync(tmem + lane_base + S.tm_qk, acc);
+    const int ones = static_cast<int>(acc[24]);
+    float x[GQ];
+    uint32_t* rm = red_m + (i & 1) * 64;
+    uint32_t keys[12];
 #pragma unroll
-      for (int j = 0; j < kGQ; ++j) {
-        const float bsum = (red_b[j] + red_b[kGQ + j]) + (red_b[2 * kGQ + j] + red_b[3 * kGQ + j]);
-        const float sint = static_cast<float>(static_cast<int>(acc[j])) +
-                           256.f * static_cast<float>(static_cast<int>(acc[8 + j])) +
-                           65536.f * static_cast<float>(static_cast<int>(acc[16 + j]) - 128 * ones);
-        const float val = sint * (c2 * exp2i(eq[j] + esc - 22)) + (bsum * exp2i(eq[j] - 22) + s16[j]) * c2;
-        sc[j] = j < GQ ? val : -INFINITY;
-        const uint32_t key = __reduce_max_sync(0xffffffffu, order_key(sc[j]));
-        if (lane == 0) red_m[warp * 16 + j] = key;
-      }
-      const uint32_t vkey = __reduce_max_sync(0xffffffffu, __float_as_uint(vs));
-      if (lane == 0) red_m[warp * 16 + 8] = vkey;
+    for (int j = 0; j < 12; ++j) keys[j] = 0u;
+#pragma unroll
+    for (int j = 0; j < GQ; ++j) {
+      const int lo = static_cast<int>(acc[j]) + (static_cast<int>(acc[8 + j]) << 8);
+      const float sint = fmaf(static_cast<float>(static_cast<int>(acc[16 + j]) - 128 * ones), 65536.f,
+                              static_cast<float>(lo));
+      x[j] = fmaf(sint, c2 * exp2i(eq[j] + esc - 22), s16[j] * c2);
+      keys[j] = order_key(x[j]);
     }
-    __syncthreads();
-    float alpha[kGQ];
-    int ev[kGQ];
-    {
-      uint32_t vk = red_m[8];
+    keys[8] = __float_as_uint(vs_i);
 #pragma unroll
-      for (int w = 1; w < 4; ++w) vk = max(vk, red_m[w * 16 + 8]);
-      const float vsmax = __uint_as_float(vk);
-      uint32_t U[kGQ];
+    for (int j = 0; j < GQ; ++j) keys[j] = __reduce_max_sync(0xffffffffu, keys[j]);
+    keys[8] = __reduce_max_sync(0xffffffffu, keys[8]);
+    if (lane == 0) {
+      *reinterpret_cast<uint4*>(rm + warp * 16) = make_uint4(keys[0], keys[1], keys[2], keys[3]);
+      *reinterpret_cast<uint4*>(rm + warp * 16 + 4) = make_uint4(keys[4], keys[5], keys[6], keys[7]);
+      *reinterpret_cast<uint4*>(rm + warp * 16 + 8) = make_uint4(keys[8], 0u, 0u, 0u);
+    }
+    named_sync(1, kDecThreads);
+    uint32_t U[kGQ];
+    {
+      uint32_t km[12];
+      float bs[8];
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const uint4 k0 = *reinterpret_cast<const uint4*>(rm + w * 16);
+        const uint4 k1 = *reinterpret_cast<const uint4*>(rm + w * 16 + 4);
+        const uint4 k2 = *reinterpret_cast<const uint4*>(rm + w * 16 + 8);
+        const float4 b0 = *reinterpret_cast<const float4*>(red_b + (i & 1) * 32 + w * 8);
+        const float4 b1 = *reinterpret_cast<const float4*>(red_b + (i & 1) * 32 + w * 8 + 4);
+        const uint32_t kk[12] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w, k2.x, k2.y, k2.z, k2.w};
+        const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+        for (int e = 0; e < 9; ++e) km[e] = w == 0 ? kk[e] : max(km[e], kk[e]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) bs[e] = w == 0 ? bb[e] : bs[e] + bb[e];
+      }
+      const int ev_vs = max(-60, min(60, exp2_ceil(__uint_as_float(km[8]))));
 #pragma unroll
       for (int j = 0; j < kGQ; ++j) {
-        uint32_t key = red_m[j];
-#pragma unroll
-        for (int w = 1; w < 4; ++w) key = max(key, red_m[w * 16 + j]);
-        const float pm = order_key_to_float(key);
-        float pj = 0.f;
         if (j < GQ) {
-          const float mnew = fmaxf(m[j], pm);
-          alpha[j] = m[j] == -INFINITY ? 0.f : ex2(m[j] - mnew);
-          m[j] = mnew;
-          pj = ex2(sc[j] - mnew);
-          ev[j] = exp2_ceil(ex2(pm - mnew) * vsmax);
+          const float bias = bs[j] * (c2 * exp2i(eq[j] - 22));
+          const float pm = order_key_to_float(km[j]) + bias;
+          const float mnew = fmaxf(mg[j], pm);
+          alpha[j] = mg[j] == -INFINITY ? 0.f : ex2(mg[j] - mnew);
+          mg[j] = mnew;
+          const float pj = ex2(x[j] + bias - mnew);
+          // Bound on p * vscale over the page: 2^(pm - mnew) * max vscale.
+          ev[j] = ev_vs + max(-60, static_cast<int>(ceilf(pm - mnew)));
+          ltg[j] = fmaf(ltg[j], alpha[j], pj);
+          lvtg[j] = fmaf(lvtg[j], alpha[j], pj * vm_i);
+          // rint(p * vs * 2^(23 - ev)) via the fp32 magic constant 2^23.
+          U[j] = __float_as_uint(fmaf(pj, vs_i * exp2i(23 - ev[j]), 8388608.0f)) - 0x4B000000u;
         } else {
-          alpha[j] = 1.f;
-          ev[j] = 0;
+          U[j] = 0u;
         }
-        lt[j] = fmaf(lt[j], alpha[j], pj);
-        lvt[j] = fmaf(lvt[j], alpha[j], pj * vm);
-        // rint(p * vs * 2^(23 - ev)) via the fp32 magic constant 2^23.
-        U[j] = __float_as_uint(fmaf(pj, vs * exp2i(23 - ev[j]), 8388608.0f)) - 0x4B000000u;
       }
+    }
+    {
       uint4 c0, c1;
       pack_limbs(U, c0, c1, 0u);
       unsigned char* dst = bpv + (tid & 7) * 16 + (tid >> 3) * 128;
@@ -488,56 +574,31 @@ __global__ void __launch_bounds__(kDecThreads, 3) decode_partial_tc(DecodeParams
     }
     fence_proxy_async_smem();
     tc_fence_before();
-    __syncthreads();
-    if (*abort_s) break;
-    if (tid == 0) {
-      tc_fence_after();
-#pragma unroll
-      for (int ks = 0; ks < kP / 32; ++ks)
-        mma_u8_ss(tmem + S.tm_pv, smem_desc(apv + 512 * ks, 128, 2048), smem_desc(bpv + 512 * ks, 128, 2048),
-                  kIdescPV, ks > 0 ? 1u : 0u);
-      mma_commit(&bars[3]);
+    mbar_arrive(&bars[kBarVReady]);
+    // U(i+1) while PV(i) runs.
+    if (i + 1 < npg) {
+      wait(&bars[kBarFull + (i + 1) % kStages], ((i + 1) / kStages) & 1);
+      unpack(i + 1);
     }
-    mma_open |= 2;
-    // [C] accumulate this thread's head-dim position.
-    if (!mbar_wait_bounded(&bars[3], i & 1, kWaitLimitNs)) { *abort_s = 1; ok = false; }
-    else mma_open &= ~2;
+    // C(i): accumulate this thread's head-dim position.
+    wait(&bars[kBarPV], i & 1);
     tc_fence_after();
-    tmem_ld_x32(tmem + lane_base + S.tm_pv, acc);
-    tmem_wait_ld();
+    tmem_ld_x32_sync(tmem + lane_base + S.tm_pv, acc);
 #pragma unroll
-    for (int j = 0; j < kGQ; ++j) {
-      const float v = static_cast<float>(static_cast<int>(acc[j])) +
-                      256.f * static_cast<float>(static_cast<int>(acc[8 + j])) +
-                      65536.f * static_cast<float>(static_cast<int>(acc[16 + j]));
-      o[j] = fmaf(o[j], alpha[j], v * exp2i(ev[j] - 23));
+    for (int j = 0; j < GQ; ++j) {
+      const int lo = static_cast<int>(acc[j]) + (static_cast<int>(acc[8 + j]) << 8);
+      const float v = fmaf(static_cast<float>(static_cast<int>(acc[16 + j])), 65536.f, static_cast<float>(lo));
+      og[j] = fmaf(og[j], alpha[j], v * exp2i(ev[j] - 23));
     }
   }
 
-  tc_fence_before();
-  __syncthreads();
-  if (*abort_s) {
-    // Drain this CTA's own copies and MMAs (bounded), record the failure.
-    if (tid == 0) {
-      for (int st = 0; st < 2; ++st)
-        while (waited[st] < issued[st]) {
-          mbar_wait_bounded(&bars[st], waited[st] & 1, kWaitLimitNs);
-          ++waited[st];
-        }
-      if (p.status != nullptr) atomicExch(p.status, LF_ERR_DEVICE_TIMEOUT);
-    }
-    if (mma_open & 1) mbar_wait_bounded(&bars[2], i & 1, kWaitLimitNs);
-    if (mma_open & 2) mbar_wait_bounded(&bars[3], i & 1, kWaitLimitNs);
-    __syncthreads();
-  }
-  tc_fence_after();
-  if (warp == 0) tmem_dealloc(tmem, S.tm_cols);
-  (void)ok;
 #pragma unroll
-  for (int j = 0; j < kGQ; ++j) m[j] *= kLn2;  // log2 units -> natural-log units
+  for (int j = 0; j < GQ; ++j) mg[j] *= kLn2;  // log2 units -> natural-log units
   // PV row t holds head-dim channel d(t): t = 16w + 4k + i  <->  d = 16w + k + 4i.
   const int d = (tid & ~15) + ((tid & 15) >> 2) + 4 * (tid & 3);
-  write_partial(p, b, h, s, d, o, m, lt, lvt, red + 128);
+  write_partial_group<GQ>(p, b, h, s, d, og, mg, ltg, lvtg, red_w, 1);
+  tc_fence_before();
+  __syncthreads();
 }
 
 }  // namespace tc
@@ -545,36 +606,38 @@ __global__ void __launch_bounds__(kDecThreads, 3) decode_partial_tc(DecodeParams
 bool tc_supported(const lf_layout& L, int gq, int pps) {
   if (L.head_dim != tc::kD || L.page_size != tc::kP || L.k_group != tc::kP || L.v_group != tc::kD) return false;
   if (L.bit_v != 2 || gq > kGQ || gq < 1) return false;
-  if (tc::n_slots_of(L) > 384) return false;
-  return tc::tc_smem(L, pps).total <= 227 * 1024;
+  if (tc::n_slots_of(L) > 2 * kDecThreads) return false;  // two K positions per compute thread
+  if (pps > tc::kMaxPagesPerItem) return false;
+  const tc::TcSmem S = tc::tc_smem(L, pps);
+  // The residual split's fp32 rows must end before the query staging.
+  if (S.stage0 + resid_smem(tc::kD).total > S.qs) return false;
+  return S.total <= 227 * 1024;
 }
 
-template <typename RT, typename QT>
-static int launch_tc_typed(const DecodeParams& p, cudaStream_t stream) {
-  const tc::TcSmem S = tc::tc_smem(p.L, p.pps);
-  auto kern = tc::decode_partial_tc<RT, QT>;
-  static std::atomic<int> configured{48 * 1024};
-  if (S.total > configured.load()) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S.total);
-    if (e != cudaSuccess) {
-      set_error("lf_decode_partial (tcgen05): shared memory %d B: %s", S.total, cudaGetErrorString(e));
-      return LF_ERR_UNSUPPORTED;
-    }
-    configured.store(S.total);
+template <int GQ>
+static void* tc_kernel_ptr() {
+  return reinterpret_cast<void*>(tc::decode_partial_tc<GQ>);
+}
+static void* tc_kernel_for(int gq) {
+  switch (gq) {
+    case 1: return tc_kernel_ptr<1>();
+    case 2: return tc_kernel_ptr<2>();
+    case 3: return tc_kernel_ptr<3>();
+    case 4: return tc_kernel_ptr<4>();
+    case 5: return tc_kernel_ptr<5>();
+    case 6: return tc_kernel_ptr<6>();
+    case 7: return tc_kernel_ptr<7>();
+    default: return tc_kernel_ptr<8>();
   }
-  dim3 grid(p.max_splits, p.L.kv_heads, p.batch);
-  kern<<<grid, kDecThreads, S.total, stream>>>(p);
-  return launch_status("lf_decode_partial (tcgen05)");
 }
 
-int occupancy_tc(const lf_layout& L, int pps) {
+int occupancy_tc(const lf_layout& L, int gq, int pps) {
   const tc::TcSmem S = tc::tc_smem(L, pps);
   if (S.total > 227 * 1024) return 0;
-  cudaFuncSetAttribute(tc::decode_partial_tc<__nv_bfloat16, __nv_bfloat16>,
-                       cudaFuncAttributeMaxDynamicSharedMemorySize, S.total);
+  void* kern = tc_kernel_for(gq);
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S.total);
   int blocks = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, tc::decode_partial_tc<__nv_bfloat16, __nv_bfloat16>,
-                                                    kDecThreads, S.total) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kern, tc::kThreads, S.total) != cudaSuccess) {
     cudaGetLastError();
     return -1;
   }
@@ -583,21 +646,28 @@ int occupancy_tc(const lf_layout& L, int pps) {
 }
 
 int launch_partial_tc(const DecodeParams& p, int resid_dtype, int q_dtype, cudaStream_t stream) {
-#define LF_TC_Q(RT)                                                        \
-  switch (q_dtype) {                                                       \
-    case LF_F32: return launch_tc_typed<RT, float>(p, stream);             \
-    case LF_F16: return launch_tc_typed<RT, __half>(p, stream);            \
-    case LF_BF16: return launch_tc_typed<RT, __nv_bfloat16>(p, stream);    \
-  }                                                                        \
-  break;
-  switch (resid_dtype) {
-    case LF_F32: LF_TC_Q(float)
-    case LF_F16: LF_TC_Q(__half)
-    case LF_BF16: LF_TC_Q(__nv_bfloat16)
+  DecodeParams q = p;
+  q.resid_dtype = resid_dtype;
+  q.q_dtype = q_dtype;
+  const tc::TcSmem S = tc::tc_smem(q.L, q.pps);
+  void* kern = tc_kernel_for(q.gq);
+  static std::atomic<int> configured[kGQ + 1];
+  if (S.total > 48 * 1024 && S.total > configured[q.gq].load()) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S.total);
+    if (e != cudaSuccess) {
+      set_error("lf_decode_partial (tcgen05): shared memory %d B: %s", S.total, cudaGetErrorString(e));
+      return LF_ERR_UNSUPPORTED;
+    }
+    configured[q.gq].store(S.total);
   }
-#undef LF_TC_Q
-  set_error("lf_decode_partial: dtype residual %d / query %d", resid_dtype, q_dtype);
-  return LF_ERR_INVALID_ARGUMENT;
+  dim3 grid(q.max_splits, q.L.kv_heads, q.batch);
+  void* args[] = {&q};
+  cudaError_t e = cudaLaunchKernel(kern, grid, dim3(tc::kThreads), args, S.total, stream);
+  if (e != cudaSuccess) {
+    set_error("lf_decode_partial (tcgen05): %s", cudaGetErrorString(e));
+    return LF_ERR_LAUNCH;
+  }
+  return launch_status("lf_decode_partial (tcgen05)");
 }
 
 }  // namespace lf

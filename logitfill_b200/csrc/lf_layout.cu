@@ -83,7 +83,10 @@ extern "C" int lf_layout_init(lf_layout* out, int kv_heads, int head_dim, int pa
   L.half_off = off;
   const int halves = L.width[3] + 2 * (head_dim / v_group);
   off += (halves + 1) / 2;
-  L.row_words = round_up(off, 4);
+  // Odd row length: the 32 rows a warp reads at one word offset fall in 32
+  // different shared-memory banks.  A page block (page_size rows) stays a
+  // multiple of 16 bytes for the 1-D bulk copies.
+  L.row_words = off | 1;
   int hoff = 0;
   for (int t = 0; t < 3; ++t) {
     L.scale_off[t] = hoff;

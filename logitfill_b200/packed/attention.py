@@ -14,6 +14,9 @@ import torch
 from logitfill_b200 import _lib
 from logitfill_b200.packed.cache import PackedKVCache, PackedKVManager
 
+MAX_PAGES_PER_SPLIT = 16  # the tensor-core kernel stages one item's Key meta rows in shared memory
+
+
 def pages_per_split(cache: PackedKVCache, layer_idx: int = 0) -> int:
     """Pages per K2 work item.  Every (sequence, KV head) history is cut into
     ceil(pages / pps) items, plus up to ceil(page/32) residual items; the
@@ -29,7 +32,7 @@ def pages_per_split(cache: PackedKVCache, layer_idx: int = 0) -> int:
     pairs = cache.batch * cache.n_kv
     resid = sum(-(-(int(t) + 1) // 32) for t in layer.tail_len) * cache.n_kv
     best, best_cost = 1, None
-    for pps in range(1, pages + 1):
+    for pps in range(1, min(pages, MAX_PAGES_PER_SPLIT) + 1):
         occ = so.lf_decode_occupancy(ctypes.byref(layer.layout.c), cache.n_q, pps)
         if occ <= 0:
             continue
