@@ -166,6 +166,30 @@ LF_API int lf_decode_merge(const float* workspace, const int32_t* hist_tokens, i
                     void* out, int out_dtype, int64_t out_seq_stride, int64_t out_head_stride,
                     lf_stream_t stream);
 
+/*
+ * K2 + K3 without a caller workspace, for callers that cannot allocate
+ * device memory (allocator callbacks, runtimes that plan every allocation up
+ * front, hosts that link only this library).  No counterpart in the
+ * reference: its decode op allocates its output on every call.
+ * Same inputs as lf_decode_partial, same output as lf_decode_merge; the split
+ * partials live in a fixed 8 MiB __device__ array inside the library, held
+ * on every GPU that loads it.  Rejects (LF_ERR_INVALID_ARGUMENT) a call whose
+ * partials, lf_decode_workspace_bytes(batch, H, n_q, D, max_splits), exceed
+ * 8 MiB.  Allocates nothing.  The first call on a device looks up the array's
+ * address (cudaGetSymbolAddress); make it before any stream capture.  Calls
+ * share the array: calls that overlap on the GPU race and must be ordered by
+ * the caller.
+ */
+LF_API int lf_decode_noalloc(const lf_layout* layout, const int32_t* rows, const uint16_t* kmeta,
+                             const int32_t* slot_chan, const int32_t* hist_tokens, const void* tail_k,
+                             const void* tail_v, int64_t tail_seq_stride, int64_t tail_head_stride,
+                             const int32_t* tail_len, int resid_dtype, const void* k_new, const void* v_new,
+                             int64_t new_seq_stride, int64_t new_head_stride, const void* q, int q_dtype,
+                             int64_t q_seq_stride, int64_t q_head_stride, int batch, int n_q, float scaling,
+                             int pages_per_split, int max_splits, void* out, int out_dtype,
+                             int64_t out_seq_stride, int64_t out_head_stride, int32_t* status,
+                             lf_stream_t stream);
+
 /* Human-readable text of a status code; detail of the last failure on this thread. */
 LF_API const char* lf_status_string(int status);
 LF_API const char* lf_last_error(void);
