@@ -8,8 +8,8 @@ INT8 tensor cores (``tcgen05.mma.kind::i8``):
   power-of-two block exponent, offset by 2^23 so the three limbs (bytes) are
   unsigned.  A column of ones in the B operand returns sum_c code_c, which
   removes the offset exactly in int32: ``acc0 + 256 acc1 + 65536 (acc2 - 128 ones)``.
-* PV: integer Value codes (u8, 0..3) times ``p_t * vscale_t`` written as 16-bit
-  unsigned fixed point relative to a per-page exponent.
+* PV: integer Value codes (u8, 0..3) times ``p_t * vscale_t`` written as 23-bit
+  unsigned fixed point (three limbs) relative to a per-page exponent.
 
 This model reproduces that arithmetic (integer parts exactly, float parts in
 fp32) so the scheme's error against the oracle can be measured on the CPU;
@@ -29,7 +29,7 @@ def _exp2_ceil(x: np.ndarray) -> np.ndarray:
 
 
 def model_attention(layer: orc.OracleLayer, query: np.ndarray, key_new, value_new, scaling: float,
-                    qk_bits: int = 22, pv_bits: int = 16) -> np.ndarray:
+                    qk_bits: int = 22, pv_bits: int = 23) -> np.ndarray:
     """Decode attention of ``query`` ``[n_q, D]`` over ``layer`` (page size 128,
     k_group 128, v_group D) computed with the kernel's fixed-point scheme for
     the packed history and fp32 for the residual.  Returns ``[n_q, D]``."""
