@@ -68,6 +68,7 @@ typedef struct lf_layout {
   int32_t meta_halves;  /* fp16 per Key-group meta row, multiple of 8            */
   int32_t scale_off[3]; /* fp16 offset of each tier's scales in a meta row       */
   int32_t min_off[3];   /* fp16 offset of each tier's mins in a meta row         */
+  int32_t kmax_off;     /* fp16 offset of the group's largest INT2/4/8 Key scale */
   int64_t row_cap;      /* rows reserved per (sequence, head), multiple of page  */
   int64_t group_cap;    /* meta rows reserved per (sequence, head)               */
 } lf_layout;

@@ -28,7 +28,7 @@ class LfLayout(ctypes.Structure):
         ("v_group", c_int32), ("bit_v", c_int32), ("width", c_int32 * 4), ("words", c_int32 * 3),
         ("code_off", c_int32 * 3), ("vcode_off", c_int32), ("vcode_words", c_int32),
         ("half_off", c_int32), ("row_words", c_int32), ("meta_halves", c_int32),
-        ("scale_off", c_int32 * 3), ("min_off", c_int32 * 3), ("row_cap", c_int64),
+        ("scale_off", c_int32 * 3), ("min_off", c_int32 * 3), ("kmax_off", c_int32), ("row_cap", c_int64),
         ("group_cap", c_int64),
     ]
 

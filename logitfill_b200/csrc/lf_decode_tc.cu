@@ -3,28 +3,34 @@
 // Geometry: head_dim 128, page 128 = Key group 128, Value group 128, bit_v 2
 // (the LogitFill defaults, deepseek_qwen.py:24-46).  One CTA per (split, KV
 // head, sequence) work item: four compute warps (thread t owns token t of the
-// current page, TMEM lane t and head-dim position t of the PV result) and one
-// control warp that issues the 1-D bulk copies of the page row blocks and the
-// tensor-core MMAs.
+// current page, TMEM lane t and row t of the PV result) and one control warp.
 //
-// Per page (128 tokens) of packed history, with X = 24-bit fixed point:
-//   U_K  Key codes -> u8 in TMEM (A of QK, K-major); the B row of QK for the
-//        thread's tier slots: X(q_j[c] * scale_c) + 2^23 as three unsigned
-//        limbs plus a column of ones; FP16-tier partial scores (CUDA cores).
-//   QK   5 x M128 N32 K32:  acc0 + 256 acc1 + 65536 (acc2 - 128 ones)
-//        = sum_c code_tc X_jc, exact in int32.
-//   S    scores (+ sum_c q_j[c] min_c + FP16 part), page max per q-head over
-//        the four compute warps, online-softmax update, B row of PV for token
-//        t: 23-bit X(p_tj * vscale_t), three limbs.
-//   U_V  Value codes -> u8 in shared memory (A of PV, MN-major).
-//   PV   4 x M128 N32 K32;  C: o_j = o_j alpha_j + 2^Ev_j (acc0 + 256 acc1 + 65536 acc2).
-// Compute warps run S(i), U_K(i+1), C(i), U_V(i+1): PV(i) overlaps U_K(i+1)
-// and QK(i+1) overlaps C(i) and U_V(i+1).  The Value-min term sum_t p_tj
-// vmin_t and the normaliser are per-thread partial sums reduced per item.
+// Control warp: lane 0 issues the 1-D bulk copies (a page's row block and
+// meta row per stage) and the MMAs, nothing else: a proxy fence in the thread
+// that issued a bulk copy waits for that copy, so the copy issuer never
+// writes MMA operands.
+// Compute warps, per page i:
+//   U_K  Key codes -> u8 in TMEM (A of QK, K-major); the B rows of QK for K
+//        positions t and t + 128 (tier slot c): for each q-head j the 24-bit fixed point
+//        X = rint(q_j[c] scale_c 2^(22-Eq-Es)), offset by 2^23 and split into
+//        three unsigned limbs, plus a one in the ones column; Es is the page's
+//        Key-scale exponent, from the largest scale the packer stores in the
+//        meta row; partial sums of the Key-min bias sum_c q_j[c] min_c.
+//   S    score_tj = 2^(Eq+Es-22) (acc0 + 256 acc1 + 65536 (acc2 - 128 ones))
+//        + FP16-tier part + bias_j; page max per q-head; online softmax with
+//        the per-q-head statistics held by lane j of every warp; the B row of
+//        PV for token t: rint(p_tj vscale_t 2^(23-Ev)) in three limbs, Ev the
+//        page's Value-scale exponent (p <= 1 after the max update).
+//   C    o_j += 2^(Ev-23) 4^-k(t) (acc0 + 256 acc1 + 65536 acc2).
+//   U_V  Value codes -> u8 in shared memory (A of PV, MN-major), each 2-bit
+//        code masked in place, so row t holds code * 4^k(t), k(t) = (t>>2)&3;
+//        C removes the power of two exactly.
+// Order: S(i), U_K(i+1), C(i), U_V(i+1).  QK(i+1) overlaps C(i) and U_V(i+1),
+// PV(i) overlaps U_K(i+1).
 //
 // The integer products are exact; the fixed-point rounding is 2^-22 (QK) and
-// 2^-23 (PV) of the per-page block maximum (tests/kernel_model.py models it).
-// Every mbarrier wait is bounded (2 s).  On expiry the CTA records
+// 2^-23 (PV) of the block maxima (tests/kernel_model.py models it).  Every
+// mbarrier wait is bounded (2 s).  On expiry the CTA records
 // LF_ERR_DEVICE_TIMEOUT, stops waiting (every warp still passes the same
 // barriers, so nothing deadlocks), drains its own copies and MMAs, frees its
 // TMEM and returns.
@@ -48,45 +54,52 @@ constexpr uint32_t kM2 = 0x03030303u, kM4 = 0x0F0F0F0Fu;
 
 constexpr int kStages = 2;
 constexpr int kThreads = kDecThreads + 32;  // 4 compute warps + 1 control warp
-constexpr int kMaxPagesPerItem = 16;        // bounds the per-item meta buffer
+constexpr int kMaxPagesPerItem = 64;
 
 struct TcSmem {
-  int bars, red, kpos, esc, q16, stage0, meta, apv, qs, bqk, bpv, total;
-  int kpad, a_col, tm_qk, tm_pv, tm_cols, bqk_sbo, stage_bytes;
+  int bars, red, redb, redw, q16, qhi, posoff, stage0, bqk, bpv, apv, qs, total;
+  int kpad, a_cols, tm_qk, tm_pv, tm_cols, bqk_sbo, rows_bytes, meta_bytes, stage_bytes;
 };
 
 __host__ __device__ inline int n_slots_of(const lf_layout& L) {
   return 16 * L.words[0] + 8 * L.words[1] + 4 * L.words[2];
 }
 
-__host__ __device__ inline TcSmem tc_smem(const lf_layout& L, int pps) {
+__host__ __device__ inline TcSmem tc_smem(const lf_layout& L) {
   TcSmem s;
   const int ns = n_slots_of(L);
   s.kpad = ns == 0 ? 32 : (ns + 31) / 32 * 32;
-  s.a_col = 0;
-  const int a_cols = s.kpad / 4;
-  s.tm_qk = (a_cols + 31) / 32 * 32;
+  s.a_cols = s.kpad / 4;
+  s.tm_qk = (s.a_cols + 31) / 32 * 32;
   s.tm_pv = s.tm_qk + 32;
   int need = s.tm_pv + 32, cols = 32;
   while (cols < need) cols *= 2;
   s.tm_cols = cols;
   s.bqk_sbo = s.kpad * 16;
-  s.stage_bytes = kP * L.row_words * 4;
+  s.rows_bytes = kP * L.row_words * 4;
+  s.meta_bytes = L.meta_halves * 2;
+  s.stage_bytes = (s.rows_bytes + s.meta_bytes + 127) / 128 * 128;
   int off = 0;
   s.bars = off; off += 128;
-  s.red = off; off += 320 * 4;
-  s.kpos = off; off += s.kpad * 4;
-  s.esc = off; off += ((pps + 3) / 4 * 4) * 4;
-  s.q16 = off; off += (L.width[3] > 0 ? L.width[3] : 1) * kGQ * 4;
+  s.red = off; off += 2 * 4 * 16 * 4;   // page maxima [stage][warp][16]
+  s.redb = off; off += 2 * 4 * kGQ * 4;  // bias partials [stage][warp][8]
+  s.redw = off; off += 4 * kGQ * 4;     // item-end sums
+  s.q16 = off; off += ((L.width[3] > 0 ? L.width[3] : 1) * kGQ * 4 + 15) / 16 * 16;
+  const int hi = s.kpad > kDecThreads ? s.kpad - kDecThreads : 0;  // second K positions (t + 128)
+  s.qhi = off; off += hi * kGQ * 4;
+  s.posoff = off; off += hi * 4;
   off = (off + 127) / 128 * 128;
   s.stage0 = off; off += kStages * s.stage_bytes;
-  s.meta = off; off += (pps * L.meta_halves * 2 + 15) / 16 * 16;
-  off = (off + 1023) / 1024 * 1024;
-  s.apv = off; off += 2 * kP * kD;   // two Value tiles (page parity)
-  s.qs = s.apv + kP * kD;           // the query group aliases the second tile in the prologue
   s.bqk = off; off += s.kpad * 32;
   s.bpv = off; off += kP * 32;
-  s.total = (off + 1023) / 1024 * 1024;
+  s.apv = off; off += kP * kD;
+  // The query staging (prologue only) takes the end of the Value tile, or
+  // more room after it when the residual split's rows reach further.
+  const int resid_end = s.stage0 + resid_smem(kD).total;
+  s.qs = (s.apv + kP * kD - kGQ * kD * 4);
+  if (s.qs < resid_end) s.qs = (resid_end + 15) / 16 * 16;
+  if (s.qs + kGQ * kD * 4 > off) off = s.qs + kGQ * kD * 4;
+  s.total = (off + 127) / 128 * 128;
   return s;
 }
 
@@ -183,11 +196,39 @@ __device__ __forceinline__ float exp2i(int e) { return __int_as_float((e + 127) 
 // Barrier slots in shared memory.
 enum { kBarFull = 0, kBarKReady = kStages, kBarVReady, kBarQK, kBarPV, kNumBars };
 
+// One B row of QK (K position pp; qv = q_j[c] 2^(22-Eq), zero for a padding
+// position, whose A codes are zero) and its Key-min bias terms.
 template <int GQ>
-__global__ void __launch_bounds__(kThreads, 3) decode_partial_tc(DecodeParams p) {
+__device__ __forceinline__ void qk_b_row(unsigned char* bqk, int sbo, int pp, const float (&qv)[kGQ], float sc,
+                                         float mn, float (&bias)[kGQ]) {
+  uint32_t U[kGQ];
+#pragma unroll
+  for (int j = 0; j < kGQ; ++j) {
+    if (j < GQ) {
+      // rint(qq * sc) + 2^23 via the fp32 magic constant 1.5 * 2^23.
+      U[j] = __float_as_uint(fmaf(qv[j], sc, 12582912.0f)) - 0x4AC00000u;
+      bias[j] = fmaf(qv[j], mn, bias[j]);
+    } else {
+      U[j] = 0x800000u;  // X = 0
+    }
+  }
+  uint4 c0, c1;
+  pack_limbs(U, c0, c1, 1u);
+  unsigned char* dst = bqk + (pp & 7) * 16 + (pp >> 3) * 128;
+  *reinterpret_cast<uint4*>(dst) = c0;
+  *reinterpret_cast<uint4*>(dst + sbo) = c1;
+}
+
+// The page's Key-scale exponent: largest stored INT2/INT4/INT8 scale <= 2^Es.
+__device__ __forceinline__ int page_scale_exp(const uint16_t* meta, int kmax_off) {
+  return max(-60, min(60, exp2_ceil(half_bits_to_float(meta[kmax_off]))));
+}
+
+template <int GQ>
+__global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p) {
   extern __shared__ __align__(1024) unsigned char smem[];
   const lf_layout& L = p.L;
-  const TcSmem S = tc_smem(L, p.pps);
+  const TcSmem S = tc_smem(L);
   const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
   const int H = L.kv_heads, R = L.row_words, M = L.meta_halves;
@@ -196,8 +237,7 @@ __global__ void __launch_bounds__(kThreads, 3) decode_partial_tc(DecodeParams p)
   if (s >= n_page_splits + residual_splits(kP)) return;
 
   float* q_s = reinterpret_cast<float*>(smem + S.qs);
-  float* red = reinterpret_cast<float*>(smem + S.red);
-
+  float* red_w = reinterpret_cast<float*>(smem + S.redw);
   if (s >= n_page_splits) {  // residual splits: tail rows + new token, fp32 (compute warps)
     if (warp >= 4) return;
     float m[kGQ], o[kGQ], lt[kGQ], lvt[kGQ];
@@ -208,33 +248,40 @@ __global__ void __launch_bounds__(kThreads, 3) decode_partial_tc(DecodeParams p)
     }
     load_query_group_rt(p, b, h, q_s, kDecThreads);
     const int c = s - n_page_splits;
-    unsigned char* region = smem + S.stage0;
-    residual_chunk(p, b, h, c, q_s, region, m, o, lt);
-    write_partial_group<kGQ>(p, b, h, s, tid, o, m, lt, lvt, red, 1);
+    residual_chunk(p, b, h, c, q_s, smem + S.stage0, m, o, lt);
+    write_partial_group<kGQ>(p, b, h, s, tid, o, m, lt, lvt, red_w, 1);
     return;
   }
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S.bars);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S.bars + 8 * kNumBars);
   volatile int* abort_s = reinterpret_cast<volatile int*>(smem + S.bars + 8 * kNumBars + 4);
-  int* kpos_s = reinterpret_cast<int*>(smem + S.kpos);
-  int* esc_s = reinterpret_cast<int*>(smem + S.esc);
-  float* q16_s = reinterpret_cast<float*>(smem + S.q16);
+  uint32_t* red_m = reinterpret_cast<uint32_t*>(smem + S.red);  // [stage][warp][16]: 8 score keys, vscale
+  float* red_b = reinterpret_cast<float*>(smem + S.redb);        // [stage][warp][8] bias partials
+  float* q16_s = reinterpret_cast<float*>(smem + S.q16);         // [FP16 slot][kGQ], times scaling*log2(e)
+  float* qhi_s = reinterpret_cast<float*>(smem + S.qhi);         // K positions t + 128: q_j[c] 2^(22-Eq)
+  int* posoff_s = reinterpret_cast<int*>(smem + S.posoff);       // K positions t + 128: scale | min << 16, or -1
   unsigned char* stage0 = smem + S.stage0;
-  const uint16_t* meta_s = reinterpret_cast<const uint16_t*>(smem + S.meta);
-  unsigned char* apv = smem + S.apv;
   unsigned char* bqk = smem + S.bqk;
   unsigned char* bpv = smem + S.bpv;
-  float* red_b = red;                                         // [2][4 warps][8] bias partials
-  uint32_t* red_m = reinterpret_cast<uint32_t*>(red + 64);    // [2][4 warps][16] max keys
-  float* red_w = red + 192;                                   // item-end reductions
+  unsigned char* apv = smem + S.apv;
 
   const int pg0 = s * p.pps;
   const int npg = min(pages, pg0 + p.pps) - pg0;
   const int64_t head_row = (static_cast<int64_t>(b) * H + h) * L.row_cap;
   const int64_t head_meta = (static_cast<int64_t>(b) * H + h) * L.group_cap;
-  const uint32_t row_bytes = static_cast<uint32_t>(S.stage_bytes);
-  const uint32_t meta_bytes = static_cast<uint32_t>(npg * M * 2);
+  const float c2 = p.scaling * kLog2e;
+  const int kmax_off = L.kmax_off;
+  const bool has_hi = tid < S.kpad - kDecThreads;  // compute thread with a second K position (warp-uniform)
+
+  // Page pg of the item -> stage pg % 2 (row block + meta row); one thread.
+  auto issue_page = [&](int pg) {
+    unsigned char* dst = stage0 + (pg & 1) * S.stage_bytes;
+    uint64_t* full = &bars[kBarFull + (pg & 1)];
+    mbar_arrive_expect_tx(full, static_cast<uint32_t>(S.rows_bytes + S.meta_bytes));
+    bulk_g2s(dst, p.rows + (head_row + static_cast<int64_t>(pg0 + pg) * kP) * R, S.rows_bytes, full);
+    bulk_g2s(dst + S.rows_bytes, p.kmeta + (head_meta + pg0 + pg) * M, S.meta_bytes, full);
+  };
 
   if (tid == kDecThreads) {
 #pragma unroll
@@ -245,360 +292,341 @@ __global__ void __launch_bounds__(kThreads, 3) decode_partial_tc(DecodeParams p)
     mbar_init(&bars[kBarPV], 1);
     *abort_s = 0;
     fence_mbar_init();
+    fence_proxy_async_smem();
+    // The first two pages load while the CTA stages its query.
+    issue_page(0);
+    if (npg > 1) issue_page(1);
   }
   if (warp == 4) {
     tmem_alloc(tmem_slot, S.tm_cols);
     tmem_relinquish();
   }
+  float qq[kGQ];   // compute thread: q_j[c] 2^(22-Eq) of its K position
+  int po = -1;     // compute thread: scale | min << 16 offsets of its K position, or -1
+  int eq = 0;
   if (tid < kDecThreads) {
-    load_query_group_rt(p, b, h, q_s, kDecThreads);
-    for (int pp = tid; pp < S.kpad; pp += kDecThreads) kpos_s[pp] = kpos_entry(L, p.slot_chan, h, pp);
-    for (int q = tid; q < npg; q += kDecThreads) esc_s[q] = 0;
+    // Query group (thread = channel), its block exponent Eq
+    // (max_j,c |q_j[c]| <= 2^Eq), and the scaled query of each K position.
+    const int e = tid < S.kpad ? kpos_entry(L, p.slot_chan, h, tid) : -1;
+    float qc[kGQ];
+    {
+      const int64_t base = b * p.q_seq_stride + static_cast<int64_t>(h) * p.gq * p.q_head_stride + tid;
+      if (p.q_dtype == LF_F32) {
+        const float* qp = static_cast<const float*>(p.q) + base;
+#pragma unroll
+        for (int j = 0; j < kGQ; ++j) qc[j] = j < GQ ? qp[j * p.q_head_stride] : 0.f;
+      } else if (p.q_dtype == LF_F16) {
+        const __half* qp = static_cast<const __half*>(p.q) + base;
+#pragma unroll
+        for (int j = 0; j < kGQ; ++j) qc[j] = j < GQ ? __half2float(qp[j * p.q_head_stride]) : 0.f;
+      } else {
+        const __nv_bfloat16* qp = static_cast<const __nv_bfloat16*>(p.q) + base;
+#pragma unroll
+        for (int j = 0; j < kGQ; ++j) qc[j] = j < GQ ? __bfloat162float(qp[j * p.q_head_stride]) : 0.f;
+      }
+    }
+    float qmax = 0.f;
+#pragma unroll
+    for (int j = 0; j < kGQ; ++j) {
+      q_s[j * kD + tid] = qc[j];
+      qmax = fmaxf(qmax, fabsf(qc[j]));
+    }
+    const uint32_t wmax = __reduce_max_sync(0xffffffffu, __float_as_uint(qmax));
+    if (lane == 0) red_m[warp] = wmax;
+    named_sync(1, kDecThreads);
+    const uint32_t mx = max(max(red_m[0], red_m[1]), max(red_m[2], red_m[3]));
+    eq = max(-60, min(60, exp2_ceil(__uint_as_float(mx))));
+    const float qscale = exp2i(22 - eq);
+    if (e >= 0) {
+      const int tier = (e >> 16) & 3, slot = e >> 18, ch = e & 0xFFFF;
+      po = (L.scale_off[tier] + slot) | ((L.min_off[tier] + slot) << 16);
+#pragma unroll
+      for (int j = 0; j < kGQ; ++j) qq[j] = q_s[j * kD + ch] * qscale;
+    } else {
+#pragma unroll
+      for (int j = 0; j < kGQ; ++j) qq[j] = 0.f;
+    }
+    // Second K positions t + 128 (wide layouts), kept in shared memory.
+    for (int pp = kDecThreads + tid; pp < S.kpad; pp += kDecThreads) {
+      const int e2 = kpos_entry(L, p.slot_chan, h, pp);
+      const int r = pp - kDecThreads;
+      int po2 = -1;
+      if (e2 >= 0) {
+        const int tier = (e2 >> 16) & 3, slot = e2 >> 18;
+        po2 = (L.scale_off[tier] + slot) | ((L.min_off[tier] + slot) << 16);
+      }
+#pragma unroll
+      for (int j = 0; j < kGQ; ++j) qhi_s[r * kGQ + j] = e2 >= 0 ? q_s[j * kD + (e2 & 0xFFFF)] * qscale : 0.f;
+      posoff_s[r] = po2;
+    }
+    for (int i = tid; i < L.width[3] * kGQ; i += kDecThreads) {
+      const int c = i / kGQ, j = i % kGQ;
+      const int ch = p.slot_chan[(3 * H + h) * kD + c];
+      q16_s[i] = ch < 0 ? 0.f : q_s[j * kD + ch] * c2;
+    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const uint64_t kLimit = kWaitLimitNs;
 
-  // ------------------------------------------------------------ control warp
   if (warp == 4) {
-    if (lane == 0) {
-      const uint64_t kLimit = kWaitLimitNs;
-      int issued[kStages] = {0, 0};
-      for (int i = 0; i < kStages && i < npg; ++i) {
-        uint64_t* full = &bars[kBarFull + i];
-        mbar_arrive_expect_tx(full, row_bytes + (i == 0 ? meta_bytes : 0u));
-        if (i == 0 && meta_bytes) bulk_g2s(smem + S.meta, p.kmeta + (head_meta + pg0) * M, meta_bytes, full);
-        bulk_g2s(stage0 + i * S.stage_bytes, p.rows + (head_row + static_cast<int64_t>(pg0 + i) * kP) * R,
-                 row_bytes, full);
-        ++issued[i];
-      }
-      // Descriptors: QK B per K step, PV A/B per K step and Value-tile parity.
-      const uint32_t n_ks = static_cast<uint32_t>(S.kpad / 32);
-      const uint64_t bqk_desc0 = smem_desc(bqk, 128, S.bqk_sbo);
-      const uint64_t apv_desc0 = smem_desc(apv, 128, 2048);
-      const uint64_t bpv_desc0 = smem_desc(bpv, 128, 2048);
-      int qk_open = 0, pv_open = 0;
-      for (int i = 0; i < npg; ++i) {
+    // ------------------------------------------------------------ control warp
+    int issued0 = 1, issued1 = npg > 1 ? 1 : 0, qk_open = 0, pv_open = 0;
+    const uint32_t n_ks = static_cast<uint32_t>(S.kpad / 32);
+    const uint64_t bqk_desc0 = smem_desc(bqk, 128, S.bqk_sbo);
+    const uint64_t apv_desc0 = smem_desc(apv, 128, 2048);
+    const uint64_t bpv_desc0 = smem_desc(bpv, 128, 2048);
+    for (int i = 0; i < npg; ++i) {
+      if (lane == 0) {
         if (!*abort_s && !mbar_wait_bounded(&bars[kBarKReady], i & 1, kLimit)) *abort_s = 1;
         tc_fence_after();
         for (uint32_t ks = 0; ks < n_ks; ++ks)  // +512 B per K step = +32 in descriptor units
-          mma_u8_ts(tmem + S.tm_qk, tmem + S.a_col + 8 * ks, bqk_desc0 + 32 * ks, kIdescQK, ks > 0 ? 1u : 0u);
+          mma_u8_ts(tmem + S.tm_qk, tmem + 8 * ks, bqk_desc0 + 32 * ks, kIdescQK, ks > 0 ? 1u : 0u);
         mma_commit(&bars[kBarQK]);
         qk_open = i + 1;
         if (!*abort_s && !mbar_wait_bounded(&bars[kBarVReady], i & 1, kLimit)) *abort_s = 1;
         tc_fence_after();
-        const uint64_t a_tile = apv_desc0 + static_cast<uint64_t>((i & 1) * (kP * kD / 16));
 #pragma unroll
         for (int ks = 0; ks < kP / 32; ++ks)
-          mma_u8_ss(tmem + S.tm_pv, a_tile + 32 * ks, bpv_desc0 + 32 * ks, kIdescPV, ks > 0 ? 1u : 0u);
+          mma_u8_ss(tmem + S.tm_pv, apv_desc0 + 32 * ks, bpv_desc0 + 32 * ks, kIdescPV, ks > 0 ? 1u : 0u);
         mma_commit(&bars[kBarPV]);
         pv_open = i + 1;
-        // Stage i % kStages has been read by U(i) and S(i): it takes page i + kStages.
+        // Stage i % 2 has been read by U_K(i), S(i) and U_V(i): it takes page i + 2.
         if (i + kStages < npg && !*abort_s) {
-          const int st = i % kStages;
-          uint64_t* full = &bars[kBarFull + st];
-          mbar_arrive_expect_tx(full, row_bytes);
-          bulk_g2s(stage0 + st * S.stage_bytes,
-                   p.rows + (head_row + static_cast<int64_t>(pg0 + i + kStages) * kP) * R, row_bytes, full);
-          ++issued[st];
+          issue_page(i + kStages);
+          if (i & 1) ++issued1; else ++issued0;
         }
       }
-      if (*abort_s) {
-        // Drain this CTA's copies and MMAs before its shared memory and TMEM go away.
-        for (int st = 0; st < kStages; ++st)
-          if (issued[st]) mbar_wait_bounded(&bars[kBarFull + st], (issued[st] - 1) & 1, kLimit);
-        if (qk_open) mbar_wait_bounded(&bars[kBarQK], (qk_open - 1) & 1, kLimit);
-        if (pv_open) mbar_wait_bounded(&bars[kBarPV], (pv_open - 1) & 1, kLimit);
-        if (p.status != nullptr) atomicExch(p.status, LF_ERR_DEVICE_TIMEOUT);
-      }
+    }
+    if (lane == 0 && *abort_s) {
+      // Drain this CTA's copies and MMAs before its shared memory and TMEM go away.
+      if (issued0) mbar_wait_bounded(&bars[kBarFull], (issued0 - 1) & 1, kLimit);
+      if (issued1) mbar_wait_bounded(&bars[kBarFull + 1], (issued1 - 1) & 1, kLimit);
+      if (qk_open) mbar_wait_bounded(&bars[kBarQK], (qk_open - 1) & 1, kLimit);
+      if (pv_open) mbar_wait_bounded(&bars[kBarPV], (pv_open - 1) & 1, kLimit);
+      if (p.status != nullptr) atomicExch(p.status, LF_ERR_DEVICE_TIMEOUT);
     }
     __syncwarp();
-    tc_fence_before();
-    __syncthreads();  // compute warps finished (their partial is written)
-    tc_fence_after();
-    tmem_dealloc(tmem, S.tm_cols);
-    return;
-  }
+  } else {
+    // ----------------------------------------------------------- compute warps
+    const uint32_t tm_a = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    for (int c = n_slots_of(L) / 4; c < S.a_cols; ++c) tmem_st_x1(tm_a + c, 0u);  // A padding columns
+    float og[GQ], lt[GQ], lvt[GQ];
+#pragma unroll
+    for (int j = 0; j < GQ; ++j) og[j] = lt[j] = lvt[j] = 0.f;
+    float m_l = -INFINITY;  // running max of q-head (lane & 7), log2 units
+    const int l8 = lane & 7;
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+      if (*abort_s) return;
+      if (!mbar_wait_bounded(bar, parity, kLimit)) *abort_s = 1;
+    };
+    const int wd0 = L.words[0], wd1 = L.words[1], wd2 = L.words[2], w3 = L.width[3];
+    const int co0 = L.code_off[0], co1 = L.code_off[1], co2 = L.code_off[2], vco = L.vcode_off;
+    const int row_off = tid * R;
+    const int rk = (tid >> 2) & 3;               // PV row t carries code * 4^rk
+    const bool has_pos = tid < S.kpad;           // warp-uniform (K padded to 32)
+    const int soff = po >= 0 ? (po & 0xFFFF) : 0, moff = po >= 0 ? (po >> 16) : 0;
+    const float cf = c2 * exp2i(eq - 22);        // fixed-point unit 2^(Eq-22) -> log2-scaled score
+    const int bslot = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
 
-  // ----------------------------------------------------------- compute warps
-  float mg[GQ], og[GQ], ltg[GQ], lvtg[GQ];
-#pragma unroll
-  for (int j = 0; j < GQ; ++j) {
-    mg[j] = -INFINITY;
-    og[j] = ltg[j] = lvtg[j] = 0.f;
-  }
-  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-  const uint64_t kLimit = kWaitLimitNs;
-  auto wait = [&](uint64_t* bar, uint32_t parity) {
-    if (*abort_s) return;
-    if (!mbar_wait_bounded(bar, parity, kLimit)) *abort_s = 1;
-  };
-
-  // Per-q-head block exponent of the query: max_c |q_j[c]| <= 2^eq_j.
-  int eq[GQ];
-#pragma unroll
-  for (int j = 0; j < GQ; ++j) {
-    const uint32_t mx = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(q_s[j * kD + tid])));
-    if (lane == 0) red_m[warp * 16 + j] = mx;
-  }
-  for (int i = tid; i < L.width[3] * kGQ; i += kDecThreads) {
-    const int ii = i / kGQ, j = i % kGQ;
-    const int ch = p.slot_chan[(3 * H + h) * kD + ii];
-    q16_s[i] = ch < 0 ? 0.f : q_s[j * kD + ch];
-  }
-  named_sync(1, kDecThreads);
-#pragma unroll
-  for (int j = 0; j < GQ; ++j) {
-    const uint32_t mx = max(max(red_m[j], red_m[16 + j]), max(red_m[32 + j], red_m[48 + j]));
-    eq[j] = max(-60, min(60, exp2_ceil(__uint_as_float(mx))));
-  }
-  // This thread's QK B rows: K positions tid and tid+128 (scaled query values).
-  float qq[2][GQ];
-  int soff[2], moff[2];
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const int pp = tid + k * kDecThreads;
-    const int e = pp < S.kpad ? kpos_s[pp] : -1;
-    soff[k] = moff[k] = -1;
-    if (e >= 0) {
-      const int tier = (e >> 16) & 3, slot = e >> 18;
-      soff[k] = L.scale_off[tier] + slot;
-      moff[k] = L.min_off[tier] + slot;
-    }
-#pragma unroll
-    for (int j = 0; j < GQ; ++j) qq[k][j] = e >= 0 ? q_s[j * kD + (e & 0xFFFF)] * exp2i(22 - eq[j]) : 0.f;
-  }
-  // A columns past the packed slots stay zero for the whole item.
-  for (int c = n_slots_of(L) / 4; c < S.kpad / 4; ++c) tmem_st_x1(tmem + lane_base + S.a_col + c, 0u);
-  const float c2 = p.scaling * kLog2e;
-
-  // Page-0 data (with the item's meta rows) -> per-page Key-scale exponents.
-  wait(&bars[kBarFull + 0], 0);
-  for (int q = 0; q < npg; ++q) {
-    float mx = 0.f;
-#pragma unroll
-    for (int k = 0; k < 2; ++k)
-      if (soff[k] >= 0) mx = fmaxf(mx, half_bits_to_float(meta_s[q * M + soff[k]]));
-    const uint32_t wmax = __reduce_max_sync(0xffffffffu, __float_as_uint(mx));
-    if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(esc_s) + q, wmax);
-  }
-  named_sync(1, kDecThreads);  // also: every read of the query staging (second Value tile) is done
-  for (int q = tid; q < npg; q += kDecThreads) esc_s[q] = max(-60, min(60, exp2_ceil(__uint_as_float(esc_s[q]))));
-  named_sync(1, kDecThreads);
-
-  // U(i): one pass over the token's row -- Key codes -> TMEM, Value codes ->
-  // Value tile (i & 1), QK B rows for this thread's slots, bias partials.
-  auto unpack = [&](int i) {
-    const uint32_t* rowp = reinterpret_cast<const uint32_t*>(stage0 + (i % kStages) * S.stage_bytes) + tid * R;
-    uint32_t vw[kD / 16];
-#pragma unroll
-    for (int w = 0; w < kD / 16; ++w) vw[w] = rowp[L.vcode_off + w];
-    const uint16_t* mrow = meta_s + i * M;
-    float msc[2], mmn[2];
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      msc[k] = soff[k] >= 0 ? half_bits_to_float(mrow[soff[k]]) : 0.f;
-      mmn[k] = soff[k] >= 0 ? half_bits_to_float(mrow[moff[k]]) : 0.f;
-    }
-    uint32_t col = tmem + lane_base + S.a_col;
-    {
-      const uint32_t* src = rowp + L.code_off[0];
+    // U_K(i): Key codes of the thread's token -> its TMEM lane (A of QK); the
+    // B row of K position tid; bias partials.  Returns the page's Es.
+    auto unpack_k = [&](int i) -> int {
+      const unsigned char* stage = stage0 + (i & 1) * S.stage_bytes;
+      const uint32_t* rowp = reinterpret_cast<const uint32_t*>(stage) + row_off;
+      const uint16_t* meta = reinterpret_cast<const uint16_t*>(stage + S.rows_bytes);
+      uint32_t col = tm_a;
+      {
+        const uint32_t* src = rowp + co0;
 #pragma unroll 4
-      for (int w = 0; w < L.words[0]; ++w) {
-        const uint32_t x = src[w];
-        tmem_st_x4(col + 4 * w, x & kM2, (x >> 2) & kM2, (x >> 4) & kM2, (x >> 6) & kM2);
+        for (int w = 0; w < wd0; ++w) {
+          const uint32_t x = src[w];
+          tmem_st_x4(col + 4 * w, x & kM2, (x >> 2) & kM2, (x >> 4) & kM2, (x >> 6) & kM2);
+        }
+        col += 4 * wd0;
       }
-      col += 4 * L.words[0];
-    }
-    {
-      const uint32_t* src = rowp + L.code_off[1];
+      {
+        const uint32_t* src = rowp + co1;
 #pragma unroll 4
-      for (int w = 0; w < L.words[1]; ++w) {
-        const uint32_t x = src[w];
-        tmem_st_x2(col + 2 * w, x & kM4, (x >> 4) & kM4);
+        for (int w = 0; w < wd1; ++w) {
+          const uint32_t x = src[w];
+          tmem_st_x2(col + 2 * w, x & kM4, (x >> 4) & kM4);
+        }
+        col += 2 * wd1;
       }
-      col += 2 * L.words[1];
-    }
-    {
-      const uint32_t* src = rowp + L.code_off[2];
+      {
+        const uint32_t* src = rowp + co2;
 #pragma unroll 4
-      for (int w = 0; w < L.words[2]; ++w) tmem_st_x1(col + w, src[w]);
-    }
-    {
-      unsigned char* dst = apv + (i & 1) * (kP * kD) + (tid & 7) * 16 + (tid >> 3) * 128;
+        for (int w = 0; w < wd2; ++w) tmem_st_x1(col + w, src[w]);
+      }
+      const int esc = page_scale_exp(meta, kmax_off);
+      const float fsc = exp2i(-esc);
+      if (has_pos) {
+        const float sc = po >= 0 ? half_bits_to_float(meta[soff]) * fsc : 0.f;
+        const float mn = po >= 0 ? half_bits_to_float(meta[moff]) : 0.f;
+        float bias[kGQ];
+#pragma unroll
+        for (int j = 0; j < kGQ; ++j) bias[j] = 0.f;
+        qk_b_row<GQ>(bqk, S.bqk_sbo, tid, qq, sc, mn, bias);
+        if (has_hi) {
+          const int o = posoff_s[tid];
+          const float4 qa = *reinterpret_cast<const float4*>(qhi_s + tid * kGQ);
+          const float4 qb = *reinterpret_cast<const float4*>(qhi_s + tid * kGQ + 4);
+          const float qv[kGQ] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+          const float sc2 = o >= 0 ? half_bits_to_float(meta[o & 0xFFFF]) * fsc : 0.f;
+          const float mn2 = o >= 0 ? half_bits_to_float(meta[o >> 16]) : 0.f;
+          qk_b_row<GQ>(bqk, S.bqk_sbo, kDecThreads + tid, qv, sc2, mn2, bias);
+        }
+        const float part = warp_sum8_scatter(bias, lane);
+        if ((lane & 3) == 0) red_b[(i & 1) * 32 + warp * kGQ + bslot] = part;
+      } else if ((lane & 3) == 0) {
+        red_b[(i & 1) * 32 + warp * kGQ + bslot] = 0.f;
+      }
+      tmem_wait_st();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars[kBarKReady]);
+      return esc;
+    };
+    // U_V(i): Value codes of the thread's token -> row t of the Value tile.
+    auto unpack_v = [&](int i) {
+      const uint32_t* src = reinterpret_cast<const uint32_t*>(stage0 + (i & 1) * S.stage_bytes) + row_off + vco;
+      uint32_t vw[kD / 16];
+#pragma unroll
+      for (int w = 0; w < kD / 16; ++w) vw[w] = src[w];
+      unsigned char* dst = apv + (tid & 7) * 16 + (tid >> 3) * 128;
 #pragma unroll
       for (int w = 0; w < kD / 16; ++w) {
         const uint32_t x = vw[w];
-        *reinterpret_cast<uint4*>(dst + w * 2048) = make_uint4(x & kM2, (x >> 2) & kM2, (x >> 4) & kM2, (x >> 6) & kM2);
+        *reinterpret_cast<uint4*>(dst + w * 2048) = make_uint4(x & kM2, x & (kM2 << 2), x & (kM2 << 4), x & (kM2 << 6));
       }
-    }
-    float bias[kGQ];
-#pragma unroll
-    for (int j = 0; j < kGQ; ++j) bias[j] = 0.f;
-    const float fsc = exp2i(-esc_s[i]);
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int pp = tid + k * kDecThreads;
-      if (pp >= S.kpad) break;
-      uint4 c0 = make_uint4(0u, 0u, 0u, 0u), c1 = c0;
-      if (soff[k] >= 0) {
-        const float sc = msc[k] * fsc;
-        uint32_t U[kGQ];
-#pragma unroll
-        for (int j = 0; j < kGQ; ++j) {
-          if (j < GQ) {
-            // rint(qq * sc) + 2^23 via the fp32 magic constant 1.5 * 2^23.
-            U[j] = __float_as_uint(fmaf(qq[k][j], sc, 12582912.0f)) - 0x4AC00000u;
-            bias[j] = fmaf(qq[k][j], mmn[k], bias[j]);
-          } else {
-            U[j] = 0x800000u;  // X = 0
-          }
-        }
-        pack_limbs(U, c0, c1, 1u);
-      }
-      unsigned char* dst = bqk + (pp & 7) * 16 + (pp >> 3) * 128;
-      *reinterpret_cast<uint4*>(dst) = c0;
-      *reinterpret_cast<uint4*>(dst + S.bqk_sbo) = c1;
-    }
-    const float part = warp_sum8_scatter(bias, lane);
-    if ((lane & 3) == 0)
-      red_b[(i & 1) * 32 + warp * kGQ + (((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1))] = part;
-    tmem_wait_st();
-    fence_proxy_async_smem();
-    tc_fence_before();
-    mbar_arrive(&bars[kBarKReady]);
-  };
+    };
 
-  float alpha[GQ];
-  int ev[GQ];
-  // Iteration i runs S(i), U(i+1), C(i); iteration -1 only U(0).
-  for (int i = -1; i < npg; ++i) {
-    if (i < 0) {
-      unpack(0);
-      continue;
-    }
-    // S(i): scores, page max, online softmax, PV B rows.  The FP16 Key tier
-    // (CUDA cores) and the token's Value scale / min come from the page's
-    // stage, resident until this page's V-ready arrive.
-    const uint16_t* row16 =
-        reinterpret_cast<const uint16_t*>(stage0 + (i % kStages) * S.stage_bytes) + 2 * tid * R + 2 * L.half_off;
-    float s16[GQ];
+    wait(&bars[kBarFull], 0);
+    int esc = unpack_k(0);
+    unpack_v(0);
+    for (int i = 0; i < npg; ++i) {
+      const int st = i & 1;
+      // S(i).  The FP16 Key tier (CUDA cores) and the token's Value scale /
+      // min come from the page's stage, resident until this page's V-ready.
+      const uint16_t* row16 =
+          reinterpret_cast<const uint16_t*>(stage0 + st * S.stage_bytes) + 2 * (row_off + L.half_off);
+      float s16[GQ];
 #pragma unroll
-    for (int j = 0; j < GQ; ++j) s16[j] = 0.f;
+      for (int j = 0; j < GQ; ++j) s16[j] = 0.f;
 #pragma unroll 4
-    for (int c = 0; c < L.width[3]; ++c) {
-      const float kv = half_bits_to_float(row16[c]);
-      const float4 qa = *reinterpret_cast<const float4*>(q16_s + c * kGQ);
-      const float4 qb = *reinterpret_cast<const float4*>(q16_s + c * kGQ + 4);
-      const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+      for (int c = 0; c < w3; ++c) {
+        const float kv = half_bits_to_float(row16[c]);
+        const float4 qa = *reinterpret_cast<const float4*>(q16_s + c * kGQ);
+        const float4 qb = *reinterpret_cast<const float4*>(q16_s + c * kGQ + 4);
+        const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-      for (int j = 0; j < GQ; ++j) s16[j] = fmaf(qv[j], kv, s16[j]);
-    }
-    const float vs_i = half_bits_to_float(row16[L.width[3]]);
-    const float vm_i = half_bits_to_float(row16[L.width[3] + 1]);
-    const int esc = esc_s[i];
-    wait(&bars[kBarQK], i & 1);
-    tc_fence_after();
-    uint32_t acc[32];
-    tmem_ld_x32_sync(tmem + lane_base + S.tm_qk, acc);
-    const int ones = static_cast<int>(acc[24]);
-    float x[GQ];
-    uint32_t* rm = red_m + (i & 1) * 64;
-    uint32_t keys[12];
-#pragma unroll
-    for (int j = 0; j < 12; ++j) keys[j] = 0u;
-#pragma unroll
-    for (int j = 0; j < GQ; ++j) {
-      const int lo = static_cast<int>(acc[j]) + (static_cast<int>(acc[8 + j]) << 8);
-      const float sint = fmaf(static_cast<float>(static_cast<int>(acc[16 + j]) - 128 * ones), 65536.f,
-                              static_cast<float>(lo));
-      x[j] = fmaf(sint, c2 * exp2i(eq[j] + esc - 22), s16[j] * c2);
-      keys[j] = order_key(x[j]);
-    }
-    keys[8] = __float_as_uint(vs_i);
-#pragma unroll
-    for (int j = 0; j < GQ; ++j) keys[j] = __reduce_max_sync(0xffffffffu, keys[j]);
-    keys[8] = __reduce_max_sync(0xffffffffu, keys[8]);
-    if (lane == 0) {
-      *reinterpret_cast<uint4*>(rm + warp * 16) = make_uint4(keys[0], keys[1], keys[2], keys[3]);
-      *reinterpret_cast<uint4*>(rm + warp * 16 + 4) = make_uint4(keys[4], keys[5], keys[6], keys[7]);
-      *reinterpret_cast<uint4*>(rm + warp * 16 + 8) = make_uint4(keys[8], 0u, 0u, 0u);
-    }
-    named_sync(1, kDecThreads);
-    uint32_t U[kGQ];
-    {
-      uint32_t km[12];
-      float bs[8];
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        const uint4 k0 = *reinterpret_cast<const uint4*>(rm + w * 16);
-        const uint4 k1 = *reinterpret_cast<const uint4*>(rm + w * 16 + 4);
-        const uint4 k2 = *reinterpret_cast<const uint4*>(rm + w * 16 + 8);
-        const float4 b0 = *reinterpret_cast<const float4*>(red_b + (i & 1) * 32 + w * 8);
-        const float4 b1 = *reinterpret_cast<const float4*>(red_b + (i & 1) * 32 + w * 8 + 4);
-        const uint32_t kk[12] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w, k2.x, k2.y, k2.z, k2.w};
-        const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-        for (int e = 0; e < 9; ++e) km[e] = w == 0 ? kk[e] : max(km[e], kk[e]);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) bs[e] = w == 0 ? bb[e] : bs[e] + bb[e];
+        for (int j = 0; j < GQ; ++j) s16[j] = fmaf(qv[j], kv, s16[j]);
       }
-      const int ev_vs = max(-60, min(60, exp2_ceil(__uint_as_float(km[8]))));
+      const float vs = half_bits_to_float(row16[w3]);
+      const float vm = half_bits_to_float(row16[w3 + 1]);
+      const float f = cf * exp2i(esc), f16 = f * 65536.f;
+      wait(&bars[kBarQK], st);
+      tc_fence_after();
+      uint32_t a[32];
+      tmem_ld_x32_sync(tm_a + S.tm_qk, a);
+      const int ones128 = static_cast<int>(a[24]) * 128;
+      float x[GQ];
+      uint32_t key[GQ];
+#pragma unroll
+      for (int j = 0; j < GQ; ++j) {
+        const uint32_t lo = a[j] + (a[8 + j] << 8);
+        const int hi = static_cast<int>(a[16 + j]) - ones128;
+        x[j] = fmaf(static_cast<float>(hi), f16, fmaf(static_cast<float>(lo), f, s16[j]));
+        key[j] = __reduce_max_sync(0xffffffffu, order_key(x[j]));
+      }
+      const uint32_t vkey = __reduce_max_sync(0xffffffffu, __float_as_uint(vs));
+      uint32_t* rm = red_m + st * 64;
+      if (lane == 0) {
+#pragma unroll
+        for (int j = 0; j < kGQ; ++j) rm[warp * 16 + j] = j < GQ ? key[j] : 0u;
+        rm[warp * 16 + 8] = vkey;
+      }
+      named_sync(1, kDecThreads);
+      // Lane j (mod 8): statistics of q-head j.  The bias is the same for
+      // every token of the page, so the page max is max(score) + bias.
+      const float* rb = red_b + st * 32 + l8;
+      const float bias = ((rb[0] + rb[8]) + (rb[16] + rb[24])) * cf;
+      const uint32_t km = max(max(rm[l8], rm[16 + l8]), max(rm[32 + l8], rm[48 + l8]));
+      const uint32_t vk = max(max(rm[8], rm[24]), max(rm[40], rm[56]));
+      const float mnew = fmaxf(m_l, order_key_to_float(km) + bias);
+      const float alpha = m_l == -INFINITY ? 0.f : ex2(m_l - mnew);
+      m_l = mnew;
+      const float off = bias - mnew;
+      if (__any_sync(0xffffffffu, l8 < GQ && alpha != 1.f)) {
+#pragma unroll
+        for (int j = 0; j < GQ; ++j) {
+          const float aj = __shfl_sync(0xffffffffu, alpha, j);
+          og[j] *= aj;
+          lt[j] *= aj;
+          lvt[j] *= aj;
+        }
+      }
+      const int ev = max(-60, min(60, exp2_ceil(__uint_as_float(vk))));
+      const float vsc = vs * exp2i(23 - ev);
+      uint32_t U[kGQ];
 #pragma unroll
       for (int j = 0; j < kGQ; ++j) {
         if (j < GQ) {
-          const float bias = bs[j] * (c2 * exp2i(eq[j] - 22));
-          const float pm = order_key_to_float(km[j]) + bias;
-          const float mnew = fmaxf(mg[j], pm);
-          alpha[j] = mg[j] == -INFINITY ? 0.f : ex2(mg[j] - mnew);
-          mg[j] = mnew;
-          const float pj = ex2(x[j] + bias - mnew);
-          // Bound on p * vscale over the page: 2^(pm - mnew) * max vscale.
-          ev[j] = ev_vs + max(-60, static_cast<int>(ceilf(pm - mnew)));
-          ltg[j] = fmaf(ltg[j], alpha[j], pj);
-          lvtg[j] = fmaf(lvtg[j], alpha[j], pj * vm_i);
-          // rint(p * vs * 2^(23 - ev)) via the fp32 magic constant 2^23.
-          U[j] = __float_as_uint(fmaf(pj, vs_i * exp2i(23 - ev[j]), 8388608.0f)) - 0x4B000000u;
+          const float pj = ex2(x[j] + __shfl_sync(0xffffffffu, off, j));
+          lt[j] += pj;
+          lvt[j] = fmaf(pj, vm, lvt[j]);
+          // rint(p * vs * 2^(23 - Ev)) via the fp32 magic constant 2^23.
+          U[j] = __float_as_uint(fmaf(pj, vsc, 8388608.0f)) - 0x4B000000u;
         } else {
           U[j] = 0u;
         }
       }
-    }
-    {
-      uint4 c0, c1;
-      pack_limbs(U, c0, c1, 0u);
-      unsigned char* dst = bpv + (tid & 7) * 16 + (tid >> 3) * 128;
-      *reinterpret_cast<uint4*>(dst) = c0;
-      *reinterpret_cast<uint4*>(dst + 2048) = c1;
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    mbar_arrive(&bars[kBarVReady]);
-    // U(i+1) while PV(i) runs.
-    if (i + 1 < npg) {
-      wait(&bars[kBarFull + (i + 1) % kStages], ((i + 1) / kStages) & 1);
-      unpack(i + 1);
-    }
-    // C(i): accumulate this thread's head-dim position.
-    wait(&bars[kBarPV], i & 1);
-    tc_fence_after();
-    tmem_ld_x32_sync(tmem + lane_base + S.tm_pv, acc);
+      {
+        uint4 c0, c1;
+        pack_limbs(U, c0, c1, 0u);
+        unsigned char* dst = bpv + (tid & 7) * 16 + (tid >> 3) * 128;
+        *reinterpret_cast<uint4*>(dst) = c0;
+        *reinterpret_cast<uint4*>(dst + 2048) = c1;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars[kBarVReady]);
+      // U_K(i+1) while PV(i) runs.
+      if (i + 1 < npg) {
+        wait(&bars[kBarFull + (st ^ 1)], ((i + 1) >> 1) & 1);
+        esc = unpack_k(i + 1);
+      }
+      // C(i): accumulate PV row t.
+      wait(&bars[kBarPV], st);
+      tc_fence_after();
+      tmem_ld_x32_sync(tm_a + S.tm_pv, a);
+      const float sc = exp2i(ev - 23 - 2 * rk);
 #pragma unroll
-    for (int j = 0; j < GQ; ++j) {
-      const int lo = static_cast<int>(acc[j]) + (static_cast<int>(acc[8 + j]) << 8);
-      const float v = fmaf(static_cast<float>(static_cast<int>(acc[16 + j])), 65536.f, static_cast<float>(lo));
-      og[j] = fmaf(og[j], alpha[j], v * exp2i(ev[j] - 23));
+      for (int j = 0; j < GQ; ++j) {
+        const uint32_t lo = a[j] + (a[8 + j] << 8);
+        const float v = fmaf(static_cast<float>(a[16 + j]), 65536.f, static_cast<float>(lo));
+        og[j] = fmaf(v, sc, og[j]);
+      }
+      // U_V(i+1): the Value tile is free once PV(i) has completed.
+      if (i + 1 < npg) unpack_v(i + 1);
     }
-  }
 
+    float mg[GQ];
 #pragma unroll
-  for (int j = 0; j < GQ; ++j) mg[j] *= kLn2;  // log2 units -> natural-log units
-  // PV row t holds head-dim channel d(t): t = 16w + 4k + i  <->  d = 16w + k + 4i.
-  const int d = (tid & ~15) + ((tid & 15) >> 2) + 4 * (tid & 3);
-  write_partial_group<GQ>(p, b, h, s, d, og, mg, ltg, lvtg, red_w, 1);
+    for (int j = 0; j < GQ; ++j) mg[j] = __shfl_sync(0xffffffffu, m_l, j) * kLn2;  // natural-log units
+    // PV row t holds head-dim channel d(t): t = 16w + 4k + i  <->  d = 16w + k + 4i.
+    const int d = (tid & ~15) + ((tid & 15) >> 2) + 4 * (tid & 3);
+    write_partial_group<GQ>(p, b, h, s, d, og, mg, lt, lvt, red_w, 1);
+  }
   tc_fence_before();
-  __syncthreads();
+  __syncthreads();  // compute warps finished (their partial is written); copies and MMAs drained
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem, S.tm_cols);
+  }
 }
 
 }  // namespace tc
@@ -608,7 +636,7 @@ bool tc_supported(const lf_layout& L, int gq, int pps) {
   if (L.bit_v != 2 || gq > kGQ || gq < 1) return false;
   if (tc::n_slots_of(L) > 2 * kDecThreads) return false;  // two K positions per compute thread
   if (pps > tc::kMaxPagesPerItem) return false;
-  const tc::TcSmem S = tc::tc_smem(L, pps);
+  const tc::TcSmem S = tc::tc_smem(L);
   // The residual split's fp32 rows must end before the query staging.
   if (S.stage0 + resid_smem(tc::kD).total > S.qs) return false;
   return S.total <= 227 * 1024;
@@ -631,11 +659,24 @@ static void* tc_kernel_for(int gq) {
   }
 }
 
+// Largest dynamic shared memory and the full shared-memory carveout, so
+// several CTAs fit on one SM (the occupancy query reads both attributes).
+static cudaError_t configure_tc(void* kern, int smem_bytes) {
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                              cudaSharedmemCarveoutMaxShared);
+}
+
 int occupancy_tc(const lf_layout& L, int gq, int pps) {
-  const tc::TcSmem S = tc::tc_smem(L, pps);
+  (void)pps;  // the stage holds one page's meta row: shared memory does not depend on pps
+  const tc::TcSmem S = tc::tc_smem(L);
   if (S.total > 227 * 1024) return 0;
   void* kern = tc_kernel_for(gq);
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S.total);
+  if (configure_tc(kern, S.total) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
   int blocks = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kern, tc::kThreads, S.total) != cudaSuccess) {
     cudaGetLastError();
@@ -649,11 +690,11 @@ int launch_partial_tc(const DecodeParams& p, int resid_dtype, int q_dtype, cudaS
   DecodeParams q = p;
   q.resid_dtype = resid_dtype;
   q.q_dtype = q_dtype;
-  const tc::TcSmem S = tc::tc_smem(q.L, q.pps);
+  const tc::TcSmem S = tc::tc_smem(q.L);
   void* kern = tc_kernel_for(q.gq);
   static std::atomic<int> configured[kGQ + 1];
-  if (S.total > 48 * 1024 && S.total > configured[q.gq].load()) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S.total);
+  if (S.total > configured[q.gq].load()) {
+    cudaError_t e = configure_tc(kern, S.total);
     if (e != cudaSuccess) {
       set_error("lf_decode_partial (tcgen05): shared memory %d B: %s", S.total, cudaGetErrorString(e));
       return LF_ERR_UNSUPPORTED;

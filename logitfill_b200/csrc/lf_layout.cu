@@ -94,6 +94,10 @@ extern "C" int lf_layout_init(lf_layout* out, int kv_heads, int head_dim, int pa
     L.min_off[t] = hoff;
     hoff += L.width[t];
   }
+  // The Key group's largest tier scale (written by lf_pack_pages): the
+  // decoder's fixed-point exponent for the page, readable without a reduction.
+  L.kmax_off = hoff;
+  hoff += 1;
   L.meta_halves = round_up(hoff, 8);
   L.row_cap = row_cap;
   L.group_cap = group_cap;

@@ -124,6 +124,15 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
     vlo[i] = lo;
   }
   __syncthreads();
+  // Largest stored Key scale of each group over the head's INT2/INT4/INT8
+  // channels (positive fp16 values order as their bit patterns).
+  for (int g = tid; g < G; g += kPackThreads) {
+    uint16_t mx = 0;
+    for (int b = 0; b < 3; ++b)
+      for (int slot = 0; slot < L.width[b]; ++slot)
+        if (slotmap[b * D + slot] >= 0) mx = max(mx, meta[g * M + L.scale_off[b] + slot]);
+    meta[g * M + L.kmax_off] = mx;
+  }
 
   // Assemble every word of the page's rows.
   int32_t* out_rows = rows + ((static_cast<int64_t>(dst_seq) * H + h) * L.row_cap +
@@ -170,6 +179,7 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
     }
     out_rows[i] = static_cast<int32_t>(word);
   }
+  __syncthreads();  // the group maxima
   uint16_t* out_meta = kmeta + ((static_cast<int64_t>(dst_seq) * H + h) * L.group_cap +
                                 static_cast<int64_t>(dst_page) * G) * M;
   for (int i = tid; i < G * M; i += kPackThreads) out_meta[i] = meta[i];

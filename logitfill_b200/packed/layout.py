@@ -9,7 +9,8 @@ preallocated buffers per batch,
 * ``rows``  int32 ``[B, H, row_cap, row_words]`` -- per token: INT2 | INT4 |
   INT8 Key codes, Value codes, then fp16 FP16-tier Key, Value scale, Value min;
 * ``kmeta`` fp16  ``[B, H, group_cap, meta_halves]`` -- per Key group: scale
-  and min of each INT2/INT4/INT8 tier channel;
+  and min of each INT2/INT4/INT8 tier channel, then the group's largest
+  scale (the decoder's fixed-point exponent for the page);
 
 and every reference array is a strided view of them (:meth:`LayerLayout.hist_k_views`),
 so a sequence's history has the reference's shapes and bytes with no copy.

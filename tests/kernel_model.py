@@ -5,11 +5,13 @@ INT8 tensor cores (``tcgen05.mma.kind::i8``):
 
 * QK: integer Key codes (u8, 0..255) times the per-page products
   ``q_j[c] * scale_c`` written as 24-bit fixed point ``X`` relative to a
-  power-of-two block exponent, offset by 2^23 so the three limbs (bytes) are
-  unsigned.  A column of ones in the B operand returns sum_c code_c, which
-  removes the offset exactly in int32: ``acc0 + 256 acc1 + 65536 (acc2 - 128 ones)``.
+  power-of-two block exponent (one per query group and page), offset by 2^23
+  so the three limbs (bytes) are unsigned.  A column of ones in the B operand
+  returns sum_c code_c, which removes the offset exactly:
+  ``acc0 + 256 acc1 + 65536 (acc2 - 128 ones)``.
 * PV: integer Value codes (u8, 0..3) times ``p_t * vscale_t`` written as 23-bit
-  unsigned fixed point (three limbs) relative to a per-page exponent.
+  unsigned fixed point (three limbs) relative to a per-page exponent (the page's
+  largest Value scale: p <= 1 after the max update).
 
 This model reproduces that arithmetic (integer parts exactly, float parts in
 fp32) so the scheme's error against the oracle can be measured on the CPU;
@@ -42,7 +44,8 @@ def model_attention(layer: orc.OracleLayer, query: np.ndarray, key_new, value_ne
     kh, vh = layer.dequantize() if T else (None, None)
     for h in range(H):
         q = query[h * gq:(h + 1) * gq].astype(np.float32)        # [gq, D]
-        eq = _exp2_ceil(np.maximum(np.abs(q).max(axis=1), 1e-30))  # per q-head block exponent
+        # one block exponent for the whole query group: max_j,c |q_j[c]| <= 2^eq
+        eq = np.full(gq, int(_exp2_ceil(max(float(np.abs(q).max()), 1e-30))))
         m = np.full(gq, -np.inf)
         l = np.zeros(gq)
         o = np.zeros((gq, D))
@@ -88,7 +91,8 @@ def model_attention(layer: orc.OracleLayer, query: np.ndarray, key_new, value_ne
             vs = layer.hist_v["scale"][h, t0:t0 + 128, 0].astype(np.float64)
             vm = layer.hist_v["min"][h, t0:t0 + 128, 0].astype(np.float64)
             vcodes = orc.unpack_ints(layer.hist_v["code"][h, t0:t0 + 128], D, 2).astype(np.int64)
-            ev = _exp2_ceil(np.maximum(np.exp(pm - m_new) * vs.max(), 1e-30))   # per q-head
+            # p <= 1 after the max update, so p * vscale <= max vscale: one exponent per page.
+            ev = np.full(gq, int(_exp2_ceil(np.maximum(vs.max(), 1e-30))))
             U = np.minimum(np.rint(p * vs[:, None] * np.ldexp(1.0, pv_bits - ev)[None, :]),
                            (1 << pv_bits) - 1).astype(np.int64)
             acc = sum(((U >> (8 * k)) & 0xFF).T @ vcodes * 256.0 ** k for k in range((pv_bits + 7) // 8))

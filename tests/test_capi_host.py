@@ -50,7 +50,7 @@ def _layout_restated(counts, D, P, kg, vg, bit_v):
     half_off = vcode_off + vcode_words
     halves = width[3] + 2 * (D // vg)
     row_words = (half_off + (halves + 1) // 2) | 1
-    meta = -(-(2 * sum(width[:3])) // 8) * 8
+    meta = -(-(2 * sum(width[:3]) + 1) // 8) * 8  # scales, mins, then the group's largest scale
     return width, words, code_off, vcode_off, half_off, row_words, meta
 
 
@@ -68,6 +68,7 @@ def test_layout_init_matches_restatement(target_bit):
     assert list(c.code_off) == code_off
     assert (c.vcode_off, c.half_off, c.row_words, c.meta_halves) == (vcode_off, half_off, row_words, meta)
     assert c.row_words % 2 == 1 and c.meta_halves % 8 == 0
+    assert c.kmax_off == 2 * sum(width[:3]) and list(c.min_off) == [c.scale_off[t] + width[t] for t in range(3)]
     assert (c.row_cap, c.group_cap) == (512, 4)
 
 

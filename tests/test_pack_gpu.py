@@ -86,6 +86,28 @@ def test_config0_store(name):
     _check_store(manager_for(case), case)
 
 
+def test_group_max_scale_field():
+    """K1 also writes, at ``kmax_off`` of each meta row, the Key group's
+    largest stored INT2/INT4/INT8 scale over the head's channels (the decode
+    kernel's fixed-point exponent for the page): checked against the oracle's
+    scales, padding channels excluded."""
+    case = cases.config0_like(1024, 37)
+    mgr = manager_for(case)
+    ref = oracle_layer_for(case)
+    layer = mgr.cache.layers[0]
+    off = int(layer.layout.c.kmax_off)
+    got = layer.kmeta[0, :, : ref.hist_len // 128, off].cpu().numpy().view(np.uint16)
+    H = got.shape[0]
+    want = np.zeros_like(got)
+    for h in range(H):
+        for code in range(3):
+            cnt = int(ref.table[code]["count"][h])
+            if cnt:
+                sc = np.asarray(ref.hist_k[code]["scale"], np.float16)[h, :cnt].view(np.uint16)  # [cnt, G]
+                want[h] = np.maximum(want[h], sc.max(axis=0))
+    np.testing.assert_array_equal(got, want)
+
+
 def test_capacity_growth_keeps_history():
     """Commits beyond the initial capacity reallocate and keep every byte."""
     case = cases.config0_like(1024, 37)
