@@ -6,17 +6,17 @@
 // current page, TMEM lane t and row t of the PV result) and one control warp.
 //
 // Control warp: lane 0 issues the 1-D bulk copies (a page's row block and
-// meta row per stage) and the MMAs, nothing else: a proxy fence in the thread
-// that issued a bulk copy waits for that copy, so the copy issuer never
-// writes MMA operands.
+// meta row per stage) and the MMAs; the warp builds the QK B rows of K
+// positions 128 and up (wide layouts) between its PV issue and the next copy:
+// a proxy fence in the thread that issued a bulk copy waits for that copy.
 // Compute warps, per page i:
-//   U_K  Key codes -> u8 in TMEM (A of QK, K-major); the B rows of QK for K
-//        positions t and t + 128 (tier slot c): for each q-head j the 24-bit fixed point
-//        X = rint(q_j[c] scale_c 2^(22-Eq-Es)), offset by 2^23 and split into
+//   U_K  Key codes -> u8 in TMEM (A of QK, K-major); the B row of QK for K
+//        position t (tier slot c): for each q-head j the fixed point
+//        X = rint(q_j[c] scale_c 2^(21-Eq-Es)), offset by 2^22 and split into
 //        three unsigned limbs, plus a one in the ones column; Es is the page's
 //        Key-scale exponent, from the largest scale the packer stores in the
 //        meta row; partial sums of the Key-min bias sum_c q_j[c] min_c.
-//   S    score_tj = 2^(Eq+Es-22) (acc0 + 256 acc1 + 65536 (acc2 - 128 ones))
+//   S    score_tj = 2^(Eq+Es-21) (acc0 + 256 acc1 + 65536 (acc2 - 64 ones))
 //        + FP16-tier part + bias_j; page max per q-head; online softmax with
 //        the per-q-head statistics held by lane j of every warp; the B row of
 //        PV for token t: rint(p_tj vscale_t 2^(23-Ev)) in three limbs, Ev the
@@ -28,12 +28,13 @@
 // Order: S(i), U_K(i+1), C(i), U_V(i+1).  QK(i+1) overlaps C(i) and U_V(i+1),
 // PV(i) overlaps U_K(i+1).
 //
-// The integer products are exact; the fixed-point rounding is 2^-22 (QK) and
+// The integer products are exact; the fixed-point rounding is 2^-21 (QK) and
 // 2^-23 (PV) of the block maxima (tests/kernel_model.py models it).  Every
 // mbarrier wait is bounded (2 s).  On expiry the CTA records
 // LF_ERR_DEVICE_TIMEOUT, stops waiting (every warp still passes the same
 // barriers, so nothing deadlocks), drains its own copies and MMAs, frees its
 // TMEM and returns.
+#include <algorithm>
 #include <atomic>
 
 #include "lf_decode_common.cuh"
@@ -82,10 +83,10 @@ __host__ __device__ inline TcSmem tc_smem(const lf_layout& L) {
   int off = 0;
   s.bars = off; off += 128;
   s.red = off; off += 2 * 4 * 16 * 4;   // page maxima [stage][warp][16]
-  s.redb = off; off += 2 * 4 * kGQ * 4;  // bias partials [stage][warp][8]
+  s.redb = off; off += 2 * 5 * kGQ * 4;  // bias partials [stage][4 compute warps + control][8]
   s.redw = off; off += 4 * kGQ * 4;     // item-end sums
   s.q16 = off; off += ((L.width[3] > 0 ? L.width[3] : 1) * kGQ * 4 + 15) / 16 * 16;
-  const int hi = s.kpad > kDecThreads ? s.kpad - kDecThreads : 0;  // second K positions (t + 128)
+  const int hi = s.kpad > kDecThreads ? s.kpad - kDecThreads : 0;  // K positions of the control warp
   s.qhi = off; off += hi * kGQ * 4;
   s.posoff = off; off += hi * 4;
   off = (off + 127) / 128 * 128;
@@ -196,8 +197,11 @@ __device__ __forceinline__ float exp2i(int e) { return __int_as_float((e + 127) 
 // Barrier slots in shared memory.
 enum { kBarFull = 0, kBarKReady = kStages, kBarVReady, kBarQK, kBarPV, kNumBars };
 
-// One B row of QK (K position pp; qv = q_j[c] 2^(22-Eq), zero for a padding
-// position, whose A codes are zero) and its Key-min bias terms.
+// One B row of QK (K position pp; qv = q_j[c] 2^(21-Eq), zero for a padding
+// position, whose A codes are zero) and its Key-min bias terms.  With
+// |X| <= 2^21 the fp32 sum 1.5 * 2^23 + X lies in [2^23, 2^24), where the
+// spacing is 1: the sum is rint(X) + 1.5 * 2^23 and its low 24 bits are
+// U = X + 2^22, the three limbs, with no integer arithmetic.
 template <int GQ>
 __device__ __forceinline__ void qk_b_row(unsigned char* bqk, int sbo, int pp, const float (&qv)[kGQ], float sc,
                                          float mn, float (&bias)[kGQ]) {
@@ -205,11 +209,10 @@ __device__ __forceinline__ void qk_b_row(unsigned char* bqk, int sbo, int pp, co
 #pragma unroll
   for (int j = 0; j < kGQ; ++j) {
     if (j < GQ) {
-      // rint(qq * sc) + 2^23 via the fp32 magic constant 1.5 * 2^23.
-      U[j] = __float_as_uint(fmaf(qv[j], sc, 12582912.0f)) - 0x4AC00000u;
+      U[j] = __float_as_uint(fmaf(qv[j], sc, 12582912.0f));
       bias[j] = fmaf(qv[j], mn, bias[j]);
     } else {
-      U[j] = 0x800000u;  // X = 0
+      U[j] = 0x400000u;  // X = 0
     }
   }
   uint4 c0, c1;
@@ -229,7 +232,10 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
   extern __shared__ __align__(1024) unsigned char smem[];
   const lf_layout& L = p.L;
   const TcSmem S = tc_smem(L);
-  const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
+  // Grid: x = (sequence, KV head) pair, y = split.  Blocks launch in x-fastest
+  // order, so every pair's first splits start together and the short residual
+  // splits (the last y) take the SMs the page splits leave.
+  const int s = blockIdx.y, h = blockIdx.x % p.L.kv_heads, b = blockIdx.x / p.L.kv_heads, tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
   const int H = L.kv_heads, R = L.row_words, M = L.meta_halves;
   const int pages = p.hist_tokens[b] / kP;
@@ -257,10 +263,10 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S.bars + 8 * kNumBars);
   volatile int* abort_s = reinterpret_cast<volatile int*>(smem + S.bars + 8 * kNumBars + 4);
   uint32_t* red_m = reinterpret_cast<uint32_t*>(smem + S.red);  // [stage][warp][16]: 8 score keys, vscale
-  float* red_b = reinterpret_cast<float*>(smem + S.redb);        // [stage][warp][8] bias partials
+  float* red_b = reinterpret_cast<float*>(smem + S.redb);        // [stage][5][8] bias partials
   float* q16_s = reinterpret_cast<float*>(smem + S.q16);         // [FP16 slot][kGQ], times scaling*log2(e)
-  float* qhi_s = reinterpret_cast<float*>(smem + S.qhi);         // K positions t + 128: q_j[c] 2^(22-Eq)
-  int* posoff_s = reinterpret_cast<int*>(smem + S.posoff);       // K positions t + 128: scale | min << 16, or -1
+  float* qhi_s = reinterpret_cast<float*>(smem + S.qhi);         // K positions 128..: q_j[c] 2^(21-Eq)
+  int* posoff_s = reinterpret_cast<int*>(smem + S.posoff);       // K positions 128..: scale | min << 16, or -1
   unsigned char* stage0 = smem + S.stage0;
   unsigned char* bqk = smem + S.bqk;
   unsigned char* bpv = smem + S.bpv;
@@ -272,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
   const int64_t head_meta = (static_cast<int64_t>(b) * H + h) * L.group_cap;
   const float c2 = p.scaling * kLog2e;
   const int kmax_off = L.kmax_off;
-  const bool has_hi = tid < S.kpad - kDecThreads;  // compute thread with a second K position (warp-uniform)
+  const int n_hi = S.kpad > kDecThreads ? (S.kpad - kDecThreads) / 32 : 0;  // K positions per control lane
 
   // Page pg of the item -> stage pg % 2 (row block + meta row); one thread.
   auto issue_page = [&](int pg) {
@@ -288,14 +294,13 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     for (int i = 0; i < kStages; ++i) mbar_init(&bars[kBarFull + i], 1);
     mbar_init(&bars[kBarKReady], kDecThreads);
     mbar_init(&bars[kBarVReady], kDecThreads);
-    mbar_init(&bars[kBarQK], 1);
+    mbar_init(&bars[kBarQK], 2);  // the QK commit + the control warp's arrive after its B rows
     mbar_init(&bars[kBarPV], 1);
     *abort_s = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
-    // The first two pages load while the CTA stages its query.
+    // The first page loads while the CTA stages its query.
     issue_page(0);
-    if (npg > 1) issue_page(1);
   }
   if (warp == 4) {
     tmem_alloc(tmem_slot, S.tm_cols);
@@ -336,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     named_sync(1, kDecThreads);
     const uint32_t mx = max(max(red_m[0], red_m[1]), max(red_m[2], red_m[3]));
     eq = max(-60, min(60, exp2_ceil(__uint_as_float(mx))));
-    const float qscale = exp2i(22 - eq);
+    const float qscale = exp2i(21 - eq);
     if (e >= 0) {
       const int tier = (e >> 16) & 3, slot = e >> 18, ch = e & 0xFFFF;
       po = (L.scale_off[tier] + slot) | ((L.min_off[tier] + slot) << 16);
@@ -346,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
 #pragma unroll
       for (int j = 0; j < kGQ; ++j) qq[j] = 0.f;
     }
-    // Second K positions t + 128 (wide layouts), kept in shared memory.
+    // K positions 128.. (wide layouts): built by the control warp.
     for (int pp = kDecThreads + tid; pp < S.kpad; pp += kDecThreads) {
       const int e2 = kpos_entry(L, p.slot_chan, h, pp);
       const int r = pp - kDecThreads;
@@ -364,6 +369,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       const int ch = p.slot_chan[(3 * H + h) * kD + c];
       q16_s[i] = ch < 0 ? 0.f : q_s[j * kD + ch] * c2;
     }
+    if (tid < 2 * 5 * kGQ) red_b[tid] = 0.f;  // the control slots stay zero without K positions 128..
   }
   tc_fence_before();
   __syncthreads();
@@ -373,11 +379,54 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
 
   if (warp == 4) {
     // ------------------------------------------------------------ control warp
-    int issued0 = 1, issued1 = npg > 1 ? 1 : 0, qk_open = 0, pv_open = 0;
+    auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+      if (*abort_s) return;
+      if (!mbar_wait_bounded(bar, parity, kLimit)) *abort_s = 1;
+    };
+    // B rows of K positions 128.. for page pg (none for narrow layouts) and
+    // their bias partials, then the release arrive on the QK barrier.  The
+    // proxy fence here also waits for this warp's own copies and MMAs still in
+    // flight, so it runs only when they have all completed: after the page's
+    // copy has landed and QK(pg - 1) has finished, before PV(pg - 1) is issued.
+    auto build_hi = [&](int pg) {
+      if (n_hi > 0) {
+        const uint16_t* meta = reinterpret_cast<const uint16_t*>(stage0 + (pg & 1) * S.stage_bytes + S.rows_bytes);
+        const float fsc = exp2i(-page_scale_exp(meta, kmax_off));
+        float bias[kGQ];
+#pragma unroll
+        for (int j = 0; j < kGQ; ++j) bias[j] = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (k >= n_hi) break;
+          const int r = 32 * k + lane;
+          const int o = posoff_s[r];
+          const float4 qa = *reinterpret_cast<const float4*>(qhi_s + r * kGQ);
+          const float4 qb = *reinterpret_cast<const float4*>(qhi_s + r * kGQ + 4);
+          const float qv[kGQ] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+          const float sc = o >= 0 ? half_bits_to_float(meta[o & 0xFFFF]) * fsc : 0.f;
+          const float mn = o >= 0 ? half_bits_to_float(meta[o >> 16]) : 0.f;
+          qk_b_row<GQ>(bqk, S.bqk_sbo, kDecThreads + r, qv, sc, mn, bias);
+        }
+        const float part = warp_sum8_scatter(bias, lane);
+        if ((lane & 3) == 0)
+          red_b[(pg & 1) * 40 + 32 + (((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1))] = part;
+        fence_proxy_async_smem();
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[kBarQK]);
+    };
+
+    int issued0 = 1, issued1 = 0, qk_open = 0, pv_open = 0;
     const uint32_t n_ks = static_cast<uint32_t>(S.kpad / 32);
     const uint64_t bqk_desc0 = smem_desc(bqk, 128, S.bqk_sbo);
     const uint64_t apv_desc0 = smem_desc(apv, 128, 2048);
     const uint64_t bpv_desc0 = smem_desc(bpv, 128, 2048);
+    if (n_hi > 0) wait_all(&bars[kBarFull], 0);
+    build_hi(0);
+    if (lane == 0 && npg > 1) {
+      issue_page(1);
+      issued1 = 1;
+    }
     for (int i = 0; i < npg; ++i) {
       if (lane == 0) {
         if (!*abort_s && !mbar_wait_bounded(&bars[kBarKReady], i & 1, kLimit)) *abort_s = 1;
@@ -386,6 +435,14 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
           mma_u8_ts(tmem + S.tm_qk, tmem + 8 * ks, bqk_desc0 + 32 * ks, kIdescQK, ks > 0 ? 1u : 0u);
         mma_commit(&bars[kBarQK]);
         qk_open = i + 1;
+      }
+      __syncwarp();
+      if (i + 1 < npg) {
+        if (n_hi > 0) wait_all(&bars[kBarFull + ((i + 1) & 1)], ((i + 1) >> 1) & 1);
+        wait_all(&bars[kBarQK], i & 1);  // QK(i) has read the B rows; phase i + 1 may start
+        build_hi(i + 1);
+      }
+      if (lane == 0) {
         if (!*abort_s && !mbar_wait_bounded(&bars[kBarVReady], i & 1, kLimit)) *abort_s = 1;
         tc_fence_after();
 #pragma unroll
@@ -393,12 +450,13 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
           mma_u8_ss(tmem + S.tm_pv, apv_desc0 + 32 * ks, bpv_desc0 + 32 * ks, kIdescPV, ks > 0 ? 1u : 0u);
         mma_commit(&bars[kBarPV]);
         pv_open = i + 1;
-        // Stage i % 2 has been read by U_K(i), S(i) and U_V(i): it takes page i + 2.
+        // Stage i % 2 has been read by U_K(i), S(i), U_V(i) and build_hi(i): it takes page i + 2.
         if (i + kStages < npg && !*abort_s) {
           issue_page(i + kStages);
           if (i & 1) ++issued1; else ++issued0;
         }
       }
+      __syncwarp();
     }
     if (lane == 0 && *abort_s) {
       // Drain this CTA's copies and MMAs before its shared memory and TMEM go away.
@@ -428,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     const int rk = (tid >> 2) & 3;               // PV row t carries code * 4^rk
     const bool has_pos = tid < S.kpad;           // warp-uniform (K padded to 32)
     const int soff = po >= 0 ? (po & 0xFFFF) : 0, moff = po >= 0 ? (po >> 16) : 0;
-    const float cf = c2 * exp2i(eq - 22);        // fixed-point unit 2^(Eq-22) -> log2-scaled score
+    const float cf = c2 * exp2i(eq - 21);        // fixed-point unit 2^(Eq-21) -> log2-scaled score
     const int bslot = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
 
     // U_K(i): Key codes of the thread's token -> its TMEM lane (A of QK); the
@@ -470,19 +528,10 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
 #pragma unroll
         for (int j = 0; j < kGQ; ++j) bias[j] = 0.f;
         qk_b_row<GQ>(bqk, S.bqk_sbo, tid, qq, sc, mn, bias);
-        if (has_hi) {
-          const int o = posoff_s[tid];
-          const float4 qa = *reinterpret_cast<const float4*>(qhi_s + tid * kGQ);
-          const float4 qb = *reinterpret_cast<const float4*>(qhi_s + tid * kGQ + 4);
-          const float qv[kGQ] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-          const float sc2 = o >= 0 ? half_bits_to_float(meta[o & 0xFFFF]) * fsc : 0.f;
-          const float mn2 = o >= 0 ? half_bits_to_float(meta[o >> 16]) : 0.f;
-          qk_b_row<GQ>(bqk, S.bqk_sbo, kDecThreads + tid, qv, sc2, mn2, bias);
-        }
         const float part = warp_sum8_scatter(bias, lane);
-        if ((lane & 3) == 0) red_b[(i & 1) * 32 + warp * kGQ + bslot] = part;
+        if ((lane & 3) == 0) red_b[(i & 1) * 40 + warp * kGQ + bslot] = part;
       } else if ((lane & 3) == 0) {
-        red_b[(i & 1) * 32 + warp * kGQ + bslot] = 0.f;
+        red_b[(i & 1) * 40 + warp * kGQ + bslot] = 0.f;
       }
       tmem_wait_st();
       fence_proxy_async_smem();
@@ -532,13 +581,13 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       tc_fence_after();
       uint32_t a[32];
       tmem_ld_x32_sync(tm_a + S.tm_qk, a);
-      const int ones128 = static_cast<int>(a[24]) * 128;
+      const int ones64 = static_cast<int>(a[24]) * 64;  // offset 2^22 = 64 * 65536 per unit of code
       float x[GQ];
       uint32_t key[GQ];
 #pragma unroll
       for (int j = 0; j < GQ; ++j) {
         const uint32_t lo = a[j] + (a[8 + j] << 8);
-        const int hi = static_cast<int>(a[16 + j]) - ones128;
+        const int hi = static_cast<int>(a[16 + j]) - ones64;
         x[j] = fmaf(static_cast<float>(hi), f16, fmaf(static_cast<float>(lo), f, s16[j]));
         key[j] = __reduce_max_sync(0xffffffffu, order_key(x[j]));
       }
@@ -552,8 +601,8 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       named_sync(1, kDecThreads);
       // Lane j (mod 8): statistics of q-head j.  The bias is the same for
       // every token of the page, so the page max is max(score) + bias.
-      const float* rb = red_b + st * 32 + l8;
-      const float bias = ((rb[0] + rb[8]) + (rb[16] + rb[24])) * cf;
+      const float* rb = red_b + st * 40 + l8;
+      const float bias = ((rb[0] + rb[8]) + (rb[16] + rb[24]) + rb[32]) * cf;
       const uint32_t km = max(max(rm[l8], rm[16 + l8]), max(rm[32 + l8], rm[48 + l8]));
       const uint32_t vk = max(max(rm[8], rm[24]), max(rm[40], rm[56]));
       const float mnew = fmaxf(m_l, order_key_to_float(km) + bias);
@@ -578,8 +627,9 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
           const float pj = ex2(x[j] + __shfl_sync(0xffffffffu, off, j));
           lt[j] += pj;
           lvt[j] = fmaf(pj, vm, lvt[j]);
-          // rint(p * vs * 2^(23 - Ev)) via the fp32 magic constant 2^23.
-          U[j] = __float_as_uint(fmaf(pj, vsc, 8388608.0f)) - 0x4B000000u;
+          // Y = rint(p * vs * 2^(23 - Ev)) in [0, 2^23]: the low 24 bits of the
+          // fp32 sum 2^23 + Y are Y (2^24 itself has low bits 2^23).
+          U[j] = __float_as_uint(fmaf(pj, vsc, 8388608.0f));
         } else {
           U[j] = 0u;
         }
@@ -668,22 +718,34 @@ static cudaError_t configure_tc(void* kern, int smem_bytes) {
                               cudaSharedmemCarveoutMaxShared);
 }
 
+// Resident CTAs per SM from the kernel's own limits: registers, shared memory
+// (with the per-block reservation), threads and TMEM columns.  The runtime's
+// occupancy query answers 1 for this kernel while the hardware runs four of
+// its CTAs on one SM (observed with per-CTA SM ids and timestamps), so it is
+// not used.
 int occupancy_tc(const lf_layout& L, int gq, int pps) {
   (void)pps;  // the stage holds one page's meta row: shared memory does not depend on pps
   const tc::TcSmem S = tc::tc_smem(L);
   if (S.total > 227 * 1024) return 0;
   void* kern = tc_kernel_for(gq);
-  if (configure_tc(kern, S.total) != cudaSuccess) {
+  cudaFuncAttributes fa;
+  int dev = 0, smem_sm = 0, reserved = 0, regs_sm = 0, threads_sm = 0;
+  if (configure_tc(kern, S.total) != cudaSuccess || cudaFuncGetAttributes(&fa, kern) != cudaSuccess ||
+      cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&threads_sm, cudaDevAttrMaxThreadsPerMultiProcessor, dev) != cudaSuccess) {
     cudaGetLastError();
     return -1;
   }
-  int blocks = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kern, tc::kThreads, S.total) != cudaSuccess) {
-    cudaGetLastError();
-    return -1;
-  }
-  const int by_tmem = 512 / S.tm_cols;
-  return blocks < by_tmem ? blocks : by_tmem;
+  const int warps = tc::kThreads / 32;
+  const int regs_warp = (fa.numRegs * 32 + 255) / 256 * 256;  // allocated per warp in units of 256
+  int blocks = regs_sm / (warps * regs_warp);
+  blocks = std::min(blocks, smem_sm / (S.total + reserved));
+  blocks = std::min(blocks, threads_sm / tc::kThreads);
+  blocks = std::min(blocks, 512 / S.tm_cols);
+  return std::max(blocks, 0);
 }
 
 int launch_partial_tc(const DecodeParams& p, int resid_dtype, int q_dtype, cudaStream_t stream) {
@@ -701,7 +763,7 @@ int launch_partial_tc(const DecodeParams& p, int resid_dtype, int q_dtype, cudaS
     }
     configured[q.gq].store(S.total);
   }
-  dim3 grid(q.max_splits, q.L.kv_heads, q.batch);
+  dim3 grid(q.L.kv_heads * q.batch, q.max_splits);
   void* args[] = {&q};
   cudaError_t e = cudaLaunchKernel(kern, grid, dim3(tc::kThreads), args, S.total, stream);
   if (e != cudaSuccess) {

@@ -14,14 +14,16 @@ import torch
 from logitfill_b200 import _lib
 from logitfill_b200.packed.cache import PackedKVCache, PackedKVManager
 
-MAX_PAGES_PER_SPLIT = 16  # the tensor-core kernel stages one item's Key meta rows in shared memory
+MAX_PAGES_PER_SPLIT = 64  # largest work item the tensor-core kernel accepts
 
 
 def pages_per_split(cache: PackedKVCache, layer_idx: int = 0) -> int:
     """Pages per K2 work item.  Every (sequence, KV head) history is cut into
-    ceil(pages / pps) items, plus up to ceil(page/32) residual items; the
-    choice minimises (waves of resident CTAs) x (pages per item), i.e. it
-    balances the grid over the SMs instead of just making it large."""
+    ceil(pages / pps) items, plus up to ceil(page/32) short residual items
+    that launch after all of them.  An item costs about pps pages plus a fixed
+    start (query staging, first copy) worth ~1.5 pages; the choice minimises
+    (waves of resident CTAs) x (pps + 1.5), i.e. it balances the page items
+    over the SMs instead of just making the grid large."""
     layer = cache.layers[layer_idx]
     P = cache.page_size
     pages = int(layer.hist_len.max()) // P if layer.hist_len.size else 0
@@ -30,16 +32,15 @@ def pages_per_split(cache: PackedKVCache, layer_idx: int = 0) -> int:
     so = _lib.lib()
     sms = torch.cuda.get_device_properties(cache.device).multi_processor_count
     pairs = cache.batch * cache.n_kv
-    resid = sum(-(-(int(t) + 1) // 32) for t in layer.tail_len) * cache.n_kv
     best, best_cost = 1, None
     for pps in range(1, min(pages, MAX_PAGES_PER_SPLIT) + 1):
         occ = so.lf_decode_occupancy(ctypes.byref(layer.layout.c), cache.n_q, pps)
         if occ <= 0:
             continue
         ctas = pairs * (-(-pages // pps))
-        waves = -(-(ctas + resid // 4) // (sms * occ))
-        cost = waves * pps + 0.05 * (-(-pages // pps))
-        if best_cost is None or cost < best_cost:
+        waves = -(-ctas // (sms * occ))
+        cost = waves * (pps + 1.5)
+        if best_cost is None or cost < best_cost - 1e-9:
             best, best_cost = pps, cost
     return best
 

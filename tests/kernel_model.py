@@ -4,11 +4,11 @@ The sm_100a decode kernel (K2) runs both contractions of a packed page on the
 INT8 tensor cores (``tcgen05.mma.kind::i8``):
 
 * QK: integer Key codes (u8, 0..255) times the per-page products
-  ``q_j[c] * scale_c`` written as 24-bit fixed point ``X`` relative to a
-  power-of-two block exponent (one per query group and page), offset by 2^23
+  ``q_j[c] * scale_c`` written as fixed point ``X`` (|X| <= 2^21) relative to
+  a power-of-two block exponent (one per query group and page), offset by 2^22
   so the three limbs (bytes) are unsigned.  A column of ones in the B operand
   returns sum_c code_c, which removes the offset exactly:
-  ``acc0 + 256 acc1 + 65536 (acc2 - 128 ones)``.
+  ``acc0 + 256 acc1 + 65536 (acc2 - 64 ones)``.
 * PV: integer Value codes (u8, 0..3) times ``p_t * vscale_t`` written as 23-bit
   unsigned fixed point (three limbs) relative to a per-page exponent (the page's
   largest Value scale: p <= 1 after the max update).
@@ -31,7 +31,7 @@ def _exp2_ceil(x: np.ndarray) -> np.ndarray:
 
 
 def model_attention(layer: orc.OracleLayer, query: np.ndarray, key_new, value_new, scaling: float,
-                    qk_bits: int = 22, pv_bits: int = 23) -> np.ndarray:
+                    qk_bits: int = 21, pv_bits: int = 23) -> np.ndarray:
     """Decode attention of ``query`` ``[n_q, D]`` over ``layer`` (page size 128,
     k_group 128, v_group D) computed with the kernel's fixed-point scheme for
     the packed history and fp32 for the residual.  Returns ``[n_q, D]``."""
@@ -71,10 +71,11 @@ def model_attention(layer: orc.OracleLayer, query: np.ndarray, key_new, value_ne
                 qq = (q[:, idx] * np.ldexp(np.float32(1), (qk_bits - eq))[:, None]).astype(np.float32)
                 sp = (sc * np.float32(2.0 ** -esc)).astype(np.float32)
                 X = np.rint((qq * sp[None, :]).astype(np.float32)).astype(np.int64)   # [gq, cnt]
-                U = X + (1 << 23)
+                U = X + (1 << (qk_bits + 1))
+                assert U.min() >= 0 and U.max() < (1 << 24)
                 acc = [codes.astype(np.int64) @ ((U >> (8 * k)) & 0xFF).T for k in range(3)]
                 ones = codes.astype(np.int64).sum(axis=1)[:, None]
-                s_int += acc[0] + 256.0 * acc[1] + 65536.0 * (acc[2] - 128 * ones)
+                s_int += acc[0] + 256.0 * acc[1] + 65536.0 * acc[2] - float(1 << (qk_bits + 1)) * ones
                 bias += (q[:, idx].astype(np.float64) @ mn.astype(np.float64))
             scale_qk = np.ldexp(1.0, eq + esc - qk_bits)            # per q-head
             s = s_int * scale_qk[None, :] + bias[None, :]
