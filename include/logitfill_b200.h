@@ -161,6 +161,7 @@ LF_API int lf_decode_partial(const lf_layout* layout, const int32_t* rows, const
  * K3: merge the split partials into the attention output
  * out [batch][n_q][D] (strides out_seq_stride, out_head_stride), dtype out_dtype.
  * Softmax-exact: out = sum_s e^(m_s - M) acc_s / sum_s e^(m_s - M) l_s.
+ * head_dim must be even (the partials are read two channels at a time).
  */
 LF_API int lf_decode_merge(const float* workspace, const int32_t* hist_tokens, int batch, int kv_heads,
                     int n_q, int head_dim, int page_size, int pages_per_split, int max_splits,

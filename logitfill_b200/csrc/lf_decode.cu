@@ -230,33 +230,62 @@ decode_partial_simt(DecodeParams p) {
   write_partial(p, b, h, s, tid, acc, m, lt, lvt, red);
 }
 
+// K3: one warp per (sequence, q-head).  Lane s (mod 32) reads split s's max
+// and sum; the global max, the weights exp(m_s - M) and the normaliser are
+// warp reductions; then every lane accumulates two channels per 64 over all
+// splits, the weight of split s broadcast from the lane that computed it.
+// The partial records (GQ x (D + 2) floats) are 8-byte aligned, so the
+// values are read as float2.
+constexpr int kMergeWarps = 4;
+
 template <typename OT>
-__global__ void __launch_bounds__(128)
-decode_merge_kernel(const float* __restrict__ ws, const int32_t* __restrict__ hist_tokens,
+__global__ void __launch_bounds__(kMergeWarps * 32)
+decode_merge_kernel(const float* __restrict__ ws, const int32_t* __restrict__ hist_tokens, int batch,
                     int kv_heads, int n_q, int D, int P, int pps, int max_splits, OT* __restrict__ out,
                     int64_t out_seq_stride, int64_t out_head_stride) {
-  const int b = blockIdx.x, qh = blockIdx.y;
+  const int lane = threadIdx.x & 31;
+  const int task = blockIdx.x * kMergeWarps + (threadIdx.x >> 5);
+  if (task >= batch * n_q) return;
+  const int b = task / n_q, qh = task - b * n_q;
   const int GQ = n_q / kv_heads, h = qh / GQ, j = qh - h * GQ;
   const int pages = hist_tokens[b] / P;
-  const int n_s = (pages + pps - 1) / pps + residual_splits(P);
-  const float* base = ws + (static_cast<int64_t>(b) * kv_heads + h) * max_splits * (GQ * (D + 2));
-  const int item = GQ * (D + 2);
+  const int n_s = min((pages + pps - 1) / pps + residual_splits(P), max_splits);
+  const int64_t item = static_cast<int64_t>(GQ) * (D + 2);
+  const float* base = ws + (static_cast<int64_t>(b) * kv_heads + h) * max_splits * item;
+  const float* mstat = base + static_cast<int64_t>(GQ) * D + j;  // split s: mstat[s * item], lstat[s * item]
   float M = -INFINITY;
-  for (int s = 0; s < n_s; ++s) M = fmaxf(M, base[s * item + GQ * D + j]);
-  float L = 0.f;
-  for (int s = 0; s < n_s; ++s) {
-    const float ms = base[s * item + GQ * D + j];
-    if (ms != -INFINITY) L += expf(ms - M) * base[s * item + GQ * D + GQ + j];
+  for (int s = lane; s < n_s; s += 32) M = fmaxf(M, mstat[s * item]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  float Lsum = 0.f;
+  for (int s = lane; s < n_s; s += 32) {
+    const float ms = mstat[s * item];
+    if (ms != -INFINITY) Lsum = fmaf(expf(ms - M), mstat[s * item + GQ], Lsum);
   }
-  const float inv = L > 0.f ? 1.0f / L : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, o);
+  const float inv = Lsum > 0.f ? 1.0f / Lsum : 0.f;
   OT* o = out + b * out_seq_stride + qh * out_head_stride;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float a = 0.f;
-    for (int s = 0; s < n_s; ++s) {
-      const float ms = base[s * item + GQ * D + j];
-      if (ms != -INFINITY) a = fmaf(expf(ms - M), base[s * item + j * D + d], a);
+  const float* vals = base + static_cast<int64_t>(j) * D;
+  for (int d0 = 2 * lane; d0 < D; d0 += 64) {
+    float a0 = 0.f, a1 = 0.f;
+    for (int s0 = 0; s0 < n_s; s0 += 32) {
+      float wl = 0.f;
+      if (s0 + lane < n_s) {
+        const float ms = mstat[(s0 + lane) * item];
+        wl = ms == -INFINITY ? 0.f : expf(ms - M);
+      }
+      const int cnt = min(32, n_s - s0);
+#pragma unroll 4
+      for (int k = 0; k < cnt; ++k) {
+        const float w = __shfl_sync(0xffffffffu, wl, k);
+        const float2 v = *reinterpret_cast<const float2*>(vals + (s0 + k) * item + d0);
+        a0 = fmaf(w, v.x, a0);
+        a1 = fmaf(w, v.y, a1);
+      }
     }
-    Scalar<OT>::store(o + d, a * inv);
+    Scalar<OT>::store(o + d0, a0 * inv);
+    Scalar<OT>::store(o + d0 + 1, a1 * inv);
   }
 }
 
@@ -416,26 +445,26 @@ extern "C" int lf_decode_merge(const float* workspace, const int32_t* hist_token
   LF_CHECK_ARG(workspace && hist_tokens && out, "lf_decode_merge: null pointer");
   LF_CHECK_ARG(batch > 0 && batch <= 65535 && kv_heads > 0 && n_q % kv_heads == 0 && n_q <= 65535,
                "lf_decode_merge: batch %d n_q %d kv_heads %d", batch, n_q, kv_heads);
-  LF_CHECK_ARG(page_size > 0 && pages_per_split > 0 && max_splits > 0 && head_dim > 0,
+  LF_CHECK_ARG(page_size > 0 && pages_per_split > 0 && max_splits > 0 && head_dim > 0 && head_dim % 2 == 0,
                "lf_decode_merge: bad sizes");
-  dim3 grid(batch, n_q);
+  const int tasks = batch * n_q;
+  const dim3 grid((tasks + lf::kMergeWarps - 1) / lf::kMergeWarps);
+  const dim3 block(lf::kMergeWarps * 32);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (out_dtype) {
     case LF_F32:
-      lf::decode_merge_kernel<float><<<grid, 128, 0, s>>>(workspace, hist_tokens, kv_heads, n_q, head_dim,
-                                                          page_size, pages_per_split, max_splits,
-                                                          static_cast<float*>(out), out_seq_stride,
-                                                          out_head_stride);
+      lf::decode_merge_kernel<float><<<grid, block, 0, s>>>(workspace, hist_tokens, batch, kv_heads, n_q, head_dim,
+                                                            page_size, pages_per_split, max_splits,
+                                                            static_cast<float*>(out), out_seq_stride, out_head_stride);
       break;
     case LF_F16:
-      lf::decode_merge_kernel<__half><<<grid, 128, 0, s>>>(workspace, hist_tokens, kv_heads, n_q, head_dim,
-                                                           page_size, pages_per_split, max_splits,
-                                                           static_cast<__half*>(out), out_seq_stride,
-                                                           out_head_stride);
+      lf::decode_merge_kernel<__half><<<grid, block, 0, s>>>(workspace, hist_tokens, batch, kv_heads, n_q, head_dim,
+                                                             page_size, pages_per_split, max_splits,
+                                                             static_cast<__half*>(out), out_seq_stride, out_head_stride);
       break;
     case LF_BF16:
-      lf::decode_merge_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(
-          workspace, hist_tokens, kv_heads, n_q, head_dim, page_size, pages_per_split, max_splits,
+      lf::decode_merge_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(
+          workspace, hist_tokens, batch, kv_heads, n_q, head_dim, page_size, pages_per_split, max_splits,
           static_cast<__nv_bfloat16*>(out), out_seq_stride, out_head_stride);
       break;
     default:

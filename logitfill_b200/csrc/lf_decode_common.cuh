@@ -184,7 +184,7 @@ __device__ __forceinline__ void load_vec_to_float_rt(const void* src, int dtype,
   }
 }
 
-static __device__ __noinline__ void residual_chunk(const DecodeParams& p, int b, int h, int chunk, const float* q_s,
+static __device__ __forceinline__ void residual_chunk(const DecodeParams& p, int b, int h, int chunk, const float* q_s,
                                             unsigned char* region, float (&m)[kGQ], float (&acc)[kGQ],
                                             float (&lt)[kGQ]) {
   const int RS_ = p.resid_dtype == LF_F32 ? 4 : 2;  // element size

@@ -312,7 +312,11 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
   if (tid < kDecThreads) {
     // Query group (thread = channel), its block exponent Eq
     // (max_j,c |q_j[c]| <= 2^Eq), and the scaled query of each K position.
+    // Every global load of the prologue is issued here, before any use.
     const int e = tid < S.kpad ? kpos_entry(L, p.slot_chan, h, tid) : -1;
+    const int e2 = kDecThreads + tid < S.kpad ? kpos_entry(L, p.slot_chan, h, kDecThreads + tid) : -1;
+    const int n16 = L.width[3] * kGQ;
+    const int ch16 = tid < n16 ? p.slot_chan[(3 * H + h) * kD + tid / kGQ] : -1;
     float qc[kGQ];
     {
       const int64_t base = b * p.q_seq_stride + static_cast<int64_t>(h) * p.gq * p.q_head_stride + tid;
@@ -351,23 +355,22 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
 #pragma unroll
       for (int j = 0; j < kGQ; ++j) qq[j] = 0.f;
     }
-    // K positions 128.. (wide layouts): built by the control warp.
-    for (int pp = kDecThreads + tid; pp < S.kpad; pp += kDecThreads) {
-      const int e2 = kpos_entry(L, p.slot_chan, h, pp);
-      const int r = pp - kDecThreads;
+    // K positions 128.. (wide layouts, K <= 256): built by the control warp.
+    if (kDecThreads + tid < S.kpad) {
       int po2 = -1;
       if (e2 >= 0) {
         const int tier = (e2 >> 16) & 3, slot = e2 >> 18;
         po2 = (L.scale_off[tier] + slot) | ((L.min_off[tier] + slot) << 16);
       }
 #pragma unroll
-      for (int j = 0; j < kGQ; ++j) qhi_s[r * kGQ + j] = e2 >= 0 ? q_s[j * kD + (e2 & 0xFFFF)] * qscale : 0.f;
-      posoff_s[r] = po2;
+      for (int j = 0; j < kGQ; ++j) qhi_s[tid * kGQ + j] = e2 >= 0 ? q_s[j * kD + (e2 & 0xFFFF)] * qscale : 0.f;
+      posoff_s[tid] = po2;
     }
-    for (int i = tid; i < L.width[3] * kGQ; i += kDecThreads) {
-      const int c = i / kGQ, j = i % kGQ;
-      const int ch = p.slot_chan[(3 * H + h) * kD + c];
-      q16_s[i] = ch < 0 ? 0.f : q_s[j * kD + ch] * c2;
+    // FP16-tier query values (times scaling * log2 e), slot-major.
+    if (tid < n16) q16_s[tid] = ch16 < 0 ? 0.f : q_s[(tid % kGQ) * kD + ch16] * c2;
+    for (int i = tid + kDecThreads; i < n16; i += kDecThreads) {
+      const int ch = p.slot_chan[(3 * H + h) * kD + i / kGQ];
+      q16_s[i] = ch < 0 ? 0.f : q_s[(i % kGQ) * kD + ch] * c2;
     }
     if (tid < 2 * 5 * kGQ) red_b[tid] = 0.f;  // the control slots stay zero without K positions 128..
   }
