@@ -192,6 +192,15 @@ LF_API int lf_decode_noalloc(const lf_layout* layout, const int32_t* rows, const
                              int64_t out_seq_stride, int64_t out_head_stride, int32_t* status,
                              lf_stream_t stream);
 
+/*
+ * Self-test of the bounded device-side wait used on every mbarrier of the
+ * decode kernels (no counterpart in the reference).  One thread waits, with
+ * limit_ns, for a barrier phase that completes only when arrive != 0; it
+ * writes LF_OK, or LF_ERR_DEVICE_TIMEOUT once the limit runs out, to *status
+ * (device int32) and returns.  No fault, trap or hang in either case.
+ */
+LF_API int lf_selftest_wait(int32_t* status, int64_t limit_ns, int arrive, lf_stream_t stream);
+
 /* Human-readable text of a status code; detail of the last failure on this thread. */
 LF_API const char* lf_status_string(int status);
 LF_API const char* lf_last_error(void);

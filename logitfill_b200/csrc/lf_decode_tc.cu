@@ -10,9 +10,10 @@
 // positions 128 and up (wide layouts) between its PV issue and the next copy:
 // a proxy fence in the thread that issued a bulk copy waits for that copy.
 // Compute warps, per page i:
-//   U_K  Key codes -> u8 in TMEM (A of QK, K-major); the B row of QK for K
-//        position t (tier slot c): for each q-head j the fixed point
-//        X = rint(q_j[c] scale_c 2^(21-Eq-Es)), offset by 2^22 and split into
+//   U_K  Key codes -> u8 in TMEM (A of QK, K-major), masked in place (INT2
+//        slot k of a byte as code * 4^k, INT4 as code * 16^k); the B row of QK
+//        for K position t (tier slot c, code weight w_c): for each q-head j the
+//        fixed point X = rint(q_j[c] scale_c 2^(21-Eq-Es) / w_c), offset by 2^22 and split into
 //        three unsigned limbs, plus a one in the ones column; Es is the page's
 //        Key-scale exponent, from the largest scale the packer stores in the
 //        meta row; partial sums of the Key-min bias sum_c q_j[c] min_c.
@@ -28,8 +29,9 @@
 // Order: S(i), U_K(i+1), C(i), U_V(i+1).  QK(i+1) overlaps C(i) and U_V(i+1),
 // PV(i) overlaps U_K(i+1).
 //
-// The integer products are exact; the fixed-point rounding is 2^-21 (QK) and
-// 2^-23 (PV) of the block maxima (tests/kernel_model.py models it).  Every
+// The integer products are exact; the fixed-point rounding is 2^-21 w_c (QK,
+// w_c <= 64) and 2^-23 (PV) of the block maxima (tests/kernel_model.py models
+// it).  Every
 // mbarrier wait is bounded (2 s).  On expiry the CTA records
 // LF_ERR_DEVICE_TIMEOUT, stops waiting (every warp still passes the same
 // barriers, so nothing deadlocks), drains its own copies and MMAs, frees its
@@ -222,6 +224,22 @@ __device__ __forceinline__ void qk_b_row(unsigned char* bqk, int sbo, int pp, co
   *reinterpret_cast<uint4*>(dst + sbo) = c1;
 }
 
+// K position descriptor: meta offsets of the slot's scale and min, and the
+// power of two its unpacked code carries.  The Key codes are masked in place
+// without shifting, so INT2 slot 4i + k of a word reaches the MMA as
+// code * 4^k and INT4 slot 2i + k as code * 16^k; the B row divides by the
+// same power of two (exact in fp32) and the min, multiplied back, keeps the
+// bias exact.
+__device__ __forceinline__ int pos_desc(const lf_layout& L, int e) {
+  if (e < 0) return -1;
+  const int tier = (e >> 16) & 3, slot = e >> 18;
+  const int lg = tier == 0 ? 2 * (slot & 3) : tier == 1 ? 4 * (slot & 1) : 0;
+  return (L.scale_off[tier] + slot) | ((L.min_off[tier] + slot) << 13) | (lg << 26);
+}
+__device__ __forceinline__ int pos_scale(int po) { return po & 0x1FFF; }
+__device__ __forceinline__ int pos_min(int po) { return (po >> 13) & 0x1FFF; }
+__device__ __forceinline__ int pos_lg(int po) { return (po >> 26) & 7; }
+
 // The page's Key-scale exponent: largest stored INT2/INT4/INT8 scale <= 2^Es.
 __device__ __forceinline__ int page_scale_exp(const uint16_t* meta, int kmax_off) {
   return max(-60, min(60, exp2_ceil(half_bits_to_float(meta[kmax_off]))));
@@ -346,24 +364,16 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     const uint32_t mx = max(max(red_m[0], red_m[1]), max(red_m[2], red_m[3]));
     eq = max(-60, min(60, exp2_ceil(__uint_as_float(mx))));
     const float qscale = exp2i(21 - eq);
-    if (e >= 0) {
-      const int tier = (e >> 16) & 3, slot = e >> 18, ch = e & 0xFFFF;
-      po = (L.scale_off[tier] + slot) | ((L.min_off[tier] + slot) << 16);
+    po = pos_desc(L, e);
+    const float qs1 = po >= 0 ? qscale * exp2i(-pos_lg(po)) : 0.f;
 #pragma unroll
-      for (int j = 0; j < kGQ; ++j) qq[j] = q_s[j * kD + ch] * qscale;
-    } else {
-#pragma unroll
-      for (int j = 0; j < kGQ; ++j) qq[j] = 0.f;
-    }
+    for (int j = 0; j < kGQ; ++j) qq[j] = e >= 0 ? q_s[j * kD + (e & 0xFFFF)] * qs1 : 0.f;
     // K positions 128.. (wide layouts, K <= 256): built by the control warp.
     if (kDecThreads + tid < S.kpad) {
-      int po2 = -1;
-      if (e2 >= 0) {
-        const int tier = (e2 >> 16) & 3, slot = e2 >> 18;
-        po2 = (L.scale_off[tier] + slot) | ((L.min_off[tier] + slot) << 16);
-      }
+      const int po2 = pos_desc(L, e2);
+      const float qs2 = po2 >= 0 ? qscale * exp2i(-pos_lg(po2)) : 0.f;
 #pragma unroll
-      for (int j = 0; j < kGQ; ++j) qhi_s[tid * kGQ + j] = e2 >= 0 ? q_s[j * kD + (e2 & 0xFFFF)] * qscale : 0.f;
+      for (int j = 0; j < kGQ; ++j) qhi_s[tid * kGQ + j] = e2 >= 0 ? q_s[j * kD + (e2 & 0xFFFF)] * qs2 : 0.f;
       posoff_s[tid] = po2;
     }
     // FP16-tier query values (times scaling * log2 e), slot-major.
@@ -406,8 +416,8 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
           const float4 qa = *reinterpret_cast<const float4*>(qhi_s + r * kGQ);
           const float4 qb = *reinterpret_cast<const float4*>(qhi_s + r * kGQ + 4);
           const float qv[kGQ] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-          const float sc = o >= 0 ? half_bits_to_float(meta[o & 0xFFFF]) * fsc : 0.f;
-          const float mn = o >= 0 ? half_bits_to_float(meta[o >> 16]) : 0.f;
+          const float sc = o >= 0 ? half_bits_to_float(meta[pos_scale(o)]) * fsc : 0.f;
+          const float mn = o >= 0 ? half_bits_to_float(meta[pos_min(o)]) * exp2i(pos_lg(o)) : 0.f;
           qk_b_row<GQ>(bqk, S.bqk_sbo, kDecThreads + r, qv, sc, mn, bias);
         }
         const float part = warp_sum8_scatter(bias, lane);
@@ -488,7 +498,8 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     const int row_off = tid * R;
     const int rk = (tid >> 2) & 3;               // PV row t carries code * 4^rk
     const bool has_pos = tid < S.kpad;           // warp-uniform (K padded to 32)
-    const int soff = po >= 0 ? (po & 0xFFFF) : 0, moff = po >= 0 ? (po >> 16) : 0;
+    const int soff = po >= 0 ? pos_scale(po) : 0, moff = po >= 0 ? pos_min(po) : 0;
+    const float mmul = po >= 0 ? exp2i(pos_lg(po)) : 0.f;
     const float cf = c2 * exp2i(eq - 21);        // fixed-point unit 2^(Eq-21) -> log2-scaled score
     const int bslot = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
 
@@ -504,7 +515,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
 #pragma unroll 4
         for (int w = 0; w < wd0; ++w) {
           const uint32_t x = src[w];
-          tmem_st_x4(col + 4 * w, x & kM2, (x >> 2) & kM2, (x >> 4) & kM2, (x >> 6) & kM2);
+          tmem_st_x4(col + 4 * w, x & kM2, x & (kM2 << 2), x & (kM2 << 4), x & (kM2 << 6));
         }
         col += 4 * wd0;
       }
@@ -513,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
 #pragma unroll 4
         for (int w = 0; w < wd1; ++w) {
           const uint32_t x = src[w];
-          tmem_st_x2(col + 2 * w, x & kM4, (x >> 4) & kM4);
+          tmem_st_x2(col + 2 * w, x & kM4, x & (kM4 << 4));
         }
         col += 2 * wd1;
       }
@@ -526,7 +537,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       const float fsc = exp2i(-esc);
       if (has_pos) {
         const float sc = po >= 0 ? half_bits_to_float(meta[soff]) * fsc : 0.f;
-        const float mn = po >= 0 ? half_bits_to_float(meta[moff]) : 0.f;
+        const float mn = half_bits_to_float(meta[moff]) * mmul;
         float bias[kGQ];
 #pragma unroll
         for (int j = 0; j < kGQ; ++j) bias[j] = 0.f;

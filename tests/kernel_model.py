@@ -3,8 +3,10 @@
 The sm_100a decode kernel (K2) runs both contractions of a packed page on the
 INT8 tensor cores (``tcgen05.mma.kind::i8``):
 
-* QK: integer Key codes (u8, 0..255) times the per-page products
-  ``q_j[c] * scale_c`` written as fixed point ``X`` (|X| <= 2^21) relative to
+* QK: integer Key codes (u8, 0..255; INT2/INT4 codes masked in place, so
+  they carry a power-of-two weight w_c that the B row divides out) times the
+  per-page products ``q_j[c] * scale_c / w_c`` written as fixed point ``X``
+  (|X| <= 2^21) relative to
   a power-of-two block exponent (one per query group and page), offset by 2^22
   so the three limbs (bytes) are unsigned.  A column of ones in the B operand
   returns sum_c code_c, which removes the offset exactly:
@@ -63,18 +65,24 @@ def model_attention(layer: orc.OracleLayer, query: np.ndarray, key_new, value_ne
                 codes = orc.unpack_ints(layer.hist_k[code]["code"][h, t0:t0 + 128], cnt, bits)
                 sc = layer.hist_k[code]["scale"][h, :cnt, pg].astype(np.float32)
                 mn = layer.hist_k[code]["min"][h, :cnt, pg].astype(np.float32)
-                tiers.append((idx, codes, sc, mn))
+                # codes masked in place: INT2 slot 4i+k carries 4^k, INT4 slot 2i+k carries 16^k
+                slots = np.arange(cnt)
+                weight = 4 ** (slots % 4) if bits == 2 else 16 ** (slots % 2) if bits == 4 else np.ones(cnt, np.int64)
+                tiers.append((idx, codes, sc, mn, weight))
                 scale_max = max(scale_max, float(sc.max()))
             esc = int(_exp2_ceil(scale_max))
-            for idx, codes, sc, mn in tiers:
-                # X = rint(q * 2^(qk_bits - eq) * (scale * 2^-esc)), |X| <= 2^qk_bits
+            for idx, codes, sc, mn, weight in tiers:
+                # X = rint(q * 2^(qk_bits - eq) / w * (scale * 2^-esc)), |X| <= 2^qk_bits
                 qq = (q[:, idx] * np.ldexp(np.float32(1), (qk_bits - eq))[:, None]).astype(np.float32)
+                qq = (qq / weight.astype(np.float32)[None, :]).astype(np.float32)
                 sp = (sc * np.float32(2.0 ** -esc)).astype(np.float32)
                 X = np.rint((qq * sp[None, :]).astype(np.float32)).astype(np.int64)   # [gq, cnt]
                 U = X + (1 << (qk_bits + 1))
                 assert U.min() >= 0 and U.max() < (1 << 24)
-                acc = [codes.astype(np.int64) @ ((U >> (8 * k)) & 0xFF).T for k in range(3)]
-                ones = codes.astype(np.int64).sum(axis=1)[:, None]
+                A = codes.astype(np.int64) * weight[None, :]
+                assert A.max() <= 255
+                acc = [A @ ((U >> (8 * k)) & 0xFF).T for k in range(3)]
+                ones = A.sum(axis=1)[:, None]
                 s_int += acc[0] + 256.0 * acc[1] + 65536.0 * acc[2] - float(1 << (qk_bits + 1)) * ones
                 bias += (q[:, idx].astype(np.float64) @ mn.astype(np.float64))
             scale_qk = np.ldexp(1.0, eq + esc - qk_bits)            # per q-head

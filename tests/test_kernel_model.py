@@ -31,7 +31,7 @@ def _case(target_bit: float, T: int, seed: int = 1):
 def test_kernel_fixed_point_within_tolerance(target_bit):
     store, q, kn, vn, want = _case(target_bit, 2048)
     got = model_attention(store, q, kn, vn, 128 ** -0.5)
-    ok, err, cos = attention_close(got, want, atol=2e-4)  # 10x tighter than the decode bound
+    ok, err, cos = attention_close(got, want, atol=5e-4)  # 4x tighter than the decode bound
     assert ok, (err, cos)
 
 
