@@ -59,6 +59,19 @@ def measured_peak_hbm() -> tuple[float, str]:
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def ncu_traffic(config_id: int):
+    """DRAM bytes (read + write) of one K2 launch for this config, from the
+    committed ncu capture summary (profiles/k2_decode_traffic.txt), or None."""
+    try:
+        for line in (ROOT / "profiles" / "k2_decode_traffic.txt").read_text().splitlines():
+            parts = line.split()
+            if len(parts) == 2 and parts[0] == f"config{config_id}":
+                return int(parts[1])
+    except (OSError, ValueError):
+        return None
+    return None
+
+
 def tails_for(cfg: dict, rank: int):
     import numpy as np
 
@@ -385,7 +398,9 @@ def run_b200(args, cfg) -> None:
             "pages_per_split": calls[0].pps,
             "roofline": {"kernel": "lf_decode_partial (K2)", "bound": "hbm", "achieved": achieved,
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                         "traffic": None, "bytes_per_launch": k2_bytes_avg, "avg_launch_ms": k2_avg_ms},
+                         "traffic": ncu_traffic(args.config),
+                         "traffic_source": f"ncu --set full, profiles/k2_decode_config{args.config}_ncu.md",
+                         "bytes_per_launch": k2_bytes_avg, "avg_launch_ms": k2_avg_ms},
             "e2e": {"value": world * B / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "cpu_baseline": cpu,
