@@ -72,6 +72,19 @@ def ncu_traffic(config_id: int):
     return None
 
 
+def max_over_ranks(value: float, device) -> float:
+    """Max of a per-rank time over the default process group (the value
+    itself without one): every multi-GPU time is the slowest rank's."""
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def tails_for(cfg: dict, rank: int):
     import numpy as np
 
@@ -327,11 +340,7 @@ def run_b200(args, cfg) -> None:
         torch.cuda.synchronize()
         barrier()
     ms = e0.elapsed_time(e1) / args.steps
-    ms_max = ms
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = float(t.item())
+    ms_max = max_over_ranks(ms, dev)
 
     # K2 launch durations over the same kind of timed steps (eager launches, events per K2).
     k2_ms = []
@@ -344,7 +353,7 @@ def run_b200(args, cfg) -> None:
             c.launch_merge()
         torch.cuda.synchronize()
         k2_ms.extend(a.elapsed_time(b) for a, b in ev)
-    k2_avg_ms = sum(k2_ms) / len(k2_ms)
+    k2_avg_ms = max_over_ranks(sum(k2_ms) / len(k2_ms), dev)
 
     # End to end: pinned host inputs -> device, step, outputs -> host, every step.
     hq, hk, hv = (x.cpu().pin_memory() for x in (q, kn, vn))
@@ -360,11 +369,7 @@ def run_b200(args, cfg) -> None:
         hout.copy_(out, non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, dev)
     h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
     d2h = hout.numel() * hout.element_size()
 

@@ -1,7 +1,7 @@
 // Thin wrappers over the sm_100a PTX used by the tensor-core decode kernel:
 // mbarriers with bounded waits, 1-D bulk copies, tensor memory (TMEM)
 // allocation / loads / stores, UMMA descriptors and tcgen05.mma (kind::i8).
-// No TMA multicast anywhere: every CTA fetches its own data.
+// Every CTA fetches its own data with plain copies into its own shared memory.
 #pragma once
 
 #include <stdint.h>
