@@ -314,8 +314,7 @@ def run_b200(args, cfg) -> None:
 
     def step():
         for c in calls:
-            c.launch_partial()
-            c.launch_merge()
+            c.launch()
 
     # Warm-up (also configures kernels before capture).
     for _ in range(max(args.warmup, 1)):

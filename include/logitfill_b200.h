@@ -169,6 +169,20 @@ LF_API int lf_decode_merge(const float* workspace, const int32_t* hist_tokens, i
                     lf_stream_t stream);
 
 /*
+ * K2 then K3 in one call (the reference's single decode op, logitfill_decode,
+ * kernel.cu:198-284): same inputs as lf_decode_partial (workspace of
+ * lf_decode_workspace_bytes bytes), same output as lf_decode_merge.
+ */
+LF_API int lf_decode(const lf_layout* layout, const int32_t* rows, const uint16_t* kmeta,
+                     const int32_t* slot_chan, const int32_t* hist_tokens, const void* tail_k,
+                     const void* tail_v, int64_t tail_seq_stride, int64_t tail_head_stride,
+                     const int32_t* tail_len, int resid_dtype, const void* k_new, const void* v_new,
+                     int64_t new_seq_stride, int64_t new_head_stride, const void* q, int q_dtype,
+                     int64_t q_seq_stride, int64_t q_head_stride, int batch, int n_q, float scaling,
+                     int pages_per_split, int max_splits, float* workspace, void* out, int out_dtype,
+                     int64_t out_seq_stride, int64_t out_head_stride, int32_t* status, lf_stream_t stream);
+
+/*
  * K2 + K3 without a caller workspace, for callers that cannot allocate
  * device memory (allocator callbacks, runtimes that plan every allocation up
  * front, hosts that link only this library).  No counterpart in the

@@ -352,27 +352,28 @@ extern "C" int lf_decode_max_splits(int64_t max_pages, int pages_per_split, int 
   return static_cast<int>((max_pages + pages_per_split - 1) / pages_per_split) + lf::residual_splits(page_size);
 }
 
-extern "C" int lf_decode_partial(const lf_layout* layout, const int32_t* rows, const uint16_t* kmeta,
-                                 const int32_t* slot_chan, const int32_t* hist_tokens,
-                                 const void* tail_k, const void* tail_v, int64_t tail_seq_stride,
-                                 int64_t tail_head_stride, const int32_t* tail_len, int resid_dtype,
-                                 const void* k_new, const void* v_new, int64_t new_seq_stride,
-                                 int64_t new_head_stride, const void* q, int q_dtype,
-                                 int64_t q_seq_stride, int64_t q_head_stride, int batch, int n_q,
-                                 float scaling, int pages_per_split, int max_splits,
-                                 float* workspace, int32_t* status, lf_stream_t stream) {
-  LF_CHECK_ARG(layout != nullptr, "lf_decode_partial: null layout");
+namespace lf {
+
+// Validated launch parameters of K2 (shared by lf_decode_partial and lf_decode).
+static int prepare_decode(const char* who, const lf_layout* layout, const int32_t* rows, const uint16_t* kmeta,
+                          const int32_t* slot_chan, const int32_t* hist_tokens, const void* tail_k,
+                          const void* tail_v, int64_t tail_seq_stride, int64_t tail_head_stride,
+                          const int32_t* tail_len, int resid_dtype, const void* k_new, const void* v_new,
+                          int64_t new_seq_stride, int64_t new_head_stride, const void* q, int q_dtype,
+                          int64_t q_seq_stride, int64_t q_head_stride, int batch, int n_q, float scaling,
+                          int pages_per_split, int max_splits, float* workspace, int32_t* status,
+                          DecodeParams& p) {
+  LF_CHECK_ARG(layout != nullptr, "%s: null layout", who);
   const lf_layout& L = *layout;
   LF_CHECK_ARG(rows && slot_chan && hist_tokens && tail_k && tail_v && tail_len && q && workspace,
-               "lf_decode_partial: null pointer");
-  LF_CHECK_ARG((k_new == nullptr) == (v_new == nullptr), "lf_decode_partial: k_new/v_new mismatch");
+               "%s: null pointer", who);
+  LF_CHECK_ARG((k_new == nullptr) == (v_new == nullptr), "%s: k_new/v_new mismatch", who);
   LF_CHECK_ARG(batch > 0 && batch <= 65535 && n_q > 0 && n_q % L.kv_heads == 0,
-               "lf_decode_partial: batch %d, n_q %d, kv_heads %d", batch, n_q, L.kv_heads);
+               "%s: batch %d, n_q %d, kv_heads %d", who, batch, n_q, L.kv_heads);
   LF_CHECK_ARG(pages_per_split > 0 && max_splits >= 1 && max_splits <= 65535,
-               "lf_decode_partial: pages_per_split %d, max_splits %d", pages_per_split, max_splits);
+               "%s: pages_per_split %d, max_splits %d", who, pages_per_split, max_splits);
   LF_CHECK_ARG(max_splits >= lf_decode_max_splits(L.row_cap / L.page_size, pages_per_split, L.page_size),
-               "lf_decode_partial: max_splits %d cannot cover row_cap %lld", max_splits,
-               (long long)L.row_cap);
+               "%s: max_splits %d cannot cover row_cap %lld", who, max_splits, (long long)L.row_cap);
   {
     const int esz = resid_dtype == LF_F32 ? 4 : 2;
     const bool aligned = (reinterpret_cast<uintptr_t>(tail_k) % 16 == 0) &&
@@ -381,21 +382,23 @@ extern "C" int lf_decode_partial(const lf_layout* layout, const int32_t* rows, c
                          (k_new == nullptr || ((reinterpret_cast<uintptr_t>(k_new) % 16 == 0) &&
                                                (reinterpret_cast<uintptr_t>(v_new) % 16 == 0) &&
                                                (new_seq_stride * esz) % 16 == 0 && (new_head_stride * esz) % 16 == 0));
-    LF_CHECK_ARG(aligned, "lf_decode_partial: residual / new-token rows must be 16-byte aligned");
+    LF_CHECK_ARG(aligned, "%s: residual / new-token rows must be 16-byte aligned", who);
   }
+  LF_CHECK_ARG(resid_dtype == LF_F32 || resid_dtype == LF_F16 || resid_dtype == LF_BF16, "%s: residual dtype %d",
+               who, resid_dtype);
+  LF_CHECK_ARG(q_dtype == LF_F32 || q_dtype == LF_F16 || q_dtype == LF_BF16, "%s: q dtype %d", who, q_dtype);
   LF_CHECK_SUPPORTED(L.head_dim % 8 == 0, "decode head_dim %d must be a multiple of 8", L.head_dim);
   LF_CHECK_SUPPORTED(L.bit_v == 2, "decode supports bit_v 2, got %d", L.bit_v);
   LF_CHECK_SUPPORTED(L.k_group == L.page_size, "decode needs k_group == page_size (%d vs %d)",
                      L.k_group, L.page_size);
   LF_CHECK_SUPPORTED(L.v_group == L.head_dim, "decode needs v_group == head_dim (%d vs %d)",
                      L.v_group, L.head_dim);
-  LF_CHECK_SUPPORTED(L.head_dim % 16 == 0 && L.head_dim <= lf::kDecThreads,
+  LF_CHECK_SUPPORTED(L.head_dim % 16 == 0 && L.head_dim <= kDecThreads,
                      "decode head_dim %d not supported", L.head_dim);
-  LF_CHECK_SUPPORTED(L.page_size <= lf::kDecThreads && L.page_size % 4 == 0,
-                     "decode page_size %d must be a multiple of 4 and at most %d", L.page_size, lf::kDecThreads);
-  LF_CHECK_SUPPORTED(n_q / L.kv_heads <= lf::kGQ, "decode GQA group %d > %d", n_q / L.kv_heads,
-                     lf::kGQ);
-  lf::DecodeParams p{};
+  LF_CHECK_SUPPORTED(L.page_size <= kDecThreads && L.page_size % 4 == 0,
+                     "decode page_size %d must be a multiple of 4 and at most %d", L.page_size, kDecThreads);
+  LF_CHECK_SUPPORTED(n_q / L.kv_heads <= kGQ, "decode GQA group %d > %d", n_q / L.kv_heads, kGQ);
+  p = DecodeParams{};
   p.L = L;
   p.rows = rows;
   p.kmeta = kmeta;
@@ -418,23 +421,68 @@ extern "C" int lf_decode_partial(const lf_layout* layout, const int32_t* rows, c
   p.gq = n_q / L.kv_heads;
   p.pps = pages_per_split;
   p.max_splits = max_splits;
-  p.n_slots = lf::n_slots_of(L);
+  p.n_slots = n_slots_of(L);
   p.scaling = scaling;
   p.ws = workspace;
   p.status = status;
   p.resid_dtype = resid_dtype;
   p.q_dtype = q_dtype;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (lf::tc_supported(L, p.gq, pages_per_split)) return lf::launch_partial_tc(p, resid_dtype, q_dtype, s);
-  LF_CHECK_SUPPORTED(lf::decode_smem(L, p.n_slots).total <= 227 * 1024,
-                     "decode shared memory %d B too large", lf::decode_smem(L, p.n_slots).total);
-  switch (resid_dtype) {
-    case LF_F32: return lf::dispatch_q<float>(p, q_dtype, s);
-    case LF_F16: return lf::dispatch_q<__half>(p, q_dtype, s);
-    case LF_BF16: return lf::dispatch_q<__nv_bfloat16>(p, q_dtype, s);
+  return LF_OK;
+}
+
+// K2 on the kernel the geometry selects.
+static int launch_decode(const DecodeParams& p, cudaStream_t s) {
+  if (tc_supported(p.L, p.gq, p.pps)) return launch_partial_tc(p, p.resid_dtype, p.q_dtype, s);
+  LF_CHECK_SUPPORTED(decode_smem(p.L, p.n_slots).total <= 227 * 1024, "decode shared memory %d B too large",
+                     decode_smem(p.L, p.n_slots).total);
+  switch (p.resid_dtype) {
+    case LF_F32: return dispatch_q<float>(p, p.q_dtype, s);
+    case LF_F16: return dispatch_q<__half>(p, p.q_dtype, s);
+    default: return dispatch_q<__nv_bfloat16>(p, p.q_dtype, s);
   }
-  lf::set_error("lf_decode_partial: residual dtype %d", resid_dtype);
-  return LF_ERR_INVALID_ARGUMENT;
+}
+
+}  // namespace lf
+
+extern "C" int lf_decode_partial(const lf_layout* layout, const int32_t* rows, const uint16_t* kmeta,
+                                 const int32_t* slot_chan, const int32_t* hist_tokens,
+                                 const void* tail_k, const void* tail_v, int64_t tail_seq_stride,
+                                 int64_t tail_head_stride, const int32_t* tail_len, int resid_dtype,
+                                 const void* k_new, const void* v_new, int64_t new_seq_stride,
+                                 int64_t new_head_stride, const void* q, int q_dtype,
+                                 int64_t q_seq_stride, int64_t q_head_stride, int batch, int n_q,
+                                 float scaling, int pages_per_split, int max_splits,
+                                 float* workspace, int32_t* status, lf_stream_t stream) {
+  lf::DecodeParams p;
+  const int st = lf::prepare_decode("lf_decode_partial", layout, rows, kmeta, slot_chan, hist_tokens, tail_k, tail_v,
+                                    tail_seq_stride, tail_head_stride, tail_len, resid_dtype, k_new, v_new,
+                                    new_seq_stride, new_head_stride, q, q_dtype, q_seq_stride, q_head_stride, batch,
+                                    n_q, scaling, pages_per_split, max_splits, workspace, status, p);
+  if (st != LF_OK) return st;
+  return lf::launch_decode(p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lf_decode(const lf_layout* layout, const int32_t* rows, const uint16_t* kmeta,
+                         const int32_t* slot_chan, const int32_t* hist_tokens, const void* tail_k,
+                         const void* tail_v, int64_t tail_seq_stride, int64_t tail_head_stride,
+                         const int32_t* tail_len, int resid_dtype, const void* k_new, const void* v_new,
+                         int64_t new_seq_stride, int64_t new_head_stride, const void* q, int q_dtype,
+                         int64_t q_seq_stride, int64_t q_head_stride, int batch, int n_q, float scaling,
+                         int pages_per_split, int max_splits, float* workspace, void* out, int out_dtype,
+                         int64_t out_seq_stride, int64_t out_head_stride, int32_t* status, lf_stream_t stream) {
+  lf::DecodeParams p;
+  const int st = lf::prepare_decode("lf_decode", layout, rows, kmeta, slot_chan, hist_tokens, tail_k, tail_v,
+                                    tail_seq_stride, tail_head_stride, tail_len, resid_dtype, k_new, v_new,
+                                    new_seq_stride, new_head_stride, q, q_dtype, q_seq_stride, q_head_stride, batch,
+                                    n_q, scaling, pages_per_split, max_splits, workspace, status, p);
+  if (st != LF_OK) return st;
+  LF_CHECK_ARG(out != nullptr, "lf_decode: null output");
+  LF_CHECK_ARG(out_dtype == LF_F32 || out_dtype == LF_F16 || out_dtype == LF_BF16, "lf_decode: out dtype %d",
+               out_dtype);
+  const int k2 = lf::launch_decode(p, reinterpret_cast<cudaStream_t>(stream));
+  if (k2 != LF_OK) return k2;
+  return lf_decode_merge(workspace, hist_tokens, batch, layout->kv_heads, n_q, layout->head_dim, layout->page_size,
+                         pages_per_split, max_splits, out, out_dtype, out_seq_stride, out_head_stride, stream);
 }
 
 extern "C" int lf_decode_merge(const float* workspace, const int32_t* hist_tokens, int batch,

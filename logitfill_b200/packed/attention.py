@@ -92,6 +92,20 @@ class DecodeCall:
             c.batch, c.n_q, self.scaling, self.pps, self.max_splits, _lib.ptr(self.ws), _lib.ptr(c.status),
             _lib.stream_handle(self.query.device)), "lf_decode_partial")
 
+    def launch(self) -> None:
+        """K2 then K3 in one library call (lf_decode) on the current stream."""
+        so, L, c, out = _lib.lib(), self.layer, self.cache, self.out
+        tk, kn = L.tail_k, self.key_new
+        _lib.check(so.lf_decode(
+            ctypes.byref(L.layout.c), _lib.ptr(L.rows), _lib.ptr(L.kmeta), _lib.ptr(L.layout.slot_chan),
+            _lib.ptr(L.dev_hist), _lib.ptr(tk), _lib.ptr(L.tail_v), tk.stride(0), tk.stride(1),
+            _lib.ptr(L.dev_tail), _lib.dtype_code(self.resid_dtype), _lib.ptr(kn), _lib.ptr(self.value_new),
+            kn.stride(0) if kn is not None else 0, kn.stride(1) if kn is not None else 0,
+            _lib.ptr(self.query), _lib.dtype_code(self.query.dtype), self.query.stride(0), self.query.stride(1),
+            c.batch, c.n_q, self.scaling, self.pps, self.max_splits, _lib.ptr(self.ws), _lib.ptr(out),
+            _lib.dtype_code(out.dtype), out.stride(0), out.stride(1), _lib.ptr(c.status),
+            _lib.stream_handle(self.query.device)), "lf_decode")
+
     def launch_merge(self) -> None:
         so, c, out = _lib.lib(), self.cache, self.out
         _lib.check(so.lf_decode_merge(
@@ -106,8 +120,7 @@ def decode_into(cache: PackedKVCache, layer_idx: int, query: torch.Tensor, key_n
     history, residual page and (optionally) the new token ``[B, n_kv, D]``,
     written to ``out`` ``[B, n_q, D]``.  Launches K2 then K3 on the current stream."""
     call = DecodeCall(cache, layer_idx, query, key_new, value_new, scaling, out, pps)
-    call.launch_partial()
-    call.launch_merge()
+    call.launch()
     return out
 
 

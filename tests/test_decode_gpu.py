@@ -163,3 +163,33 @@ def test_errors_are_raised_not_swallowed():
         packed_attention(mgr, 0, q, q[:, :4], q[:, :4], 0.1)
     with pytest.raises(NotImplementedError):
         PackedKVCache([None], 1, 28, 4, 128, bit_v=4, device="cuda")
+
+
+
+def test_single_call_matches_partial_then_merge():
+    """lf_decode (K2 then K3 in one library call) gives exactly the output of
+    lf_decode_partial + lf_decode_merge, on a ragged batch at several split
+    sizes, in fp32 and bf16 output."""
+    from logitfill_b200.packed.attention import DecodeCall
+
+    B, H, NQ, D = 5, 8, 40, 128
+    levels = synthetic_levels(1, H, D, 2.5, seed=19)[0]
+    lengths = [5, 128, 700, 1024 + 127, 2000]
+    k, v = synthetic_kv(B, H, max(lengths) + 1, D, seed=19, layer=0, device="cuda")
+    cache = PackedKVCache([levels], B, NQ, H, D, device="cuda", capacity=2048)
+    cache.prefill(0, k, v, lengths)
+    g = torch.Generator(device="cuda").manual_seed(3)
+    q = torch.randn(B, NQ, D, generator=g, device="cuda").to(torch.bfloat16)
+    kn = torch.stack([k[b, :, n] for b, n in enumerate(lengths)])
+    vn = torch.stack([v[b, :, n] for b, n in enumerate(lengths)])
+    for pps in (1, 5, 16):
+        for dt in (torch.float32, torch.bfloat16):
+            two = torch.empty(B, NQ, D, dtype=dt, device="cuda")
+            call = DecodeCall(cache, 0, q, kn, vn, D ** -0.5, two, pps=pps)
+            call.launch_partial()
+            call.launch_merge()
+            one = torch.full((B, NQ, D), float("nan"), dtype=dt, device="cuda")
+            DecodeCall(cache, 0, q, kn, vn, D ** -0.5, one, pps=pps).launch()
+            torch.cuda.synchronize()
+            assert torch.equal(one, two), (pps, dt)
+    cache.check_status()
