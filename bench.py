@@ -402,7 +402,7 @@ def run_b200(args, cfg) -> None:
             "pages_per_split": calls[0].pps,
             "roofline": {"kernel": "lf_decode_partial (K2)", "bound": "hbm", "achieved": achieved,
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                         "traffic": ncu_traffic(args.config),
+                         "traffic": ncu_traffic(args.config) if args.target_bit is None else None,
                          "traffic_source": f"ncu --set full, profiles/k2_decode_config{args.config}_ncu.md",
                          "bytes_per_launch": k2_bytes_avg, "avg_launch_ms": k2_avg_ms},
             "e2e": {"value": world * B / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
@@ -426,12 +426,16 @@ def main() -> None:
     ap.add_argument("--config", type=int, default=1, choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--target-bit", type=float, default=None,
+                    help="override the config's Key policy budget (config 2 sweep: 2.25, 2.5, 3.0, 4.0)")
     ap.add_argument("--pps", type=int, default=None,
                     help="pages per K2 work item (default: the occupancy-aware planner)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.target_bit is not None:
+        cfg["target_bit"] = args.target_bit
     if args.impl == "reference":
         run_reference(args, cfg)
     else:
