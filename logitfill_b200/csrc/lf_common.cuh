@@ -13,6 +13,11 @@ namespace lf {
 // Per-thread error text for lf_last_error().
 void set_error(const char* fmt, ...);
 int launch_status(const char* what);
+// Raise kern's dynamic shared-memory limit on the current device to at least
+// `bytes` (optionally with the full shared-memory carveout).  The limit only
+// grows: launches and occupancy queries for different layouts share one
+// kernel, and lowering it for a small layout would fail a larger one later.
+cudaError_t raise_smem_limit(const void* kern, int bytes, bool max_carveout);
 
 template <typename T> struct Scalar;
 template <> struct Scalar<float> {

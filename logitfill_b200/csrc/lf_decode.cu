@@ -11,7 +11,6 @@
 //   q.k_t = sum_c (q_c s_c) code_tc + sum_c q_c m_c        (per-page q' and bias)
 //   sum_t p_t v_t = sum_t (p_t s_t) code_t + (sum_t p_t m_t) 1
 // and the inner loops multiply raw integer codes by precomputed fp32 factors.
-#include <atomic>
 
 #include "lf_decode_common.cuh"
 
@@ -295,16 +294,12 @@ template <typename RT, typename QT>
 static int launch_partial(const DecodeParams& p, cudaStream_t stream) {
   const DecodeSmem S = decode_smem(p.L, p.n_slots);
   auto kern = decode_partial_simt<RT, QT>;
-  // Raise the kernel's dynamic shared-memory limit once per size, outside
-  // any later stream capture of the launch.
-  static std::atomic<int> configured{48 * 1024};
-  if (S.total > configured.load()) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S.total);
-    if (e == cudaSuccess) configured.store(S.total);
-    if (e != cudaSuccess) {
-      set_error("lf_decode_partial: shared memory %d B: %s", S.total, cudaGetErrorString(e));
-      return LF_ERR_UNSUPPORTED;
-    }
+  // The limit is raised once per size, outside any later stream capture of
+  // the launch.
+  cudaError_t e = raise_smem_limit(reinterpret_cast<const void*>(kern), S.total, false);
+  if (e != cudaSuccess) {
+    set_error("lf_decode_partial: shared memory %d B: %s", S.total, cudaGetErrorString(e));
+    return LF_ERR_UNSUPPORTED;
   }
   dim3 grid(p.max_splits, p.L.kv_heads, p.batch);
   kern<<<grid, kDecThreads, S.total, stream>>>(p);
@@ -331,8 +326,11 @@ extern "C" int lf_decode_occupancy(const lf_layout* layout, int n_q, int pages_p
   const lf::DecodeSmem S = lf::decode_smem(*layout, lf::n_slots_of(*layout));
   if (S.total > 227 * 1024) return 0;
   auto kern = lf::decode_partial_simt<__nv_bfloat16, __nv_bfloat16>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S.total);
   int blocks = 0;
+  if (lf::raise_smem_limit(reinterpret_cast<const void*>(kern), S.total, false) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kern, lf::kDecThreads, S.total) != cudaSuccess) {
     cudaGetLastError();
     return -1;

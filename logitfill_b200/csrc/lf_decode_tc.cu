@@ -13,11 +13,12 @@
 //   U_K  Key codes -> u8 in TMEM (A of QK, K-major), masked in place (INT2
 //        slot k of a byte as code * 4^k, INT4 as code * 16^k); the B row of QK
 //        for K position t (tier slot c, code weight w_c): for each q-head j the
-//        fixed point X = rint(q_j[c] scale_c 2^(21-Eq-Es) / w_c), offset by 2^22 and split into
-//        three unsigned limbs, plus a one in the ones column; Es is the page's
-//        Key-scale exponent, from the largest scale the packer stores in the
-//        meta row; partial sums of the Key-min bias sum_c q_j[c] min_c.
-//   S    score_tj = 2^(Eq+Es-21) (acc0 + 256 acc1 + 65536 (acc2 - 64 ones))
+//        fixed point X = rint(q_j[c] scale_c 2^(29-Eq-Es) / w_c), offset by 2^30 and split into
+//        four unsigned limbs (bytes); Es is the page's Key-scale exponent, from
+//        the largest scale the packer stores in the meta row; partial sums of
+//        the Key-min bias sum_c q_j[c] min_c; the token's code sum n_t (the
+//        byte sum of its code words, which is the sum of its A row).
+//   S    score_tj = 2^(Eq+Es-29) (acc0 + 2^8 acc1 + 2^16 acc2 + 2^24 (acc3 - 64 n_t))
 //        + FP16-tier part + bias_j; page max per q-head; online softmax with
 //        the per-q-head statistics held by lane j of every warp; the B row of
 //        PV for token t: rint(p_tj vscale_t 2^(23-Ev)) in three limbs, Ev the
@@ -29,7 +30,7 @@
 // Order: S(i), U_K(i+1), C(i), U_V(i+1).  QK(i+1) overlaps C(i) and U_V(i+1),
 // PV(i) overlaps U_K(i+1).
 //
-// The integer products are exact; the fixed-point rounding is 2^-21 w_c (QK,
+// The integer products are exact; the fixed-point rounding is 2^-29 w_c (QK,
 // w_c <= 64) and 2^-23 (PV) of the block maxima (tests/kernel_model.py models
 // it).  Every
 // mbarrier wait is bounded (2 s).  On expiry the CTA records
@@ -37,7 +38,6 @@
 // barriers, so nothing deadlocks), drains its own copies and MMAs, frees its
 // TMEM and returns.
 #include <algorithm>
-#include <atomic>
 
 #include "lf_decode_common.cuh"
 #include "lf_tcgen05.cuh"
@@ -133,10 +133,10 @@ __device__ __forceinline__ int kpos_entry(const lf_layout& L, const int32_t* slo
   return ch < 0 ? -1 : (ch | (tier << 16) | (slot << 18));
 }
 
-// Pack bytes 0..2 of U[0..7] into MN-major limb rows:
-// c0 = {byte0 of U0..U7, byte1 of U0..U7}, c1 = {byte2 of U0..U7, w3, 0}.
-__device__ __forceinline__ void pack_limbs(const uint32_t (&U)[kGQ], uint4& c0, uint4& c1, uint32_t w3) {
-  uint32_t b0[2], b1[2], b2[2];
+// Pack the bytes of U[0..7] into MN-major limb rows:
+// c0 = {byte0 of U0..U7, byte1 of U0..U7}, c1 = {byte2 of U0..U7, byte3 of U0..U7}.
+__device__ __forceinline__ void pack_limbs4(const uint32_t (&U)[kGQ], uint4& c0, uint4& c1) {
+  uint32_t b0[2], b1[2], b2[2], b3[2];
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const uint32_t t01 = __byte_perm(U[4 * h + 0], U[4 * h + 1], 0x5140);
@@ -146,9 +146,15 @@ __device__ __forceinline__ void pack_limbs(const uint32_t (&U)[kGQ], uint4& c0, 
     b0[h] = __byte_perm(t01, t23, 0x5410);
     b1[h] = __byte_perm(t01, t23, 0x7632);
     b2[h] = __byte_perm(s01, s23, 0x5410);
+    b3[h] = __byte_perm(s01, s23, 0x7632);
   }
   c0 = make_uint4(b0[0], b0[1], b1[0], b1[1]);
-  c1 = make_uint4(b2[0], b2[1], w3, 0u);
+  c1 = make_uint4(b2[0], b2[1], b3[0], b3[1]);
+}
+// Bytes 0..2 of U[0..7] (the PV limbs): c1 = {byte2 of U0..U7, 0, 0}.
+__device__ __forceinline__ void pack_limbs(const uint32_t (&U)[kGQ], uint4& c0, uint4& c1) {
+  pack_limbs4(U, c0, c1);
+  c1.z = c1.w = 0u;
 }
 
 // Warp reduce-scatter of 8 sums: returns the warp total of v[j] for
@@ -199,11 +205,10 @@ __device__ __forceinline__ float exp2i(int e) { return __int_as_float((e + 127) 
 // Barrier slots in shared memory.
 enum { kBarFull = 0, kBarKReady = kStages, kBarVReady, kBarQK, kBarPV, kNumBars };
 
-// One B row of QK (K position pp; qv = q_j[c] 2^(21-Eq), zero for a padding
-// position, whose A codes are zero) and its Key-min bias terms.  With
-// |X| <= 2^21 the fp32 sum 1.5 * 2^23 + X lies in [2^23, 2^24), where the
-// spacing is 1: the sum is rint(X) + 1.5 * 2^23 and its low 24 bits are
-// U = X + 2^22, the three limbs, with no integer arithmetic.
+// One B row of QK (K position pp; qv = q_j[c] 2^(29-Eq) / w_c, zero for a
+// padding position) and its Key-min bias terms.  X = rint(qv * scale) has
+// |X| <= 2^29, so U = X + 2^30 is an unsigned 31-bit number: its four bytes
+// are the limbs.
 template <int GQ>
 __device__ __forceinline__ void qk_b_row(unsigned char* bqk, int sbo, int pp, const float (&qv)[kGQ], float sc,
                                          float mn, float (&bias)[kGQ]) {
@@ -211,14 +216,14 @@ __device__ __forceinline__ void qk_b_row(unsigned char* bqk, int sbo, int pp, co
 #pragma unroll
   for (int j = 0; j < kGQ; ++j) {
     if (j < GQ) {
-      U[j] = __float_as_uint(fmaf(qv[j], sc, 12582912.0f));
+      U[j] = static_cast<uint32_t>(__float2int_rn(qv[j] * sc) + (1 << 30));
       bias[j] = fmaf(qv[j], mn, bias[j]);
     } else {
-      U[j] = 0x400000u;  // X = 0
+      U[j] = 1u << 30;  // X = 0
     }
   }
   uint4 c0, c1;
-  pack_limbs(U, c0, c1, 1u);
+  pack_limbs4(U, c0, c1);
   unsigned char* dst = bqk + (pp & 7) * 16 + (pp >> 3) * 128;
   *reinterpret_cast<uint4*>(dst) = c0;
   *reinterpret_cast<uint4*>(dst + sbo) = c1;
@@ -283,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
   uint32_t* red_m = reinterpret_cast<uint32_t*>(smem + S.red);  // [stage][warp][16]: 8 score keys, vscale
   float* red_b = reinterpret_cast<float*>(smem + S.redb);        // [stage][5][8] bias partials
   float* q16_s = reinterpret_cast<float*>(smem + S.q16);         // [FP16 slot][kGQ], times scaling*log2(e)
-  float* qhi_s = reinterpret_cast<float*>(smem + S.qhi);         // K positions 128..: q_j[c] 2^(21-Eq)
+  float* qhi_s = reinterpret_cast<float*>(smem + S.qhi);         // K positions 128..: q_j[c] 2^(29-Eq) / w_c
   int* posoff_s = reinterpret_cast<int*>(smem + S.posoff);       // K positions 128..: scale | min << 16, or -1
   unsigned char* stage0 = smem + S.stage0;
   unsigned char* bqk = smem + S.bqk;
@@ -363,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     named_sync(1, kDecThreads);
     const uint32_t mx = max(max(red_m[0], red_m[1]), max(red_m[2], red_m[3]));
     eq = max(-60, min(60, exp2_ceil(__uint_as_float(mx))));
-    const float qscale = exp2i(21 - eq);
+    const float qscale = exp2i(29 - eq);
     po = pos_desc(L, e);
     const float qs1 = po >= 0 ? qscale * exp2i(-pos_lg(po)) : 0.f;
 #pragma unroll
@@ -500,22 +505,27 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     const bool has_pos = tid < S.kpad;           // warp-uniform (K padded to 32)
     const int soff = po >= 0 ? pos_scale(po) : 0, moff = po >= 0 ? pos_min(po) : 0;
     const float mmul = po >= 0 ? exp2i(pos_lg(po)) : 0.f;
-    const float cf = c2 * exp2i(eq - 21);        // fixed-point unit 2^(Eq-21) -> log2-scaled score
+    const float cf = c2 * exp2i(eq - 29);        // fixed-point unit 2^(Eq-29) -> log2-scaled score
     const int bslot = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
 
     // U_K(i): Key codes of the thread's token -> its TMEM lane (A of QK); the
-    // B row of K position tid; bias partials.  Returns the page's Es.
+    // B row of K position tid; bias partials; the token's code sum (every bit
+    // of a code word lands in exactly one masked byte of A, so the A row sums
+    // to the byte sum of the words) into nsum.  Returns the page's Es.
+    int nsum = 0;
     auto unpack_k = [&](int i) -> int {
       const unsigned char* stage = stage0 + (i & 1) * S.stage_bytes;
       const uint32_t* rowp = reinterpret_cast<const uint32_t*>(stage) + row_off;
       const uint16_t* meta = reinterpret_cast<const uint16_t*>(stage + S.rows_bytes);
       uint32_t col = tm_a;
+      uint32_t ns = 0u;
       {
         const uint32_t* src = rowp + co0;
 #pragma unroll 4
         for (int w = 0; w < wd0; ++w) {
           const uint32_t x = src[w];
           tmem_st_x4(col + 4 * w, x & kM2, x & (kM2 << 2), x & (kM2 << 4), x & (kM2 << 6));
+          ns = __dp4a(x, 0x01010101u, ns);
         }
         col += 4 * wd0;
       }
@@ -525,14 +535,20 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
         for (int w = 0; w < wd1; ++w) {
           const uint32_t x = src[w];
           tmem_st_x2(col + 2 * w, x & kM4, x & (kM4 << 4));
+          ns = __dp4a(x, 0x01010101u, ns);
         }
         col += 2 * wd1;
       }
       {
         const uint32_t* src = rowp + co2;
 #pragma unroll 4
-        for (int w = 0; w < wd2; ++w) tmem_st_x1(col + w, src[w]);
+        for (int w = 0; w < wd2; ++w) {
+          const uint32_t x = src[w];
+          tmem_st_x1(col + w, x);
+          ns = __dp4a(x, 0x01010101u, ns);
+        }
       }
+      nsum = static_cast<int>(ns);
       const int esc = page_scale_exp(meta, kmax_off);
       const float fsc = exp2i(-esc);
       if (has_pos) {
@@ -590,19 +606,20 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       }
       const float vs = half_bits_to_float(row16[w3]);
       const float vm = half_bits_to_float(row16[w3 + 1]);
-      const float f = cf * exp2i(esc), f16 = f * 65536.f;
+      const float f = cf * exp2i(esc), f16 = f * 65536.f, f24 = f * 16777216.f;
+      const int off64 = 64 * nsum;  // offset 2^30 = 64 * 2^24 per unit of code
       wait(&bars[kBarQK], st);
       tc_fence_after();
       uint32_t a[32];
       tmem_ld_x32_sync(tm_a + S.tm_qk, a);
-      const int ones64 = static_cast<int>(a[24]) * 64;  // offset 2^22 = 64 * 65536 per unit of code
       float x[GQ];
       uint32_t key[GQ];
 #pragma unroll
       for (int j = 0; j < GQ; ++j) {
         const uint32_t lo = a[j] + (a[8 + j] << 8);
-        const int hi = static_cast<int>(a[16 + j]) - ones64;
-        x[j] = fmaf(static_cast<float>(hi), f16, fmaf(static_cast<float>(lo), f, s16[j]));
+        const int hi = static_cast<int>(a[24 + j]) - off64;
+        x[j] = fmaf(static_cast<float>(hi), f24,
+                    fmaf(static_cast<float>(a[16 + j]), f16, fmaf(static_cast<float>(lo), f, s16[j])));
         key[j] = __reduce_max_sync(0xffffffffu, order_key(x[j]));
       }
       const uint32_t vkey = __reduce_max_sync(0xffffffffu, __float_as_uint(vs));
@@ -650,7 +667,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       }
       {
         uint4 c0, c1;
-        pack_limbs(U, c0, c1, 0u);
+        pack_limbs(U, c0, c1);
         unsigned char* dst = bpv + (tid & 7) * 16 + (tid >> 3) * 128;
         *reinterpret_cast<uint4*>(dst) = c0;
         *reinterpret_cast<uint4*>(dst + 2048) = c1;
@@ -723,13 +740,11 @@ static void* tc_kernel_for(int gq) {
   }
 }
 
-// Largest dynamic shared memory and the full shared-memory carveout, so
-// several CTAs fit on one SM (the occupancy query reads both attributes).
-static cudaError_t configure_tc(void* kern, int smem_bytes) {
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
-  if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
-                              cudaSharedmemCarveoutMaxShared);
+// Dynamic shared-memory limit of the GQ-head kernel raised to at least
+// smem_bytes, with the full shared-memory carveout so several CTAs fit on
+// one SM (the occupancy computation assumes both).
+static cudaError_t configure_tc(int gq, int smem_bytes) {
+  return raise_smem_limit(tc_kernel_for(gq), smem_bytes, true);
 }
 
 // Resident CTAs per SM from the kernel's own limits: registers, shared memory
@@ -744,7 +759,7 @@ int occupancy_tc(const lf_layout& L, int gq, int pps) {
   void* kern = tc_kernel_for(gq);
   cudaFuncAttributes fa;
   int dev = 0, smem_sm = 0, reserved = 0, regs_sm = 0, threads_sm = 0;
-  if (configure_tc(kern, S.total) != cudaSuccess || cudaFuncGetAttributes(&fa, kern) != cudaSuccess ||
+  if (configure_tc(gq, S.total) != cudaSuccess || cudaFuncGetAttributes(&fa, kern) != cudaSuccess ||
       cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess ||
@@ -768,14 +783,12 @@ int launch_partial_tc(const DecodeParams& p, int resid_dtype, int q_dtype, cudaS
   q.q_dtype = q_dtype;
   const tc::TcSmem S = tc::tc_smem(q.L);
   void* kern = tc_kernel_for(q.gq);
-  static std::atomic<int> configured[kGQ + 1];
-  if (S.total > configured[q.gq].load()) {
-    cudaError_t e = configure_tc(kern, S.total);
+  {
+    cudaError_t e = configure_tc(q.gq, S.total);
     if (e != cudaSuccess) {
       set_error("lf_decode_partial (tcgen05): shared memory %d B: %s", S.total, cudaGetErrorString(e));
       return LF_ERR_UNSUPPORTED;
     }
-    configured[q.gq].store(S.total);
   }
   dim3 grid(q.L.kv_heads * q.batch, q.max_splits);
   void* args[] = {&q};

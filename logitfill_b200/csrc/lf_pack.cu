@@ -8,7 +8,6 @@
 // with coalesced stores.  Arithmetic is the reference's, bit for bit:
 // fp32 max/min, IEEE subtract and divide, clamp to [1e-5, 1e5], round half to
 // even, fp16 round-to-nearest-even of the stored scale/min (layout.py:12-18,98-99).
-#include <atomic>
 
 #include "lf_common.cuh"
 
@@ -232,16 +231,12 @@ static int launch_pack(const lf_layout& L, const void* k, const void* v, int64_t
                        int32_t* status, cudaStream_t stream) {
   const PackSmem S = pack_smem(L);
   auto kern = pack_pages_kernel<T>;
-  // Raise the kernel's dynamic shared-memory limit once per size, outside
-  // any later stream capture of the launch.
-  static std::atomic<int> configured{48 * 1024};
-  if (S.total > configured.load()) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S.total);
-    if (e == cudaSuccess) configured.store(S.total);
-    if (e != cudaSuccess) {
-      set_error("lf_pack_pages: shared memory %d B: %s", S.total, cudaGetErrorString(e));
-      return LF_ERR_UNSUPPORTED;
-    }
+  // The limit is raised once per size, outside any later stream capture of
+  // the launch.
+  cudaError_t e = raise_smem_limit(reinterpret_cast<const void*>(kern), S.total, false);
+  if (e != cudaSuccess) {
+    set_error("lf_pack_pages: shared memory %d B: %s", S.total, cudaGetErrorString(e));
+    return LF_ERR_UNSUPPORTED;
   }
   dim3 grid(n_jobs, L.kv_heads);
   kern<<<grid, kPackThreads, S.total, stream>>>(L, static_cast<const T*>(k), static_cast<const T*>(v),

@@ -97,6 +97,9 @@ class _Layer:
             raise RuntimeError(f"tensors must be on {c.device} (the packed backend has no CPU path)")
         self.ensure_residual(key.dtype)
         value = value.to(key.dtype)
+        if key.stride() != value.stride() or key.stride(3) != 1:
+            # K1 reads both pages with one set of strides.
+            key, value = key.contiguous(), value.contiguous()
         P = c.page_size
         need = max(self.hist_len[b] + ((self.tail_len[b] + T) // P) * P for b in seqs)
         if need > self.layout.row_cap:
@@ -318,6 +321,14 @@ class PackedKVManager:
         if layer_idx == len(self.layers) - 1:
             self.seq_len = self.layers[layer_idx].length
 
+    def attend(self, layer_idx: int, query: torch.Tensor, key_new: torch.Tensor, value_new: torch.Tensor,
+               scaling: float) -> torch.Tensor:
+        """``packed_attention(self, ...)`` (reference.py:112-116): K2 + K3 over
+        this layer's packed history, residual page and the new token."""
+        from logitfill_b200.packed.attention import packed_attention
+
+        return packed_attention(self, layer_idx, query, key_new, value_new, scaling)
+
 
 try:
     from transformers.cache_utils import Cache as _TransformersCache
@@ -329,10 +340,15 @@ class LogitFillCache(_TransformersCache):
     """HF ``Cache`` shim so ``generate`` can read the packed length (cache.py:149-183)."""
 
     def __init__(self, manager: PackedKVManager):
+        # transformers >= 4.56 wants the layer list (empty here: the packed
+        # store lives in the manager); older versions take no arguments.
         try:
-            super().__init__()
+            super().__init__(layers=[])
         except TypeError:
-            pass
+            try:
+                super().__init__()
+            except TypeError:
+                pass
         self.manager = manager
         self.key_cache = []
         self.value_cache = []
@@ -345,8 +361,11 @@ class LogitFillCache(_TransformersCache):
         return None
 
     def get_mask_sizes(self, cache_position, layer_idx: int = 0):
+        """(kv_length, kv_offset); transformers 4.x passes the query's
+        ``cache_position`` tensor, 5.x its length."""
         del layer_idx
-        return self.manager.seq_len + int(cache_position.shape[0]), 0
+        q_len = int(cache_position) if isinstance(cache_position, int) else int(cache_position.shape[0])
+        return self.manager.seq_len + q_len, 0
 
     def update(self, key_states, value_states, layer_idx, cache_kwargs=None):
         raise RuntimeError("packed attention writes the LogitFill manager directly")

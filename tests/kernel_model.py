@@ -6,11 +6,11 @@ INT8 tensor cores (``tcgen05.mma.kind::i8``):
 * QK: integer Key codes (u8, 0..255; INT2/INT4 codes masked in place, so
   they carry a power-of-two weight w_c that the B row divides out) times the
   per-page products ``q_j[c] * scale_c / w_c`` written as fixed point ``X``
-  (|X| <= 2^21) relative to
-  a power-of-two block exponent (one per query group and page), offset by 2^22
-  so the three limbs (bytes) are unsigned.  A column of ones in the B operand
-  returns sum_c code_c, which removes the offset exactly:
-  ``acc0 + 256 acc1 + 65536 (acc2 - 64 ones)``.
+  (|X| <= 2^29) relative to a power-of-two block exponent (one per query group
+  and page), offset by 2^30 so the four limbs (bytes) are unsigned.  The
+  token's code sum n_t (the byte sum of its code words, computed on the CUDA
+  cores) removes the offset exactly:
+  ``acc0 + 2^8 acc1 + 2^16 acc2 + 2^24 (acc3 - 64 n_t)``.
 * PV: integer Value codes (u8, 0..3) times ``p_t * vscale_t`` written as 23-bit
   unsigned fixed point (three limbs) relative to a per-page exponent (the page's
   largest Value scale: p <= 1 after the max update).
@@ -33,7 +33,7 @@ def _exp2_ceil(x: np.ndarray) -> np.ndarray:
 
 
 def model_attention(layer: orc.OracleLayer, query: np.ndarray, key_new, value_new, scaling: float,
-                    qk_bits: int = 21, pv_bits: int = 23) -> np.ndarray:
+                    qk_bits: int = 29, pv_bits: int = 23) -> np.ndarray:
     """Decode attention of ``query`` ``[n_q, D]`` over ``layer`` (page size 128,
     k_group 128, v_group D) computed with the kernel's fixed-point scheme for
     the packed history and fp32 for the residual.  Returns ``[n_q, D]``."""
@@ -78,12 +78,13 @@ def model_attention(layer: orc.OracleLayer, query: np.ndarray, key_new, value_ne
                 sp = (sc * np.float32(2.0 ** -esc)).astype(np.float32)
                 X = np.rint((qq * sp[None, :]).astype(np.float32)).astype(np.int64)   # [gq, cnt]
                 U = X + (1 << (qk_bits + 1))
-                assert U.min() >= 0 and U.max() < (1 << 24)
+                assert U.min() >= 0 and U.max() < (1 << 31)
                 A = codes.astype(np.int64) * weight[None, :]
                 assert A.max() <= 255
-                acc = [A @ ((U >> (8 * k)) & 0xFF).T for k in range(3)]
-                ones = A.sum(axis=1)[:, None]
-                s_int += acc[0] + 256.0 * acc[1] + 65536.0 * acc[2] - float(1 << (qk_bits + 1)) * ones
+                acc = [A @ ((U >> (8 * k)) & 0xFF).T for k in range(4)]
+                n_t = A.sum(axis=1)[:, None]
+                s_int += (acc[0] + 256.0 * acc[1] + 65536.0 * acc[2] + 16777216.0 * acc[3]
+                          - float(1 << (qk_bits + 1)) * n_t)
                 bias += (q[:, idx].astype(np.float64) @ mn.astype(np.float64))
             scale_qk = np.ldexp(1.0, eq + esc - qk_bits)            # per q-head
             s = s_int * scale_qk[None, :] + bias[None, :]

@@ -193,3 +193,25 @@ def test_single_call_matches_partial_then_merge():
             torch.cuda.synchronize()
             assert torch.equal(one, two), (pps, dt)
     cache.check_status()
+
+
+@pytest.mark.parametrize("q_scale", [1.0, 6.0])
+def test_sharp_attention_tc_path(q_scale):
+    """Large scores (scaled queries, sharp softmax) on the tensor-core path:
+    the QK fixed point keeps the error far inside the bound (5e-4, 4x tighter
+    than the decode tolerance) where 21-bit QK limbs would leave it."""
+    H, NQ, D, T = 4, 28, 128, 2048
+    levels = synthetic_levels(1, H, D, 2.5, seed=4)[0]
+    k, v = synthetic_kv(1, H, T + 40, D, seed=4, layer=0, device="cuda")
+    mgr = PackedKVCache([levels], 1, NQ, H, D, device="cuda", capacity=T + 128)
+    mgr.prefill(0, k, v, [T + 37])
+    g = torch.Generator(device="cuda").manual_seed(5)
+    q = torch.randn(1, NQ, D, generator=g, device="cuda") * q_scale
+    kn, vn = k[:, :, T + 37], v[:, :, T + 37]
+    out = packed_attention_batched(mgr, 0, q, kn, vn, D ** -0.5, out_dtype=torch.float32)
+    ref = orc.OracleLayer(levels, 128, 128, 128, 2)
+    ref.append(k[0, :, :T + 37].float().cpu().numpy(), v[0, :, :T + 37].float().cpu().numpy())
+    want = orc.reference_attention(ref, q[0, :, None].cpu().numpy(), kn[0, :, None].float().cpu().numpy(),
+                                   vn[0, :, None].float().cpu().numpy(), D ** -0.5)
+    ok, err, cos = attention_close(out[0].cpu().numpy(), want[:, 0], atol=5e-4)
+    assert ok, (err, cos)

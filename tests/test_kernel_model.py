@@ -1,10 +1,10 @@
 """CPU check of the tensor-core kernel's fixed-point scheme (tests/kernel_model.py).
 
-The decode kernel multiplies integer codes by 24-bit (QK) and 23-bit (PV)
-fixed-point limbs on the INT8 tensor cores.  The numpy model of that
-arithmetic must stay inside the decode tolerance against the oracle with a wide
-margin (observed ~2e-5 max-abs), and narrower fixed point must not (which is
-why the kernel uses three limbs)."""
+The decode kernel multiplies integer codes by 31-bit (QK, four limbs) and
+23-bit (PV, three limbs) fixed point on the INT8 tensor cores.  The numpy
+model of that arithmetic must stay inside the decode tolerance against the
+oracle with a wide margin (observed ~2e-5 max-abs), also for sharp attention
+(large scores), and narrower fixed point must not."""
 from __future__ import annotations
 
 import numpy as np
@@ -33,6 +33,21 @@ def test_kernel_fixed_point_within_tolerance(target_bit):
     got = model_attention(store, q, kn, vn, 128 ** -0.5)
     ok, err, cos = attention_close(got, want, atol=5e-4)  # 4x tighter than the decode bound
     assert ok, (err, cos)
+
+
+@pytest.mark.parametrize("q_scale", [1.0, 3.0, 6.0])
+def test_sharp_attention_within_tolerance(q_scale):
+    """Scaled queries make the softmax sharp and the scores large; the QK
+    rounding error grows with the score magnitude.  21-bit QK fixed point
+    (three limbs) leaves the 2e-3 bound at the largest scale; 29 bits keep a
+    20x margin."""
+    store, q, kn, vn, _ = _case(2.5, 1024)
+    q = q * q_scale
+    want = orc.reference_attention(store, q[:, None], kn, vn, 128 ** -0.5)[:, 0]
+    ok, err, cos = attention_close(model_attention(store, q, kn, vn, 128 ** -0.5), want, atol=1e-4)
+    assert ok, (err, cos)
+    if q_scale == 6.0:
+        assert not attention_close(model_attention(store, q, kn, vn, 128 ** -0.5, qk_bits=21), want)[0]
 
 
 def test_narrow_fixed_point_would_fail():
