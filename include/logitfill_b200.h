@@ -124,6 +124,11 @@ LF_API size_t lf_decode_workspace_bytes(int batch, int kv_heads, int n_q, int he
  * residual splits (32 residual tokens each, ceil(page_size / 32)). */
 LF_API int lf_decode_max_splits(int64_t max_pages, int pages_per_split, int page_size);
 
+/* As lf_decode_max_splits for calls with q_len query tokens per sequence:
+ * the residual (tail rows + q_len new tokens) takes
+ * ceil((page_size - 1 + q_len) / 32) splits. */
+LF_API int lf_decode_max_splits_multi(int64_t max_pages, int pages_per_split, int page_size, int q_len);
+
 /*
  * K2: split-K GQA decode attention over the packed history plus the
  * original-dtype residual page and the new token (replaces kernel.cu:112-190
@@ -141,9 +146,10 @@ LF_API int lf_decode_max_splits(int64_t max_pages, int pages_per_split, int page
  *   k_new/v_new [batch][H][D] (strides new_seq_stride, new_head_stride), resid_dtype, or NULL
  *   q [batch][n_q][D] (strides q_seq_stride, q_head_stride), dtype q_dtype
  * q-head j of KV head h is h * (n_q / H) + j (repeat_kv, reference.py:10-15).
+ * GQA groups above 8 are split over several CTAs per KV head.
  * status (device int32, may be NULL) is set to LF_ERR_DEVICE_TIMEOUT if a
  * bounded device-side wait expires; the kernel then returns without hanging.
- * Geometry head_dim 128 / page 128 / k_group 128 / v_group 128 / GQA <= 8
+ * Geometry head_dim 128 / page 128 / k_group 128 / v_group 128
  * runs on the tensor cores (tcgen05.mma kind::i8); other supported
  * geometries (head_dim <= 128, page <= 128, k_group == page, v_group ==
  * head_dim) on a CUDA-core kernel.
@@ -181,6 +187,33 @@ LF_API int lf_decode(const lf_layout* layout, const int32_t* rows, const uint16_
                      int64_t q_seq_stride, int64_t q_head_stride, int batch, int n_q, float scaling,
                      int pages_per_split, int max_splits, float* workspace, void* out, int out_dtype,
                      int64_t out_seq_stride, int64_t out_head_stride, int32_t* status, lf_stream_t stream);
+
+/*
+ * K2 then K3 for q_len query tokens per sequence (a chunked prefill over the
+ * packed history, or a decode step when q_len is 1): the dense attention the
+ * reference runs for a multi-token call with history, reference.py:30-56
+ * with the right-aligned causal mask of reference.py:18-27 (it has no kernel
+ * for it).  Every query token sees the packed history and the tail rows;
+ * query token i sees new tokens 0..i.
+ *   k_new/v_new [batch][H][q_len][D] (strides new_seq_stride, new_head_stride,
+ *     new_tok_stride; rows 16-byte aligned), resid_dtype, or NULL
+ *   q [batch][n_q][q_len][D] (strides q_seq_stride, q_head_stride, q_tok_stride)
+ *   out [batch][n_q][q_len][D] (strides out_seq_stride, out_head_stride, out_tok_stride)
+ *   workspace: lf_decode_workspace_bytes(batch, H, n_q * q_len, D, max_splits)
+ *   max_splits >= lf_decode_max_splits_multi(row_cap / page_size, pps, page_size, q_len)
+ * The other arguments are those of lf_decode.  One CTA per split computes up
+ * to 8 (q-head, query token) pairs, so every page is read once per 8 pairs.
+ */
+LF_API int lf_decode_multi(const lf_layout* layout, const int32_t* rows, const uint16_t* kmeta,
+                           const int32_t* slot_chan, const int32_t* hist_tokens, const void* tail_k,
+                           const void* tail_v, int64_t tail_seq_stride, int64_t tail_head_stride,
+                           const int32_t* tail_len, int resid_dtype, const void* k_new, const void* v_new,
+                           int64_t new_seq_stride, int64_t new_head_stride, int64_t new_tok_stride,
+                           const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
+                           int64_t q_tok_stride, int q_len, int batch, int n_q, float scaling,
+                           int pages_per_split, int max_splits, float* workspace, void* out, int out_dtype,
+                           int64_t out_seq_stride, int64_t out_head_stride, int64_t out_tok_stride,
+                           int32_t* status, lf_stream_t stream);
 
 /*
  * K2 + K3 without a caller workspace, for callers that cannot allocate

@@ -1,9 +1,10 @@
 // K2 (split-K GQA decode over packed pages + residual) and K3 (split merge).
 //
-// Work item = (split s, KV head h, sequence b); one 128-thread CTA each.
-// All q-heads of the GQA group are computed together, so each packed page is
-// read from HBM once per KV head (the reference kernel re-reads it once per
-// q-head, kernel.cu:112-190).
+// Work item = (split s, KV head h and virtual-head chunk c, sequence b); one
+// 128-thread CTA each.  All q-heads of the GQA group are computed together
+// (one chunk for a decode step), so each packed page is read from HBM once
+// per KV head (the reference kernel re-reads it once per q-head,
+// kernel.cu:112-190).
 //
 // The packed history is affine per page: a Key channel's scale/min is
 // constant over its k_group tokens and a token's Value scale/min is constant
@@ -59,14 +60,15 @@ decode_partial_simt(DecodeParams p) {
   int* slot16_s = reinterpret_cast<int*>(smem + S.slot16);
   unsigned char* region = smem + S.region;
 
-  const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
+  const int s = blockIdx.x, h = blockIdx.y / p.n_chunks, c = blockIdx.y % p.n_chunks, b = blockIdx.z;
+  const int tid = threadIdx.x;
   const int P = L.page_size, D = L.head_dim, R = L.row_words, H = L.kv_heads;
-  const int GQ = p.gq;
+  const int GQ = p.cg;
   const int pages = p.hist_tokens[b] / P;
   const int n_page_splits = (pages + p.pps - 1) / p.pps;
-  if (s >= n_page_splits + residual_splits(P)) return;
+  if (s >= n_page_splits + residual_splits(P, p.q_len)) return;
 
-  load_query_group<QT>(p, b, h, q_s);
+  load_query_group<QT>(p, b, h, c, q_s);
   // Tier slot -> channel, in history-row order.
   for (int i = tid; i < p.n_slots; i += kDecThreads) {
     int tier = 0, base = 0;
@@ -223,13 +225,13 @@ decode_partial_simt(DecodeParams p) {
       }
     }
   } else {
-    residual_chunk(p, b, h, s - n_page_splits, q_s, region, m, acc, lt);
+    residual_chunk(p, b, h, c, s - n_page_splits, q_s, region, m, acc, lt);
   }
 
-  write_partial(p, b, h, s, tid, acc, m, lt, lvt, red);
+  write_partial(p, item_index(p, b, h, c, s), tid, acc, m, lt, lvt, red);
 }
 
-// K3: one warp per (sequence, q-head).  Lane s (mod 32) reads split s's max
+// K3: one warp per (sequence, virtual head).  Lane s (mod 32) reads split s's max
 // and sum; the global max, the weights exp(m_s - M) and the normaliser are
 // warp reductions; then every lane accumulates two channels per 64 over all
 // splits, the weight of split s broadcast from the lane that computed it.
@@ -240,18 +242,22 @@ constexpr int kMergeWarps = 4;
 template <typename OT>
 __global__ void __launch_bounds__(kMergeWarps * 32)
 decode_merge_kernel(const float* __restrict__ ws, const int32_t* __restrict__ hist_tokens, int batch,
-                    int kv_heads, int n_q, int D, int P, int pps, int max_splits, OT* __restrict__ out,
-                    int64_t out_seq_stride, int64_t out_head_stride) {
+                    int kv_heads, int n_q, int q_len, int cg, int D, int P, int pps, int max_splits,
+                    OT* __restrict__ out, int64_t out_seq_stride, int64_t out_head_stride,
+                    int64_t out_tok_stride) {
   const int lane = threadIdx.x & 31;
   const int task = blockIdx.x * kMergeWarps + (threadIdx.x >> 5);
-  if (task >= batch * n_q) return;
-  const int b = task / n_q, qh = task - b * n_q;
-  const int GQ = n_q / kv_heads, h = qh / GQ, j = qh - h * GQ;
+  const int nv = n_q * q_len;  // virtual heads per sequence
+  if (task >= batch * nv) return;
+  const int b = task / nv, vh = task - b * nv;
+  const int VG = nv / kv_heads, h = vh / VG, v = vh - h * VG;  // virtual head v of KV head h
+  const int c = v / cg, jj = v - c * cg;                       // its chunk and slot in the chunk
+  const int qh = h * (n_q / kv_heads) + v / q_len, qi = v % q_len;
   const int pages = hist_tokens[b] / P;
-  const int n_s = min((pages + pps - 1) / pps + residual_splits(P), max_splits);
-  const int64_t item = static_cast<int64_t>(GQ) * (D + 2);
-  const float* base = ws + (static_cast<int64_t>(b) * kv_heads + h) * max_splits * item;
-  const float* mstat = base + static_cast<int64_t>(GQ) * D + j;  // split s: mstat[s * item], lstat[s * item]
+  const int n_s = min((pages + pps - 1) / pps + residual_splits(P, q_len), max_splits);
+  const int64_t item = static_cast<int64_t>(cg) * (D + 2);
+  const float* base = ws + ((static_cast<int64_t>(b) * kv_heads + h) * (VG / cg) + c) * max_splits * item;
+  const float* mstat = base + static_cast<int64_t>(cg) * D + jj;  // split s: mstat[s * item], lstat[s * item]
   float M = -INFINITY;
   for (int s = lane; s < n_s; s += 32) M = fmaxf(M, mstat[s * item]);
 #pragma unroll
@@ -259,13 +265,13 @@ decode_merge_kernel(const float* __restrict__ ws, const int32_t* __restrict__ hi
   float Lsum = 0.f;
   for (int s = lane; s < n_s; s += 32) {
     const float ms = mstat[s * item];
-    if (ms != -INFINITY) Lsum = fmaf(expf(ms - M), mstat[s * item + GQ], Lsum);
+    if (ms != -INFINITY) Lsum = fmaf(expf(ms - M), mstat[s * item + cg], Lsum);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, o);
   const float inv = Lsum > 0.f ? 1.0f / Lsum : 0.f;
-  OT* o = out + b * out_seq_stride + qh * out_head_stride;
-  const float* vals = base + static_cast<int64_t>(j) * D;
+  OT* o = out + b * out_seq_stride + qh * out_head_stride + qi * out_tok_stride;
+  const float* vals = base + static_cast<int64_t>(jj) * D;
   for (int d0 = 2 * lane; d0 < D; d0 += 64) {
     float a0 = 0.f, a1 = 0.f;
     for (int s0 = 0; s0 < n_s; s0 += 32) {
@@ -301,7 +307,7 @@ static int launch_partial(const DecodeParams& p, cudaStream_t stream) {
     set_error("lf_decode_partial: shared memory %d B: %s", S.total, cudaGetErrorString(e));
     return LF_ERR_UNSUPPORTED;
   }
-  dim3 grid(p.max_splits, p.L.kv_heads, p.batch);
+  dim3 grid(p.max_splits, p.L.kv_heads * p.n_chunks, p.batch);
   kern<<<grid, kDecThreads, S.total, stream>>>(p);
   return launch_status("lf_decode_partial");
 }
@@ -317,11 +323,54 @@ static int dispatch_q(const DecodeParams& p, int q_dtype, cudaStream_t stream) {
   return LF_ERR_INVALID_ARGUMENT;
 }
 
+// Virtual heads per CTA: the largest divisor of gq * q_len that is at most kGQ
+// (the whole GQA group for a decode step with gq <= 8).
+static int chunk_heads(int gq, int q_len) {
+  const int nv = gq * q_len;
+  for (int c = kGQ; c > 1; --c)
+    if (nv % c == 0) return c;
+  return 1;
+}
+
+// K3 over the partials of a call with q_len query tokens per sequence.
+static int launch_merge(const float* workspace, const int32_t* hist_tokens, int batch, int kv_heads, int n_q,
+                        int q_len, int head_dim, int page_size, int pages_per_split, int max_splits, void* out,
+                        int out_dtype, int64_t out_seq_stride, int64_t out_head_stride, int64_t out_tok_stride,
+                        cudaStream_t s) {
+  const int cg = chunk_heads(n_q / kv_heads, q_len);
+  const int64_t tasks = static_cast<int64_t>(batch) * n_q * q_len;
+  const dim3 grid(static_cast<unsigned>((tasks + kMergeWarps - 1) / kMergeWarps));
+  const dim3 block(kMergeWarps * 32);
+  switch (out_dtype) {
+    case LF_F32:
+      decode_merge_kernel<float><<<grid, block, 0, s>>>(workspace, hist_tokens, batch, kv_heads, n_q, q_len, cg,
+                                                        head_dim, page_size, pages_per_split, max_splits,
+                                                        static_cast<float*>(out), out_seq_stride, out_head_stride,
+                                                        out_tok_stride);
+      break;
+    case LF_F16:
+      decode_merge_kernel<__half><<<grid, block, 0, s>>>(workspace, hist_tokens, batch, kv_heads, n_q, q_len, cg,
+                                                         head_dim, page_size, pages_per_split, max_splits,
+                                                         static_cast<__half*>(out), out_seq_stride, out_head_stride,
+                                                         out_tok_stride);
+      break;
+    case LF_BF16:
+      decode_merge_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(
+          workspace, hist_tokens, batch, kv_heads, n_q, q_len, cg, head_dim, page_size, pages_per_split, max_splits,
+          static_cast<__nv_bfloat16*>(out), out_seq_stride, out_head_stride, out_tok_stride);
+      break;
+    default:
+      set_error("lf_decode_merge: out dtype %d", out_dtype);
+      return LF_ERR_INVALID_ARGUMENT;
+  }
+  return launch_status("lf_decode_merge");
+}
+
 }  // namespace lf
 
 extern "C" int lf_decode_occupancy(const lf_layout* layout, int n_q, int pages_per_split) {
   if (layout == nullptr || n_q <= 0 || pages_per_split <= 0 || n_q % layout->kv_heads) return 0;
-  const int gq = n_q / layout->kv_heads;
+  const int gq = lf::chunk_heads(n_q / layout->kv_heads, 1);
   if (lf::tc_supported(*layout, gq, pages_per_split)) return lf::occupancy_tc(*layout, gq, pages_per_split);
   const lf::DecodeSmem S = lf::decode_smem(*layout, lf::n_slots_of(*layout));
   if (S.total > 227 * 1024) return 0;
@@ -345,9 +394,14 @@ extern "C" size_t lf_decode_workspace_bytes(int batch, int kv_heads, int n_q, in
   return static_cast<size_t>(batch) * kv_heads * max_splits * gq * (head_dim + 2) * sizeof(float);
 }
 
+extern "C" int lf_decode_max_splits_multi(int64_t max_pages, int pages_per_split, int page_size, int q_len) {
+  if (max_pages < 0 || pages_per_split <= 0 || page_size <= 0 || q_len <= 0) return 0;
+  return static_cast<int>((max_pages + pages_per_split - 1) / pages_per_split) +
+         lf::residual_splits(page_size, q_len);
+}
+
 extern "C" int lf_decode_max_splits(int64_t max_pages, int pages_per_split, int page_size) {
-  if (max_pages < 0 || pages_per_split <= 0 || page_size <= 0) return 0;
-  return static_cast<int>((max_pages + pages_per_split - 1) / pages_per_split) + lf::residual_splits(page_size);
+  return lf_decode_max_splits_multi(max_pages, pages_per_split, page_size, 1);
 }
 
 namespace lf {
@@ -357,10 +411,10 @@ static int prepare_decode(const char* who, const lf_layout* layout, const int32_
                           const int32_t* slot_chan, const int32_t* hist_tokens, const void* tail_k,
                           const void* tail_v, int64_t tail_seq_stride, int64_t tail_head_stride,
                           const int32_t* tail_len, int resid_dtype, const void* k_new, const void* v_new,
-                          int64_t new_seq_stride, int64_t new_head_stride, const void* q, int q_dtype,
-                          int64_t q_seq_stride, int64_t q_head_stride, int batch, int n_q, float scaling,
-                          int pages_per_split, int max_splits, float* workspace, int32_t* status,
-                          DecodeParams& p) {
+                          int64_t new_seq_stride, int64_t new_head_stride, int64_t new_tok_stride, const void* q,
+                          int q_dtype, int64_t q_seq_stride, int64_t q_head_stride, int64_t q_tok_stride,
+                          int q_len, int batch, int n_q, float scaling, int pages_per_split, int max_splits,
+                          float* workspace, int32_t* status, DecodeParams& p) {
   LF_CHECK_ARG(layout != nullptr, "%s: null layout", who);
   const lf_layout& L = *layout;
   LF_CHECK_ARG(rows && slot_chan && hist_tokens && tail_k && tail_v && tail_len && q && workspace,
@@ -370,8 +424,10 @@ static int prepare_decode(const char* who, const lf_layout* layout, const int32_
                "%s: batch %d, n_q %d, kv_heads %d", who, batch, n_q, L.kv_heads);
   LF_CHECK_ARG(pages_per_split > 0 && max_splits >= 1 && max_splits <= 65535,
                "%s: pages_per_split %d, max_splits %d", who, pages_per_split, max_splits);
-  LF_CHECK_ARG(max_splits >= lf_decode_max_splits(L.row_cap / L.page_size, pages_per_split, L.page_size),
-               "%s: max_splits %d cannot cover row_cap %lld", who, max_splits, (long long)L.row_cap);
+  LF_CHECK_ARG(q_len >= 1 && q_len <= 65535, "%s: q_len %d", who, q_len);
+  LF_CHECK_ARG(max_splits >= lf_decode_max_splits_multi(L.row_cap / L.page_size, pages_per_split, L.page_size, q_len),
+               "%s: max_splits %d cannot cover row_cap %lld with %d query tokens", who, max_splits,
+               (long long)L.row_cap, q_len);
   {
     const int esz = resid_dtype == LF_F32 ? 4 : 2;
     const bool aligned = (reinterpret_cast<uintptr_t>(tail_k) % 16 == 0) &&
@@ -379,7 +435,8 @@ static int prepare_decode(const char* who, const lf_layout* layout, const int32_
                          (tail_seq_stride * esz) % 16 == 0 && (tail_head_stride * esz) % 16 == 0 &&
                          (k_new == nullptr || ((reinterpret_cast<uintptr_t>(k_new) % 16 == 0) &&
                                                (reinterpret_cast<uintptr_t>(v_new) % 16 == 0) &&
-                                               (new_seq_stride * esz) % 16 == 0 && (new_head_stride * esz) % 16 == 0));
+                                               (new_seq_stride * esz) % 16 == 0 && (new_head_stride * esz) % 16 == 0 &&
+                                               (new_tok_stride * esz) % 16 == 0));
     LF_CHECK_ARG(aligned, "%s: residual / new-token rows must be 16-byte aligned", who);
   }
   LF_CHECK_ARG(resid_dtype == LF_F32 || resid_dtype == LF_F16 || resid_dtype == LF_BF16, "%s: residual dtype %d",
@@ -395,7 +452,9 @@ static int prepare_decode(const char* who, const lf_layout* layout, const int32_
                      "decode head_dim %d not supported", L.head_dim);
   LF_CHECK_SUPPORTED(L.page_size <= kDecThreads && L.page_size % 4 == 0,
                      "decode page_size %d must be a multiple of 4 and at most %d", L.page_size, kDecThreads);
-  LF_CHECK_SUPPORTED(n_q / L.kv_heads <= kGQ, "decode GQA group %d > %d", n_q / L.kv_heads, kGQ);
+  const int gq = n_q / L.kv_heads, cg = chunk_heads(gq, q_len), n_chunks = gq * q_len / cg;
+  LF_CHECK_SUPPORTED(static_cast<int64_t>(L.kv_heads) * n_chunks <= 65535, "%s: %d KV heads x %d head chunks",
+                     who, L.kv_heads, n_chunks);
   p = DecodeParams{};
   p.L = L;
   p.rows = rows;
@@ -411,12 +470,17 @@ static int prepare_decode(const char* who, const lf_layout* layout, const int32_
   p.v_new = v_new;
   p.new_seq_stride = new_seq_stride;
   p.new_head_stride = new_head_stride;
+  p.new_tok_stride = new_tok_stride;
   p.q = q;
   p.q_seq_stride = q_seq_stride;
   p.q_head_stride = q_head_stride;
+  p.q_tok_stride = q_tok_stride;
+  p.q_len = q_len;
+  p.cg = cg;
+  p.n_chunks = n_chunks;
   p.batch = batch;
   p.n_q = n_q;
-  p.gq = n_q / L.kv_heads;
+  p.gq = gq;
   p.pps = pages_per_split;
   p.max_splits = max_splits;
   p.n_slots = n_slots_of(L);
@@ -430,7 +494,7 @@ static int prepare_decode(const char* who, const lf_layout* layout, const int32_
 
 // K2 on the kernel the geometry selects.
 static int launch_decode(const DecodeParams& p, cudaStream_t s) {
-  if (tc_supported(p.L, p.gq, p.pps)) return launch_partial_tc(p, p.resid_dtype, p.q_dtype, s);
+  if (tc_supported(p.L, p.cg, p.pps)) return launch_partial_tc(p, p.resid_dtype, p.q_dtype, s);
   LF_CHECK_SUPPORTED(decode_smem(p.L, p.n_slots).total <= 227 * 1024, "decode shared memory %d B too large",
                      decode_smem(p.L, p.n_slots).total);
   switch (p.resid_dtype) {
@@ -454,8 +518,8 @@ extern "C" int lf_decode_partial(const lf_layout* layout, const int32_t* rows, c
   lf::DecodeParams p;
   const int st = lf::prepare_decode("lf_decode_partial", layout, rows, kmeta, slot_chan, hist_tokens, tail_k, tail_v,
                                     tail_seq_stride, tail_head_stride, tail_len, resid_dtype, k_new, v_new,
-                                    new_seq_stride, new_head_stride, q, q_dtype, q_seq_stride, q_head_stride, batch,
-                                    n_q, scaling, pages_per_split, max_splits, workspace, status, p);
+                                    new_seq_stride, new_head_stride, 0, q, q_dtype, q_seq_stride, q_head_stride, 0, 1,
+                                    batch, n_q, scaling, pages_per_split, max_splits, workspace, status, p);
   if (st != LF_OK) return st;
   return lf::launch_decode(p, reinterpret_cast<cudaStream_t>(stream));
 }
@@ -468,19 +532,39 @@ extern "C" int lf_decode(const lf_layout* layout, const int32_t* rows, const uin
                          int64_t q_seq_stride, int64_t q_head_stride, int batch, int n_q, float scaling,
                          int pages_per_split, int max_splits, float* workspace, void* out, int out_dtype,
                          int64_t out_seq_stride, int64_t out_head_stride, int32_t* status, lf_stream_t stream) {
+  return lf_decode_multi(layout, rows, kmeta, slot_chan, hist_tokens, tail_k, tail_v, tail_seq_stride,
+                         tail_head_stride, tail_len, resid_dtype, k_new, v_new, new_seq_stride, new_head_stride, 0, q,
+                         q_dtype, q_seq_stride, q_head_stride, 0, 1, batch, n_q, scaling, pages_per_split,
+                         max_splits, workspace, out, out_dtype, out_seq_stride, out_head_stride, 0, status, stream);
+}
+
+extern "C" int lf_decode_multi(const lf_layout* layout, const int32_t* rows, const uint16_t* kmeta,
+                               const int32_t* slot_chan, const int32_t* hist_tokens, const void* tail_k,
+                               const void* tail_v, int64_t tail_seq_stride, int64_t tail_head_stride,
+                               const int32_t* tail_len, int resid_dtype, const void* k_new, const void* v_new,
+                               int64_t new_seq_stride, int64_t new_head_stride, int64_t new_tok_stride,
+                               const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
+                               int64_t q_tok_stride, int q_len, int batch, int n_q, float scaling,
+                               int pages_per_split, int max_splits, float* workspace, void* out, int out_dtype,
+                               int64_t out_seq_stride, int64_t out_head_stride, int64_t out_tok_stride,
+                               int32_t* status, lf_stream_t stream) {
   lf::DecodeParams p;
   const int st = lf::prepare_decode("lf_decode", layout, rows, kmeta, slot_chan, hist_tokens, tail_k, tail_v,
                                     tail_seq_stride, tail_head_stride, tail_len, resid_dtype, k_new, v_new,
-                                    new_seq_stride, new_head_stride, q, q_dtype, q_seq_stride, q_head_stride, batch,
-                                    n_q, scaling, pages_per_split, max_splits, workspace, status, p);
+                                    new_seq_stride, new_head_stride, new_tok_stride, q, q_dtype, q_seq_stride,
+                                    q_head_stride, q_tok_stride, q_len, batch, n_q, scaling, pages_per_split,
+                                    max_splits, workspace, status, p);
   if (st != LF_OK) return st;
   LF_CHECK_ARG(out != nullptr, "lf_decode: null output");
   LF_CHECK_ARG(out_dtype == LF_F32 || out_dtype == LF_F16 || out_dtype == LF_BF16, "lf_decode: out dtype %d",
                out_dtype);
-  const int k2 = lf::launch_decode(p, reinterpret_cast<cudaStream_t>(stream));
+  LF_CHECK_ARG(layout->head_dim % 2 == 0, "lf_decode: head_dim %d must be even", layout->head_dim);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int k2 = lf::launch_decode(p, s);
   if (k2 != LF_OK) return k2;
-  return lf_decode_merge(workspace, hist_tokens, batch, layout->kv_heads, n_q, layout->head_dim, layout->page_size,
-                         pages_per_split, max_splits, out, out_dtype, out_seq_stride, out_head_stride, stream);
+  return lf::launch_merge(workspace, hist_tokens, batch, layout->kv_heads, n_q, q_len, layout->head_dim,
+                          layout->page_size, pages_per_split, max_splits, out, out_dtype, out_seq_stride,
+                          out_head_stride, out_tok_stride, s);
 }
 
 extern "C" int lf_decode_merge(const float* workspace, const int32_t* hist_tokens, int batch,
@@ -493,29 +577,7 @@ extern "C" int lf_decode_merge(const float* workspace, const int32_t* hist_token
                "lf_decode_merge: batch %d n_q %d kv_heads %d", batch, n_q, kv_heads);
   LF_CHECK_ARG(page_size > 0 && pages_per_split > 0 && max_splits > 0 && head_dim > 0 && head_dim % 2 == 0,
                "lf_decode_merge: bad sizes");
-  const int tasks = batch * n_q;
-  const dim3 grid((tasks + lf::kMergeWarps - 1) / lf::kMergeWarps);
-  const dim3 block(lf::kMergeWarps * 32);
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  switch (out_dtype) {
-    case LF_F32:
-      lf::decode_merge_kernel<float><<<grid, block, 0, s>>>(workspace, hist_tokens, batch, kv_heads, n_q, head_dim,
-                                                            page_size, pages_per_split, max_splits,
-                                                            static_cast<float*>(out), out_seq_stride, out_head_stride);
-      break;
-    case LF_F16:
-      lf::decode_merge_kernel<__half><<<grid, block, 0, s>>>(workspace, hist_tokens, batch, kv_heads, n_q, head_dim,
-                                                             page_size, pages_per_split, max_splits,
-                                                             static_cast<__half*>(out), out_seq_stride, out_head_stride);
-      break;
-    case LF_BF16:
-      lf::decode_merge_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(
-          workspace, hist_tokens, batch, kv_heads, n_q, head_dim, page_size, pages_per_split, max_splits,
-          static_cast<__nv_bfloat16*>(out), out_seq_stride, out_head_stride);
-      break;
-    default:
-      lf::set_error("lf_decode_merge: out dtype %d", out_dtype);
-      return LF_ERR_INVALID_ARGUMENT;
-  }
-  return lf::launch_status("lf_decode_merge");
+  return lf::launch_merge(workspace, hist_tokens, batch, kv_heads, n_q, 1, head_dim, page_size, pages_per_split,
+                          max_splits, out, out_dtype, out_seq_stride, out_head_stride, 0,
+                          reinterpret_cast<cudaStream_t>(stream));
 }

@@ -1,6 +1,15 @@
 // Pieces shared by the decode kernels: launch parameters, CTA reductions,
-// the residual split (original-dtype tail rows + new token) and the partial
+// the residual split (original-dtype tail rows + new tokens) and the partial
 // writer read by the merge kernel.
+//
+// Query tokens.  A call attends q_len query tokens per sequence (1 for a
+// decode step, more for a chunked prefill over the packed history).  The
+// kernels see "virtual heads": KV head h owns gq * q_len of them, v = j * q_len
+// + i for q-head h * gq + j and query token i, and one CTA takes cg of them
+// (chunk c = v / cg, n_chunks = gq * q_len / cg chunks per KV head).  Every
+// virtual head sees the whole packed history and residual page; of the q_len
+// new tokens, query token i sees tokens 0..i (the causal mask aligned to the
+// right edge, reference.py:18-27).
 #pragma once
 
 #include "lf_common.cuh"
@@ -23,10 +32,11 @@ struct DecodeParams {
   const int32_t* tail_len;
   const void* k_new;
   const void* v_new;
-  int64_t new_seq_stride, new_head_stride;
+  int64_t new_seq_stride, new_head_stride, new_tok_stride;
   const void* q;
-  int64_t q_seq_stride, q_head_stride;
+  int64_t q_seq_stride, q_head_stride, q_tok_stride;
   int batch, n_q, gq, pps, max_splits, n_slots;
+  int q_len, cg, n_chunks;  // query tokens; virtual heads per CTA; CTAs per KV head and split
   float scaling;
   float* ws;
   int32_t* status;  // device status word (LF_ERR_DEVICE_TIMEOUT on a timed-out wait), may be null
@@ -63,15 +73,28 @@ __device__ __forceinline__ void block_reduce8(float (&v)[kGQ], float* red) {
   __syncthreads();
 }
 
-// Query group of KV head h (q-heads h*GQ .. h*GQ+GQ-1, the repeat_kv order
-// of reference.py:10-15) into q_s [kGQ][D] fp32, zero-padded to kGQ heads.
+// Element offset of virtual head v of KV head h in sequence b's query
+// (q-head h * gq + v / q_len, the repeat_kv order of reference.py:10-15;
+// query token v % q_len).
+__device__ __forceinline__ int64_t vhead_q_offset(const DecodeParams& p, int b, int h, int v) {
+  const int j = v / p.q_len, i = v - j * p.q_len;
+  return b * p.q_seq_stride + static_cast<int64_t>(h * p.gq + j) * p.q_head_stride +
+         static_cast<int64_t>(i) * p.q_tok_stride;
+}
+// Index of the partial record of (sequence b, KV head h, chunk c, split s).
+__device__ __forceinline__ int64_t item_index(const DecodeParams& p, int b, int h, int c, int s) {
+  return ((static_cast<int64_t>(b) * p.L.kv_heads + h) * p.n_chunks + c) * p.max_splits + s;
+}
+
+// Virtual heads c*cg .. c*cg+cg-1 of KV head h into q_s [kGQ][D] fp32,
+// zero-padded to kGQ heads.
 template <typename QT>
-__device__ __forceinline__ void load_query_group(const DecodeParams& p, int b, int h, float* q_s) {
+__device__ __forceinline__ void load_query_group(const DecodeParams& p, int b, int h, int c, float* q_s) {
   const int D = p.L.head_dim;
-  const QT* qb = static_cast<const QT*>(p.q) + b * p.q_seq_stride;
+  const QT* q = static_cast<const QT*>(p.q);
   for (int i = threadIdx.x; i < kGQ * D; i += kDecThreads) {
     const int j = i / D, d = i - j * D;
-    q_s[i] = j < p.gq ? Scalar<QT>::load(qb + (h * p.gq + j) * p.q_head_stride + d) : 0.0f;
+    q_s[i] = j < p.cg ? Scalar<QT>::load(q + vhead_q_offset(p, b, h, c * p.cg + j) + d) : 0.0f;
   }
 }
 
@@ -83,12 +106,12 @@ __device__ __forceinline__ float load_dtype(const void* base, int64_t idx, int d
   }
 }
 // Query group as load_query_group, dtype chosen at run time (p.q_dtype).
-__device__ __forceinline__ void load_query_group_rt(const DecodeParams& p, int b, int h, float* q_s, int nthreads) {
+__device__ __forceinline__ void load_query_group_rt(const DecodeParams& p, int b, int h, int c, float* q_s,
+                                                    int nthreads) {
   const int D = p.L.head_dim;
   for (int i = threadIdx.x; i < kGQ * D; i += nthreads) {
     const int j = i / D, d = i - j * D;
-    q_s[i] = j < p.gq ? load_dtype(p.q, b * p.q_seq_stride + (h * p.gq + j) * p.q_head_stride + d, p.q_dtype)
-                      : 0.0f;
+    q_s[i] = j < p.cg ? load_dtype(p.q, vhead_q_offset(p, b, h, c * p.cg + j) + d, p.q_dtype) : 0.0f;
   }
 }
 
@@ -119,10 +142,12 @@ __device__ __forceinline__ void group_sum(float (&v)[N], float* red, int bar_id)
 }
 
 // Residual splits: chunk c of the original-dtype residual (tail_len[b] tail
-// rows followed by the new token; reference.py:38-42) covers tokens
-// [kResChunk*c, kResChunk*(c+1)).  Up to ceil(page/kResChunk) chunks, one work
-// item each, so the residual is spread over several CTAs.
-__host__ __device__ inline int residual_splits(int page_size) { return (page_size + kResChunk - 1) / kResChunk; }
+// rows followed by the q_len new tokens; reference.py:38-42) covers tokens
+// [kResChunk*c, kResChunk*(c+1)).  Up to ceil((page - 1 + q_len)/kResChunk)
+// chunks, one work item each, so the residual is spread over several CTAs.
+__host__ __device__ inline int residual_splits(int page_size, int q_len) {
+  return (page_size - 1 + q_len + kResChunk - 1) / kResChunk;
+}
 
 struct ResidSmem {
   int k, v, part, p, stat, total;  // byte offsets from the region base
@@ -184,11 +209,11 @@ __device__ __forceinline__ void load_vec_to_float_rt(const void* src, int dtype,
   }
 }
 
-static __device__ __forceinline__ void residual_chunk(const DecodeParams& p, int b, int h, int chunk, const float* q_s,
-                                            unsigned char* region, float (&m)[kGQ], float (&acc)[kGQ],
-                                            float (&lt)[kGQ]) {
+static __device__ __forceinline__ void residual_chunk(const DecodeParams& p, int b, int h, int vc, int chunk,
+                                                      const float* q_s, unsigned char* region, float (&m)[kGQ],
+                                                      float (&acc)[kGQ], float (&lt)[kGQ]) {
   const int RS_ = p.resid_dtype == LF_F32 ? 4 : 2;  // element size
-  const int D = p.L.head_dim, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, GQ = p.gq;
+  const int D = p.L.head_dim, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, GQ = p.cg;
   const ResidSmem RS = resid_smem(D);
   float* k_s = reinterpret_cast<float*>(region + RS.k);
   float* v_s = reinterpret_cast<float*>(region + RS.v);
@@ -196,7 +221,7 @@ static __device__ __forceinline__ void residual_chunk(const DecodeParams& p, int
   float* p_s = reinterpret_cast<float*>(region + RS.p);
   float* stat = reinterpret_cast<float*>(region + RS.stat);
   const int tl = p.tail_len[b];
-  const int total = tl + (p.k_new != nullptr ? 1 : 0);
+  const int total = tl + (p.k_new != nullptr ? p.q_len : 0);
   const int t0 = chunk * kResChunk;
   const int ntok = min(kResChunk, total - t0);
   if (ntok <= 0) return;
@@ -219,8 +244,8 @@ static __device__ __forceinline__ void residual_chunk(const DecodeParams& p, int
     const int t = i / vec_per_row, c = i - t * vec_per_row;
     const int tok = t0 + t;
     if (i < nvec && t < ntok) {
-      const char* ks = tok < tl ? tk + static_cast<int64_t>(tok) * D * RS_ : nk;
-      const char* vs = tok < tl ? tv + static_cast<int64_t>(tok) * D * RS_ : nv;
+      const char* ks = tok < tl ? tk + static_cast<int64_t>(tok) * D * RS_ : nk + (tok - tl) * p.new_tok_stride * RS_;
+      const char* vs = tok < tl ? tv + static_cast<int64_t>(tok) * D * RS_ : nv + (tok - tl) * p.new_tok_stride * RS_;
       load_vec_to_float_rt(ks + c * 8 * RS_, p.resid_dtype, kv[r]);
       load_vec_to_float_rt(vs + c * 8 * RS_, p.resid_dtype, vv[r]);
     } else {
@@ -255,12 +280,14 @@ static __device__ __forceinline__ void residual_chunk(const DecodeParams& p, int
     *reinterpret_cast<float4*>(dst + 4) = make_float4(ps[4], ps[5], ps[6], ps[7]);
   }
   named_sync(1, kDecThreads);
-  // 3. Softmax statistics of the chunk in warp 0 (lane = token).
+  // 3. Softmax statistics of the chunk in warp 0 (lane = token).  New token
+  // r (row tl + r) is visible to virtual heads of query token i >= r.
   if (warp == 0) {
+    const int rnew = t0 + lane - tl;  // new-token index of this row, < 0 for a tail row
 #pragma unroll
     for (int j = 0; j < kGQ; ++j) {
       float sj = -INFINITY;
-      if (lane < ntok && j < GQ) {
+      if (lane < ntok && j < GQ && rnew <= (vc * GQ + j) % p.q_len) {
         sj = (part[(0 * kResChunk + lane) * kGQ + j] + part[(1 * kResChunk + lane) * kGQ + j]) +
              (part[(2 * kResChunk + lane) * kGQ + j] + part[(3 * kResChunk + lane) * kGQ + j]);
         sj *= p.scaling;
@@ -308,15 +335,15 @@ static __device__ __forceinline__ void residual_chunk(const DecodeParams& p, int
   }
 }
 
-// Partial writer for the first 128 threads only (barrier `bar_id`), N >= p.gq.
+// Partial writer for the first 128 threads only (barrier `bar_id`), N >= p.cg.
 template <int N>
-__device__ __forceinline__ void write_partial_group(const DecodeParams& p, int b, int h, int s, int channel,
+__device__ __forceinline__ void write_partial_group(const DecodeParams& p, int64_t index, int channel,
                                                     const float (&acc)[N], const float (&m)[N],
                                                     float (&lt)[N], float (&lvt)[N], float* red, int bar_id) {
-  const int D = p.L.head_dim, GQ = p.gq, H = p.L.kv_heads;
+  const int D = p.L.head_dim, GQ = p.cg;
   group_sum<N>(lt, red, bar_id);
   group_sum<N>(lvt, red, bar_id);
-  float* item = p.ws + ((static_cast<int64_t>(b) * H + h) * p.max_splits + s) * (GQ * (D + 2));
+  float* item = p.ws + index * (GQ * (D + 2));
   if (channel >= 0 && channel < D) {
 #pragma unroll
     for (int j = 0; j < N; ++j)
@@ -335,13 +362,13 @@ __device__ __forceinline__ void write_partial_group(const DecodeParams& p, int b
 
 // Write one work item's partial: acc[j][d] + lv[j], m[j] (natural-log units), l[j].
 // lt/lvt are per-thread partial sums, reduced here over the CTA.
-__device__ __forceinline__ void write_partial(const DecodeParams& p, int b, int h, int s, int channel,
+__device__ __forceinline__ void write_partial(const DecodeParams& p, int64_t index, int channel,
                                               const float (&acc)[kGQ], const float (&m)[kGQ],
                                               float (&lt)[kGQ], float (&lvt)[kGQ], float* red) {
-  const int D = p.L.head_dim, GQ = p.gq, H = p.L.kv_heads;
+  const int D = p.L.head_dim, GQ = p.cg;
   block_reduce8<false>(lt, red);
   block_reduce8<false>(lvt, red);
-  float* item = p.ws + ((static_cast<int64_t>(b) * H + h) * p.max_splits + s) * (GQ * (D + 2));
+  float* item = p.ws + index * (GQ * (D + 2));
   if (channel >= 0 && channel < D) {
 #pragma unroll
     for (int j = 0; j < kGQ; ++j)

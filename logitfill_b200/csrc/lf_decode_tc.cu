@@ -255,15 +255,17 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
   extern __shared__ __align__(1024) unsigned char smem[];
   const lf_layout& L = p.L;
   const TcSmem S = tc_smem(L);
-  // Grid: x = (sequence, KV head) pair, y = split.  Blocks launch in x-fastest
-  // order, so every pair's first splits start together and the short residual
-  // splits (the last y) take the SMs the page splits leave.
-  const int s = blockIdx.y, h = blockIdx.x % p.L.kv_heads, b = blockIdx.x / p.L.kv_heads, tid = threadIdx.x;
+  // Grid: x = (sequence, KV head, virtual-head chunk), y = split.  Blocks
+  // launch in x-fastest order, so every pair's first splits start together and
+  // the short residual splits (the last y) take the SMs the page splits leave.
+  const int s = blockIdx.y, tid = threadIdx.x;
+  const int pair = blockIdx.x / p.n_chunks, vc = blockIdx.x - pair * p.n_chunks;
+  const int h = pair % p.L.kv_heads, b = pair / p.L.kv_heads;
   const int lane = tid & 31, warp = tid >> 5;
   const int H = L.kv_heads, R = L.row_words, M = L.meta_halves;
   const int pages = p.hist_tokens[b] / kP;
   const int n_page_splits = (pages + p.pps - 1) / p.pps;
-  if (s >= n_page_splits + residual_splits(kP)) return;
+  if (s >= n_page_splits + residual_splits(kP, p.q_len)) return;
 
   float* q_s = reinterpret_cast<float*>(smem + S.qs);
   float* red_w = reinterpret_cast<float*>(smem + S.redw);
@@ -275,10 +277,9 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       m[j] = -INFINITY;
       o[j] = lt[j] = lvt[j] = 0.f;
     }
-    load_query_group_rt(p, b, h, q_s, kDecThreads);
-    const int c = s - n_page_splits;
-    residual_chunk(p, b, h, c, q_s, smem + S.stage0, m, o, lt);
-    write_partial_group<kGQ>(p, b, h, s, tid, o, m, lt, lvt, red_w, 1);
+    load_query_group_rt(p, b, h, vc, q_s, kDecThreads);
+    residual_chunk(p, b, h, vc, s - n_page_splits, q_s, smem + S.stage0, m, o, lt);
+    write_partial_group<kGQ>(p, item_index(p, b, h, vc, s), tid, o, m, lt, lvt, red_w, 1);
     return;
   }
 
@@ -342,19 +343,21 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     const int ch16 = tid < n16 ? p.slot_chan[(3 * H + h) * kD + tid / kGQ] : -1;
     float qc[kGQ];
     {
-      const int64_t base = b * p.q_seq_stride + static_cast<int64_t>(h) * p.gq * p.q_head_stride + tid;
+      int64_t off[kGQ];
+#pragma unroll
+      for (int j = 0; j < kGQ; ++j) off[j] = j < GQ ? vhead_q_offset(p, b, h, vc * GQ + j) + tid : 0;
       if (p.q_dtype == LF_F32) {
-        const float* qp = static_cast<const float*>(p.q) + base;
+        const float* qp = static_cast<const float*>(p.q);
 #pragma unroll
-        for (int j = 0; j < kGQ; ++j) qc[j] = j < GQ ? qp[j * p.q_head_stride] : 0.f;
+        for (int j = 0; j < kGQ; ++j) qc[j] = j < GQ ? qp[off[j]] : 0.f;
       } else if (p.q_dtype == LF_F16) {
-        const __half* qp = static_cast<const __half*>(p.q) + base;
+        const __half* qp = static_cast<const __half*>(p.q);
 #pragma unroll
-        for (int j = 0; j < kGQ; ++j) qc[j] = j < GQ ? __half2float(qp[j * p.q_head_stride]) : 0.f;
+        for (int j = 0; j < kGQ; ++j) qc[j] = j < GQ ? __half2float(qp[off[j]]) : 0.f;
       } else {
-        const __nv_bfloat16* qp = static_cast<const __nv_bfloat16*>(p.q) + base;
+        const __nv_bfloat16* qp = static_cast<const __nv_bfloat16*>(p.q);
 #pragma unroll
-        for (int j = 0; j < kGQ; ++j) qc[j] = j < GQ ? __bfloat162float(qp[j * p.q_head_stride]) : 0.f;
+        for (int j = 0; j < kGQ; ++j) qc[j] = j < GQ ? __bfloat162float(qp[off[j]]) : 0.f;
       }
     }
     float qmax = 0.f;
@@ -700,7 +703,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     for (int j = 0; j < GQ; ++j) mg[j] = __shfl_sync(0xffffffffu, m_l, j) * kLn2;  // natural-log units
     // PV row t holds head-dim channel d(t): t = 16w + 4k + i  <->  d = 16w + k + 4i.
     const int d = (tid & ~15) + ((tid & 15) >> 2) + 4 * (tid & 3);
-    write_partial_group<GQ>(p, b, h, s, d, og, mg, lt, lvt, red_w, 1);
+    write_partial_group<GQ>(p, item_index(p, b, h, vc, s), d, og, mg, lt, lvt, red_w, 1);
   }
   tc_fence_before();
   __syncthreads();  // compute warps finished (their partial is written); copies and MMAs drained
@@ -782,15 +785,15 @@ int launch_partial_tc(const DecodeParams& p, int resid_dtype, int q_dtype, cudaS
   q.resid_dtype = resid_dtype;
   q.q_dtype = q_dtype;
   const tc::TcSmem S = tc::tc_smem(q.L);
-  void* kern = tc_kernel_for(q.gq);
+  void* kern = tc_kernel_for(q.cg);
   {
-    cudaError_t e = configure_tc(q.gq, S.total);
+    cudaError_t e = configure_tc(q.cg, S.total);
     if (e != cudaSuccess) {
       set_error("lf_decode_partial (tcgen05): shared memory %d B: %s", S.total, cudaGetErrorString(e));
       return LF_ERR_UNSUPPORTED;
     }
   }
-  dim3 grid(q.L.kv_heads * q.batch, q.max_splits);
+  dim3 grid(q.L.kv_heads * q.batch * q.n_chunks, q.max_splits);
   void* args[] = {&q};
   cudaError_t e = cudaLaunchKernel(kern, grid, dim3(tc::kThreads), args, S.total, stream);
   if (e != cudaSuccess) {

@@ -50,6 +50,7 @@ class _Layer:
         self.tail_v: Optional[torch.Tensor] = None
         self.dev_hist = torch.zeros(c.batch, dtype=torch.int32, device=c.device)
         self.dev_tail = torch.zeros(c.batch, dtype=torch.int32, device=c.device)
+        self.pps_memo: dict = {}  # (pages, q_len) -> pages per K2 work item
 
     # -- state -------------------------------------------------------------
     def reset(self) -> None:
@@ -212,8 +213,9 @@ class PackedKVCache:
             if n:
                 self.commit(layer_idx, key[b:b + 1, :, :n], value[b:b + 1, :, :n], seqs=[b])
 
-    def workspace(self, max_splits: int) -> torch.Tensor:
-        need = _lib.lib().lf_decode_workspace_bytes(self.batch, self.n_kv, self.n_q, self.head_dim, max_splits)
+    def workspace(self, max_splits: int, q_len: int = 1) -> torch.Tensor:
+        need = _lib.lib().lf_decode_workspace_bytes(self.batch, self.n_kv, self.n_q * q_len, self.head_dim,
+                                                    max_splits)
         if self._workspace is None or self._workspace.numel() * 4 < need:
             self._workspace = torch.empty(need // 4, dtype=torch.float32, device=self.device)
         return self._workspace

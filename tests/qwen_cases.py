@@ -82,6 +82,17 @@ class OracleManager:
         return torch.from_numpy(out.astype(np.float32))[None].to(device=query.device, dtype=query.dtype)
 
 
+def _steps(ids, prompt_len, chunks=None):
+    """The prompt, then ``chunks`` (token counts; default one token per step)
+    up to the end of ``ids``."""
+    out, t = [ids[:, :prompt_len]], prompt_len
+    for n in (chunks or []):
+        out.append(ids[:, t:t + n])
+        t += n
+    out.extend(ids[:, u:u + 1] for u in range(t, ids.shape[1]))
+    return out
+
+
 def _layer_kv(cache, i):
     if hasattr(cache, "layers") and len(getattr(cache, "layers")) > i and hasattr(cache.layers[i], "keys"):
         return cache.layers[i].keys, cache.layers[i].values
@@ -107,7 +118,7 @@ def _round_trip_pages(cache, n_layers, levels, page, k_group, v_group, start, st
 
 
 @torch.no_grad()
-def fake_quant_logits(model, ids, prompt_len, levels, page, k_group, v_group):
+def fake_quant_logits(model, ids, prompt_len, levels, page, k_group, v_group, chunks=None):
     """Last-position logits of the prefill and of every teacher-forced decode
     step, with page-delayed packed-codec quantization of the dense cache."""
     from transformers import DynamicCache
@@ -119,7 +130,7 @@ def fake_quant_logits(model, ids, prompt_len, levels, page, k_group, v_group):
         cache = DynamicCache()
     outs = []
     done = 0
-    steps = [ids[:, :prompt_len]] + [ids[:, t:t + 1] for t in range(prompt_len, ids.shape[1])]
+    steps = _steps(ids, prompt_len, chunks)
     for chunk in steps:
         out = model(input_ids=chunk, past_key_values=cache, use_cache=True)
         outs.append(out.logits[:, -1].float())
@@ -132,11 +143,11 @@ def fake_quant_logits(model, ids, prompt_len, levels, page, k_group, v_group):
 
 
 @torch.no_grad()
-def adapter_logits(model, adapter, ids, prompt_len):
+def adapter_logits(model, adapter, ids, prompt_len, chunks=None):
     """Same steps through ``adapter`` (packed backend) with its cache handle."""
     cache = adapter.make_cache()
     outs = []
-    steps = [ids[:, :prompt_len]] + [ids[:, t:t + 1] for t in range(prompt_len, ids.shape[1])]
+    steps = _steps(ids, prompt_len, chunks)
     for chunk in steps:
         out = model(input_ids=chunk, past_key_values=cache, use_cache=True)
         outs.append(out.logits[:, -1].float())
@@ -144,7 +155,7 @@ def adapter_logits(model, adapter, ids, prompt_len):
 
 
 @torch.no_grad()
-def stock_logits(model, ids, prompt_len):
+def stock_logits(model, ids, prompt_len, chunks=None):
     """The unmodified model with its own dense cache (no quantization)."""
     from transformers import DynamicCache
 
@@ -153,7 +164,7 @@ def stock_logits(model, ids, prompt_len):
     except TypeError:
         cache = DynamicCache()
     outs = []
-    steps = [ids[:, :prompt_len]] + [ids[:, t:t + 1] for t in range(prompt_len, ids.shape[1])]
+    steps = _steps(ids, prompt_len, chunks)
     for chunk in steps:
         out = model(input_ids=chunk, past_key_values=cache, use_cache=True)
         outs.append(out.logits[:, -1].float())
@@ -172,6 +183,7 @@ class CheckedManager:
         self.real, self.oracle = real, oracle
         self.worst = (0.0, 1.0)
         self.calls = 0
+        self.tokens = 0
 
     def __getattr__(self, name):
         return getattr(self.real, name)
@@ -191,14 +203,14 @@ class CheckedManager:
     def attend(self, layer_idx, query, key_new, value_new, scaling):
         from logitfill_b200.packed.attention import decode_into
 
-        n_q, D = self.real.n_q, self.real.head_dim
-        out = torch.empty(1, n_q, D, dtype=torch.float32, device=query.device)
-        decode_into(self.real.cache, layer_idx, query[:, :, 0], key_new[:, :, 0], value_new[:, :, 0], scaling, out)
+        out = torch.empty(query.shape, dtype=torch.float32, device=query.device)
+        decode_into(self.real.cache, layer_idx, query, key_new, value_new, scaling, out)
         want = orc.reference_attention(self.oracle.layers[layer_idx].layer, _np(query[0]), _np(key_new[0]),
-                                       _np(value_new[0]), scaling)[:, 0]
+                                       _np(value_new[0]), scaling)
         got = out[0].cpu().numpy().astype(np.float64)
         err = float(np.abs(got - want).max())
         cos = float(np.min(np.sum(got * want, -1) / (np.linalg.norm(got, axis=-1) * np.linalg.norm(want, axis=-1))))
         self.worst = (max(self.worst[0], err), min(self.worst[1], cos))
         self.calls += 1
-        return out.to(query.dtype).view(1, n_q, 1, D)
+        self.tokens += query.shape[2]
+        return out.to(query.dtype)

@@ -178,3 +178,21 @@ def test_skip_quant_runs_the_stock_path():
     a = DeepSeekQwenKVAdapter(model, group_size=4, v_group_size=32).attach()
     a.skip_quant = True
     assert _max_abs(stock_logits(model, ids, 8), ref) < 1e-5
+
+
+def test_chunked_continuation_matches_fake_quantization():
+    """A multi-token call with history (a second prefill chunk) goes to the
+    packed attention with the causal mask; its output is laid out
+    [B, q_len, heads, D] before the output projection.  Pages complete inside
+    the chunk."""
+    model = tiny_qwen2(layers=2, n_q=8, n_kv=2, head_dim=128, vocab=128)
+    levels = list(synthetic_levels(2, 2, 128, 2.5, seed=6))
+    ids = torch.randint(0, 128, (1, 80), generator=torch.Generator().manual_seed(3))
+    page, chunks = 16, [23, 5]
+    ref = fake_quant_logits(model, ids, 21, levels, page, page, 128, chunks=chunks)
+    a = DeepSeekQwenKVAdapter(model, group_size=page, v_group_size=128).attach()
+    a.set_k_levels(levels)
+    mgr = _inject(a)
+    got = adapter_logits(model, a, ids, 21, chunks=chunks)
+    assert mgr.seq_len == 80
+    assert _max_abs(got, ref) < 1e-4

@@ -81,3 +81,30 @@ def test_greedy_decode_loop_runs_on_the_packed_path():
         assert mgr.layers[0].hist_len == (prompt_len + 100) // 128 * 128
         assert torch.isfinite(out.logits).all()
     mgr.cache.check_status()
+
+
+@pytest.mark.parametrize("page", [64, 128])
+def test_chunked_prefill_continuation(page):
+    """Prompt, then prefill chunks of 37 and 64 tokens over the packed
+    history (q_len > 1, causal among the chunk's tokens), then decode steps:
+    every call checked against the oracle on the same inputs."""
+    layers, n_q, n_kv, D = 2, 8, 2, 128
+    model = tiny_qwen2(n_q=n_q, n_kv=n_kv, head_dim=D, layers=layers, vocab=512, seed=21, device="cuda",
+                       dtype=torch.bfloat16, attn="sdpa")
+    levels = list(synthetic_levels(layers, n_kv, D, 3.0, seed=21))
+    ids = torch.randint(0, 512, (1, 300), generator=torch.Generator().manual_seed(21)).cuda()
+    a = DeepSeekQwenKVAdapter(model, group_size=page, v_group_size=D).attach()
+    a.set_k_levels(levels)
+    real = a.packed_manager()
+    checked = CheckedManager(real, OracleManager(levels, n_q, n_kv, D, page, page, D))
+    a._packed = checked
+    adapter_logits(model, a, ids, 150, chunks=[37, 64])
+    real.cache.check_status()
+    assert checked.tokens == (300 - 150) * layers and checked.calls == (2 + 300 - 251) * layers
+    err, cos = checked.worst
+    print(f"chunked page {page}: worst attention max-abs {err:.2e}, min cos {cos:.8f}")
+    assert err <= ATOL and cos >= MIN_COS
+    for i in range(layers):
+        got, want = store_arrays(real.layers[i]), layer_arrays(checked.oracle.layers[i].layer)
+        for key in want:
+            assert bit_equal(got[key], want[key]), (i, key)

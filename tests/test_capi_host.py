@@ -108,6 +108,9 @@ def test_entry_points_validate_before_launch():
     assert st == _lib.LF_ERR_UNSUPPORTED
     assert so.lf_decode_merge(None, None, 1, 1, 1, 64, 64, 1, 1, None, 0, 0, 0, None) == _lib.LF_ERR_INVALID_ARGUMENT
     assert so.lf_decode_max_splits(256, 16, 128) == 16 + 4
+    assert so.lf_decode_max_splits_multi(256, 16, 128, 1) == 16 + 4
+    assert so.lf_decode_max_splits_multi(256, 16, 128, 16) == 16 + 5   # 127 tail + 16 new rows
+    assert so.lf_decode_max_splits_multi(256, 16, 128, 0) == 0
     assert so.lf_decode_workspace_bytes(2, 4, 28, 128, 5) == 2 * 4 * 5 * 7 * 130 * 4
 
 
@@ -123,3 +126,11 @@ def test_tier_tables_match_oracle(seed):
             np.testing.assert_array_equal(ours["tiers"][code][key].numpy(), ref[code][key])
         assert ours["tiers"][code]["width"] == ref[code]["width"]
     np.testing.assert_array_equal(ours["tier"].numpy(), ref["tier"])
+
+
+def test_head_chunks():
+    """(q-head, query token) pairs per K2 CTA: the largest divisor <= 8."""
+    from logitfill_b200.packed.attention import chunk_heads
+
+    assert [chunk_heads(7, 1), chunk_heads(7, 2), chunk_heads(7, 16), chunk_heads(16, 1)] == [7, 7, 8, 8]
+    assert [chunk_heads(5, 3), chunk_heads(1, 11), chunk_heads(1, 1), chunk_heads(3, 4)] == [5, 1, 1, 6]
