@@ -251,8 +251,13 @@ decode_merge_kernel(const float* __restrict__ ws, const int32_t* __restrict__ hi
   if (task >= batch * nv) return;
   const int b = task / nv, vh = task - b * nv;
   const int VG = nv / kv_heads, h = vh / VG, v = vh - h * VG;  // virtual head v of KV head h
-  const int c = v / cg, jj = v - c * cg;                       // its chunk and slot in the chunk
-  const int qh = h * (n_q / kv_heads) + v / q_len, qi = v % q_len;
+  int c = 0, jj = v, qh = vh, qi = 0;  // one query token: one chunk per KV head, v is the q-head's slot
+  if (q_len > 1 || cg != VG) {
+    c = v / cg;  // its chunk and slot in the chunk
+    jj = v - c * cg;
+    qh = h * (n_q / kv_heads) + v / q_len;
+    qi = v % q_len;
+  }
   const int pages = hist_tokens[b] / P;
   const int n_s = min((pages + pps - 1) / pps + residual_splits(P, q_len), max_splits);
   const int64_t item = static_cast<int64_t>(cg) * (D + 2);

@@ -87,31 +87,54 @@ __device__ __forceinline__ int64_t item_index(const DecodeParams& p, int b, int 
 }
 
 // Virtual heads c*cg .. c*cg+cg-1 of KV head h into q_s [kGQ][D] fp32,
-// zero-padded to kGQ heads.
-template <typename QT>
-__device__ __forceinline__ void load_query_group(const DecodeParams& p, int b, int h, int c, float* q_s) {
-  const int D = p.L.head_dim;
-  const QT* q = static_cast<const QT*>(p.q);
-  for (int i = threadIdx.x; i < kGQ * D; i += kDecThreads) {
-    const int j = i / D, d = i - j * D;
-    q_s[i] = j < p.cg ? Scalar<QT>::load(q + vhead_q_offset(p, b, h, c * p.cg + j) + d) : 0.0f;
+// zero-padded to kGQ heads; thread d < D loads channel d of every head (all
+// loads issued before the stores).  The virtual heads are stepped in order
+// (q-head jh, query token ii), so no division is needed per head.
+template <typename LOAD>
+__device__ __forceinline__ void gather_query_group(const DecodeParams& p, int b, int h, int c, float* q_s,
+                                                   LOAD load) {
+  const int D = p.L.head_dim, d = threadIdx.x, v0 = c * p.cg;
+  int jh = v0 / p.q_len, ii = v0 - jh * p.q_len;
+  const int64_t base = b * p.q_seq_stride + static_cast<int64_t>(h) * p.gq * p.q_head_stride + d;
+  float vals[kGQ];
+#pragma unroll
+  for (int j = 0; j < kGQ; ++j) {
+    vals[j] = (j < p.cg && d < D) ? load(base + jh * p.q_head_stride + ii * p.q_tok_stride) : 0.0f;
+    if (++ii == p.q_len) {
+      ii = 0;
+      ++jh;
+    }
+  }
+  if (d < D) {
+#pragma unroll
+    for (int j = 0; j < kGQ; ++j) q_s[j * D + d] = vals[j];
   }
 }
 
-__device__ __forceinline__ float load_dtype(const void* base, int64_t idx, int dtype) {
-  switch (dtype) {
-    case LF_F32: return static_cast<const float*>(base)[idx];
-    case LF_F16: return __half2float(static_cast<const __half*>(base)[idx]);
-    default: return __bfloat162float(static_cast<const __nv_bfloat16*>(base)[idx]);
-  }
+template <typename QT>
+__device__ __forceinline__ void load_query_group(const DecodeParams& p, int b, int h, int c, float* q_s) {
+  const QT* q = static_cast<const QT*>(p.q);
+  gather_query_group(p, b, h, c, q_s, [&](int64_t o) { return Scalar<QT>::load(q + o); });
 }
+
 // Query group as load_query_group, dtype chosen at run time (p.q_dtype).
-__device__ __forceinline__ void load_query_group_rt(const DecodeParams& p, int b, int h, int c, float* q_s,
-                                                    int nthreads) {
-  const int D = p.L.head_dim;
-  for (int i = threadIdx.x; i < kGQ * D; i += nthreads) {
-    const int j = i / D, d = i - j * D;
-    q_s[i] = j < p.cg ? load_dtype(p.q, vhead_q_offset(p, b, h, c * p.cg + j) + d, p.q_dtype) : 0.0f;
+// Called by the first 128 threads (head_dim <= 128).
+__device__ __forceinline__ void load_query_group_rt(const DecodeParams& p, int b, int h, int c, float* q_s) {
+  switch (p.q_dtype) {
+    case LF_F32: {
+      const float* q = static_cast<const float*>(p.q);
+      gather_query_group(p, b, h, c, q_s, [&](int64_t o) { return q[o]; });
+      break;
+    }
+    case LF_F16: {
+      const __half* q = static_cast<const __half*>(p.q);
+      gather_query_group(p, b, h, c, q_s, [&](int64_t o) { return __half2float(q[o]); });
+      break;
+    }
+    default: {
+      const __nv_bfloat16* q = static_cast<const __nv_bfloat16*>(p.q);
+      gather_query_group(p, b, h, c, q_s, [&](int64_t o) { return __bfloat162float(q[o]); });
+    }
   }
 }
 
@@ -284,10 +307,19 @@ static __device__ __forceinline__ void residual_chunk(const DecodeParams& p, int
   // r (row tl + r) is visible to virtual heads of query token i >= r.
   if (warp == 0) {
     const int rnew = t0 + lane - tl;  // new-token index of this row, < 0 for a tail row
+    int vt[kGQ];                      // query token of each virtual head of the chunk
+    {
+      int ii = (vc * GQ) % p.q_len;
+#pragma unroll
+      for (int j = 0; j < kGQ; ++j) {
+        vt[j] = ii;
+        if (++ii == p.q_len) ii = 0;
+      }
+    }
 #pragma unroll
     for (int j = 0; j < kGQ; ++j) {
       float sj = -INFINITY;
-      if (lane < ntok && j < GQ && rnew <= (vc * GQ + j) % p.q_len) {
+      if (lane < ntok && j < GQ && rnew <= vt[j]) {
         sj = (part[(0 * kResChunk + lane) * kGQ + j] + part[(1 * kResChunk + lane) * kGQ + j]) +
              (part[(2 * kResChunk + lane) * kGQ + j] + part[(3 * kResChunk + lane) * kGQ + j]);
         sj *= p.scaling;

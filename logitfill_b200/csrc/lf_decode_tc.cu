@@ -255,12 +255,12 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
   extern __shared__ __align__(1024) unsigned char smem[];
   const lf_layout& L = p.L;
   const TcSmem S = tc_smem(L);
-  // Grid: x = (sequence, KV head, virtual-head chunk), y = split.  Blocks
-  // launch in x-fastest order, so every pair's first splits start together and
-  // the short residual splits (the last y) take the SMs the page splits leave.
-  const int s = blockIdx.y, tid = threadIdx.x;
-  const int pair = blockIdx.x / p.n_chunks, vc = blockIdx.x - pair * p.n_chunks;
-  const int h = pair % p.L.kv_heads, b = pair / p.L.kv_heads;
+  // Grid: x = (sequence, KV head) pair, y = split, z = virtual-head chunk.
+  // Blocks launch in x-fastest order, so every pair's first splits start
+  // together and the short residual splits (the last y) take the SMs the page
+  // splits leave.
+  const int s = blockIdx.y, vc = blockIdx.z, tid = threadIdx.x;
+  const int h = blockIdx.x % p.L.kv_heads, b = blockIdx.x / p.L.kv_heads;
   const int lane = tid & 31, warp = tid >> 5;
   const int H = L.kv_heads, R = L.row_words, M = L.meta_halves;
   const int pages = p.hist_tokens[b] / kP;
@@ -277,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       m[j] = -INFINITY;
       o[j] = lt[j] = lvt[j] = 0.f;
     }
-    load_query_group_rt(p, b, h, vc, q_s, kDecThreads);
+    load_query_group_rt(p, b, h, vc, q_s);
     residual_chunk(p, b, h, vc, s - n_page_splits, q_s, smem + S.stage0, m, o, lt);
     write_partial_group<kGQ>(p, item_index(p, b, h, vc, s), tid, o, m, lt, lvt, red_w, 1);
     return;
@@ -343,21 +343,30 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     const int ch16 = tid < n16 ? p.slot_chan[(3 * H + h) * kD + tid / kGQ] : -1;
     float qc[kGQ];
     {
-      int64_t off[kGQ];
+      // Virtual heads vc*GQ + j: q-head jh, query token ii, stepped in order.
+      const int v0 = vc * GQ;
+      const int jh0 = v0 / p.q_len, ii0 = v0 - jh0 * p.q_len;
+      const int64_t qb = b * p.q_seq_stride + static_cast<int64_t>(h) * p.gq * p.q_head_stride + tid;
+      auto gather = [&](auto load) {
+        int jh = jh0, ii = ii0;
 #pragma unroll
-      for (int j = 0; j < kGQ; ++j) off[j] = j < GQ ? vhead_q_offset(p, b, h, vc * GQ + j) + tid : 0;
+        for (int j = 0; j < kGQ; ++j) {
+          qc[j] = j < GQ ? load(qb + jh * p.q_head_stride + ii * p.q_tok_stride) : 0.f;
+          if (++ii == p.q_len) {
+            ii = 0;
+            ++jh;
+          }
+        }
+      };
       if (p.q_dtype == LF_F32) {
         const float* qp = static_cast<const float*>(p.q);
-#pragma unroll
-        for (int j = 0; j < kGQ; ++j) qc[j] = j < GQ ? qp[off[j]] : 0.f;
+        gather([&](int64_t o) { return qp[o]; });
       } else if (p.q_dtype == LF_F16) {
         const __half* qp = static_cast<const __half*>(p.q);
-#pragma unroll
-        for (int j = 0; j < kGQ; ++j) qc[j] = j < GQ ? __half2float(qp[off[j]]) : 0.f;
+        gather([&](int64_t o) { return __half2float(qp[o]); });
       } else {
         const __nv_bfloat16* qp = static_cast<const __nv_bfloat16*>(p.q);
-#pragma unroll
-        for (int j = 0; j < kGQ; ++j) qc[j] = j < GQ ? __bfloat162float(qp[off[j]]) : 0.f;
+        gather([&](int64_t o) { return __bfloat162float(qp[o]); });
       }
     }
     float qmax = 0.f;
@@ -703,7 +712,10 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     for (int j = 0; j < GQ; ++j) mg[j] = __shfl_sync(0xffffffffu, m_l, j) * kLn2;  // natural-log units
     // PV row t holds head-dim channel d(t): t = 16w + 4k + i  <->  d = 16w + k + 4i.
     const int d = (tid & ~15) + ((tid & 15) >> 2) + 4 * (tid & 3);
-    write_partial_group<GQ>(p, item_index(p, b, h, vc, s), d, og, mg, lt, lvt, red_w, 1);
+    // (sequence, KV head, chunk) re-read from the block index: nothing of it
+    // stays live through the page loop.
+    const int64_t item = (static_cast<int64_t>(blockIdx.x) * p.n_chunks + blockIdx.z) * p.max_splits + s;
+    write_partial_group<GQ>(p, item, d, og, mg, lt, lvt, red_w, 1);
   }
   tc_fence_before();
   __syncthreads();  // compute warps finished (their partial is written); copies and MMAs drained
@@ -793,7 +805,7 @@ int launch_partial_tc(const DecodeParams& p, int resid_dtype, int q_dtype, cudaS
       return LF_ERR_UNSUPPORTED;
     }
   }
-  dim3 grid(q.L.kv_heads * q.batch * q.n_chunks, q.max_splits);
+  dim3 grid(q.L.kv_heads * q.batch, q.max_splits, q.n_chunks);
   void* args[] = {&q};
   cudaError_t e = cudaLaunchKernel(kern, grid, dim3(tc::kThreads), args, S.total, stream);
   if (e != cudaSuccess) {

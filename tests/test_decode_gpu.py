@@ -158,9 +158,12 @@ def test_long_context_split_merge_property():
 def test_errors_are_raised_not_swallowed():
     case = cases.config0_like(128, 1)
     mgr = manager_for(case)
-    q = torch.zeros(1, 28, 2, 128, device="cuda")  # q_len 2: no kernel, no silent fallback
+    q = torch.zeros(2, 28, 1, 128, device="cuda")  # two sequences through a one-sequence manager
     with pytest.raises(NotImplementedError):
         packed_attention(mgr, 0, q, q[:, :4], q[:, :4], 0.1)
+    q = torch.zeros(1, 28, 2, 128, device="cuda")
+    with pytest.raises(ValueError):                 # new Key/Value with the wrong token count
+        packed_attention(mgr, 0, q, q[:, :4, :1], q[:, :4, :1], 0.1)
     with pytest.raises(NotImplementedError):
         PackedKVCache([None], 1, 28, 4, 128, bit_v=4, device="cuda")
 
