@@ -225,7 +225,7 @@ decode_partial_simt(DecodeParams p) {
       }
     }
   } else {
-    residual_chunk(p, b, h, c, s - n_page_splits, q_s, region, m, acc, lt);
+    residual_chunk(p, b, h, c, s - n_page_splits, q_s, false, region, m, acc, lt);
   }
 
   write_partial(p, item_index(p, b, h, c, s), tid, acc, m, lt, lvt, red);

@@ -232,9 +232,14 @@ __device__ __forceinline__ void load_vec_to_float_rt(const void* src, int dtype,
   }
 }
 
+// One residual chunk: attention of the query group (q_s [kGQ][D]) over up to
+// kResChunk tokens in fp32, first 128 threads, barrier 1.  Thread d < D
+// accumulates channel d in acc; the chunk's probability sum is added to lt of
+// thread 0 only.  When load_q is set the query group is fetched here, after
+// the row loads are issued, so the two global-memory latencies overlap.
 static __device__ __forceinline__ void residual_chunk(const DecodeParams& p, int b, int h, int vc, int chunk,
-                                                      const float* q_s, unsigned char* region, float (&m)[kGQ],
-                                                      float (&acc)[kGQ], float (&lt)[kGQ]) {
+                                                      float* q_s, bool load_q, unsigned char* region,
+                                                      float (&m)[kGQ], float (&acc)[kGQ], float (&lt)[kGQ]) {
   const int RS_ = p.resid_dtype == LF_F32 ? 4 : 2;  // element size
   const int D = p.L.head_dim, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, GQ = p.cg;
   const ResidSmem RS = resid_smem(D);
@@ -247,7 +252,10 @@ static __device__ __forceinline__ void residual_chunk(const DecodeParams& p, int
   const int total = tl + (p.k_new != nullptr ? p.q_len : 0);
   const int t0 = chunk * kResChunk;
   const int ntok = min(kResChunk, total - t0);
-  if (ntok <= 0) return;
+  if (ntok <= 0) {
+    if (load_q) load_query_group_rt(p, b, h, vc, q_s);
+    return;
+  }
   const char* tk = static_cast<const char*>(p.tail_k) + (b * p.tail_seq_stride + h * p.tail_head_stride) * RS_;
   const char* tv = static_cast<const char*>(p.tail_v) + (b * p.tail_seq_stride + h * p.tail_head_stride) * RS_;
   const char* nk = p.k_new != nullptr
@@ -276,6 +284,7 @@ static __device__ __forceinline__ void residual_chunk(const DecodeParams& p, int
       for (int e = 0; e < 8; ++e) kv[r][e] = vv[r][e] = 0.f;
     }
   }
+  if (load_q) load_query_group_rt(p, b, h, vc, q_s);
 #pragma unroll
   for (int r = 0; r < kMaxVec; ++r) {
     const int i = tid + r * kDecThreads;
@@ -287,39 +296,39 @@ static __device__ __forceinline__ void residual_chunk(const DecodeParams& p, int
     *reinterpret_cast<float4*>(v_s + t * D + c * 8 + 4) = make_float4(vv[r][4], vv[r][5], vv[r][6], vv[r][7]);
   }
   named_sync(1, kDecThreads);
-  // 2. Partial scores: lane = token, warp = quarter of the head dim.
+  // 2. Partial scores: lane = token, warp = quarter of the head dim; four
+  // channels per step, the query read as float4 (broadcast).
   {
     const int dq = D / 4, d0 = warp * dq;
     float ps[kGQ];
 #pragma unroll
     for (int j = 0; j < kGQ; ++j) ps[j] = 0.f;
-    for (int d = d0; d < d0 + dq; ++d) {
-      const float kd = k_s[lane * (D + 1) + d];
+    const float* kr = k_s + lane * (D + 1);
+#pragma unroll 2
+    for (int d = d0; d < d0 + dq; d += 4) {
+      const float k0 = kr[d], k1 = kr[d + 1], k2 = kr[d + 2], k3 = kr[d + 3];
 #pragma unroll
-      for (int j = 0; j < kGQ; ++j) ps[j] = fmaf(q_s[j * D + d], kd, ps[j]);
+      for (int j = 0; j < kGQ; ++j) {
+        const float4 qv = *reinterpret_cast<const float4*>(q_s + j * D + d);
+        ps[j] = fmaf(qv.x, k0, fmaf(qv.y, k1, fmaf(qv.z, k2, fmaf(qv.w, k3, ps[j]))));
+      }
     }
     float* dst = part + (warp * kResChunk + lane) * kGQ;
     *reinterpret_cast<float4*>(dst) = make_float4(ps[0], ps[1], ps[2], ps[3]);
     *reinterpret_cast<float4*>(dst + 4) = make_float4(ps[4], ps[5], ps[6], ps[7]);
   }
   named_sync(1, kDecThreads);
-  // 3. Softmax statistics of the chunk in warp 0 (lane = token).  New token
-  // r (row tl + r) is visible to virtual heads of query token i >= r.
-  if (warp == 0) {
+  // 3. Softmax statistics of the chunk (lane = token): warp w takes heads
+  // 2w and 2w + 1.  New token r (row tl + r) is visible to virtual heads of
+  // query token i >= r.
+  {
     const int rnew = t0 + lane - tl;  // new-token index of this row, < 0 for a tail row
-    int vt[kGQ];                      // query token of each virtual head of the chunk
-    {
-      int ii = (vc * GQ) % p.q_len;
 #pragma unroll
-      for (int j = 0; j < kGQ; ++j) {
-        vt[j] = ii;
-        if (++ii == p.q_len) ii = 0;
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < kGQ; ++j) {
+    for (int jj = 0; jj < 2; ++jj) {
+      const int j = 2 * warp + jj;
+      const int vt = (vc * GQ + j) % p.q_len;  // query token of virtual head j
       float sj = -INFINITY;
-      if (lane < ntok && j < GQ && rnew <= vt[j]) {
+      if (lane < ntok && j < GQ && rnew <= vt) {
         sj = (part[(0 * kResChunk + lane) * kGQ + j] + part[(1 * kResChunk + lane) * kGQ + j]) +
              (part[(2 * kResChunk + lane) * kGQ + j] + part[(3 * kResChunk + lane) * kGQ + j]);
         sj *= p.scaling;
@@ -327,7 +336,11 @@ static __device__ __forceinline__ void residual_chunk(const DecodeParams& p, int
       float mx = sj;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float mnew = fmaxf(m[j], mx);
+      float mj = m[0];  // running max of head j (the same in every thread); selected without dynamic indexing
+#pragma unroll
+      for (int t = 1; t < kGQ; ++t)
+        if (t == j) mj = m[t];
+      const float mnew = fmaxf(mj, mx);
       const float pj = (sj == -INFINITY) ? 0.f : expf(sj - mnew);
       p_s[lane * kGQ + j] = pj;
       float sum = pj;
@@ -335,7 +348,7 @@ static __device__ __forceinline__ void residual_chunk(const DecodeParams& p, int
       for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
       if (lane == 0) {
         stat[j] = mnew;
-        stat[kGQ + j] = (m[j] == -INFINITY || mnew == -INFINITY) ? 0.f : expf(m[j] - mnew);
+        stat[kGQ + j] = (mj == -INFINITY || mnew == -INFINITY) ? 0.f : expf(mj - mnew);
         stat[2 * kGQ + j] = sum;
       }
     }
@@ -351,6 +364,7 @@ static __device__ __forceinline__ void residual_chunk(const DecodeParams& p, int
     acc[j] *= alpha;
   }
   if (tid < D) {
+#pragma unroll 4
     for (int t = 0; t < ntok; ++t) {
       const float v = v_s[t * D + tid];
       const float4 a = *reinterpret_cast<const float4*>(p_s + t * kGQ);
@@ -363,6 +377,29 @@ static __device__ __forceinline__ void residual_chunk(const DecodeParams& p, int
       acc[5] = fmaf(c.y, v, acc[5]);
       acc[6] = fmaf(c.z, v, acc[6]);
       acc[7] = fmaf(c.w, v, acc[7]);
+    }
+  }
+}
+
+// Partial of a residual item, whose statistics need no reduction: m is the
+// same in every thread, the probability sum lives in thread 0 and there is
+// no Value-min term.  Thread d < D writes channel d.
+__device__ __forceinline__ void write_partial_resid(const DecodeParams& p, int64_t index, const float (&acc)[kGQ],
+                                                    const float (&m)[kGQ], const float (&lt)[kGQ]) {
+  const int D = p.L.head_dim, GQ = p.cg, d = threadIdx.x;
+  float* item = p.ws + index * (GQ * (D + 2));
+  if (d < D) {
+#pragma unroll
+    for (int j = 0; j < kGQ; ++j)
+      if (j < GQ) item[j * D + d] = acc[j];
+  }
+  if (d == 0) {
+#pragma unroll
+    for (int j = 0; j < kGQ; ++j) {
+      if (j < GQ) {
+        item[GQ * D + j] = m[j];
+        item[GQ * D + GQ + j] = lt[j];
+      }
     }
   }
 }

@@ -271,15 +271,14 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
   float* red_w = reinterpret_cast<float*>(smem + S.redw);
   if (s >= n_page_splits) {  // residual splits: tail rows + new token, fp32 (compute warps)
     if (warp >= 4) return;
-    float m[kGQ], o[kGQ], lt[kGQ], lvt[kGQ];
+    float m[kGQ], o[kGQ], lt[kGQ];
 #pragma unroll
     for (int j = 0; j < kGQ; ++j) {
       m[j] = -INFINITY;
-      o[j] = lt[j] = lvt[j] = 0.f;
+      o[j] = lt[j] = 0.f;
     }
-    load_query_group_rt(p, b, h, vc, q_s);
-    residual_chunk(p, b, h, vc, s - n_page_splits, q_s, smem + S.stage0, m, o, lt);
-    write_partial_group<kGQ>(p, item_index(p, b, h, vc, s), tid, o, m, lt, lvt, red_w, 1);
+    residual_chunk(p, b, h, vc, s - n_page_splits, q_s, true, smem + S.stage0, m, o, lt);
+    write_partial_resid(p, item_index(p, b, h, vc, s), o, m, lt);
     return;
   }
 
