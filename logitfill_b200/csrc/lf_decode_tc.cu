@@ -424,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
         float bias[kGQ];
 #pragma unroll
         for (int j = 0; j < kGQ; ++j) bias[j] = 0.f;
-#pragma unroll
+#pragma unroll 1
         for (int k = 0; k < 4; ++k) {
           if (k >= n_hi) break;
           const int r = 32 * k + lane;
@@ -532,7 +532,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       uint32_t ns = 0u;
       {
         const uint32_t* src = rowp + co0;
-#pragma unroll 4
+#pragma unroll 2
         for (int w = 0; w < wd0; ++w) {
           const uint32_t x = src[w];
           tmem_st_x4(col + 4 * w, x & kM2, x & (kM2 << 2), x & (kM2 << 4), x & (kM2 << 6));
@@ -542,7 +542,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       }
       {
         const uint32_t* src = rowp + co1;
-#pragma unroll 4
+#pragma unroll 2
         for (int w = 0; w < wd1; ++w) {
           const uint32_t x = src[w];
           tmem_st_x2(col + 2 * w, x & kM4, x & (kM4 << 4));
@@ -552,7 +552,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       }
       {
         const uint32_t* src = rowp + co2;
-#pragma unroll 4
+#pragma unroll 2
         for (int w = 0; w < wd2; ++w) {
           const uint32_t x = src[w];
           tmem_st_x1(col + w, x);
@@ -606,7 +606,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       float s16[GQ];
 #pragma unroll
       for (int j = 0; j < GQ; ++j) s16[j] = 0.f;
-#pragma unroll 4
+#pragma unroll 2
       for (int c = 0; c < w3; ++c) {
         const float kv = half_bits_to_float(row16[c]);
         const float4 qa = *reinterpret_cast<const float4*>(q16_s + c * kGQ);
