@@ -256,6 +256,51 @@ def run_reference(args, cfg) -> None:
     print(json.dumps(line), flush=True)
 
 
+def time_k1(cache, k, v, T: int, dev) -> dict:
+    """K1 (page quantize + pack) on layer 0's prefill: every full page of every
+    sequence re-packed into the slot it already occupies (the output bytes do
+    not change).  Algorithmic bytes: the pages' Key and Value in their dtype
+    plus the packed rows and meta rows written."""
+    import numpy as np
+    import torch
+
+    import ctypes
+
+    from logitfill_b200 import _lib
+    from logitfill_b200.packed.layout import pack_pages
+
+    layer, P = cache.layers[0], cache.page_size
+    pages = T // P
+    jobs = [(b, p * P, b, p) for b in range(cache.batch) for p in range(pages)]
+    lay = layer.layout
+    moved = len(jobs) * cache.n_kv * (2 * P * cache.head_dim * k.element_size()
+                                      + P * lay.row_words * 4 + lay.meta_halves * 2)
+    pack_pages(lay, layer.rows, layer.kmeta, k, v, jobs)  # validates the jobs once
+    jobs_dev = torch.tensor(jobs, dtype=torch.int32, device=dev)
+    so = _lib.lib()
+
+    def launch():  # the kernel alone: jobs already on the device
+        _lib.check(so.lf_pack_pages(
+            ctypes.byref(lay.c), _lib.ptr(k), _lib.ptr(v), _lib.dtype_code(k.dtype), k.stride(0), k.stride(1),
+            k.stride(2), _lib.ptr(jobs_dev), len(jobs), cache.batch, _lib.ptr(lay.chan_code), _lib.ptr(layer.rows),
+            _lib.ptr(layer.kmeta), _lib.ptr(cache.status), _lib.stream_handle(dev)), "lf_pack_pages")
+
+    launch()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(5):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        launch()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    cache.check_status()
+    ms = float(np.median(times))
+    return {"kernel": "lf_pack_pages (K1)", "bound": "hbm", "unit": "GB/s", "pages_per_launch": len(jobs) * cache.n_kv,
+            "bytes_per_launch": moved, "avg_launch_ms": ms, "achieved": moved / (ms * 1e-3) / 1e9}
+
+
 def workload_config(cfg: dict, n_gpus: int) -> dict:
     return {
         "workload": f"{cfg['name']}: {cfg['layers']} layers, {cfg['n_q']} q / {cfg['n_kv']} kv heads, "
@@ -302,8 +347,12 @@ def run_b200(args, cfg) -> None:
     for layer in range(L):
         k, v = synthetic_kv(B, H, T + 128, D, seed=cfg["seed"] * 1000 + rank, layer=layer, device=dev)
         cache.prefill(layer, k, v, lengths)
+        if layer == 0:
+            k1_src = (k, v)  # kept for the K1 timing below
         del k, v
     torch.cuda.synchronize()
+    k1 = time_k1(cache, *k1_src, T, dev)
+    del k1_src
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
     q = torch.randn(L, B, NQ, D, generator=gen, device=dev).to(torch.bfloat16)
     kn = torch.randn(L, B, H, D, generator=gen, device=dev).to(torch.bfloat16)
@@ -405,6 +454,7 @@ def run_b200(args, cfg) -> None:
                          "traffic": ncu_traffic(args.config) if args.target_bit is None else None,
                          "traffic_source": f"ncu --set full, profiles/k2_decode_config{args.config}_ncu.md",
                          "bytes_per_launch": k2_bytes_avg, "avg_launch_ms": k2_avg_ms},
+            "k1": dict(k1, peak=peak, frac=k1["achieved"] / peak),
             "e2e": {"value": world * B / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "cpu_baseline": cpu,

@@ -57,6 +57,27 @@ __device__ __forceinline__ uint32_t asym_code(float x, float lo, float scale, in
   return static_cast<uint32_t>(c);
 }
 
+// asym_code with the division done by Markstein's method (P. Markstein,
+// "Computation of elementary functions on the IBM RISC System/6000
+// processor", IBM J. Res. Develop. 34(1), 1990): with rcp = RN(1/scale) and
+// q0 = RN(d * rcp) within one ulp of d / scale, the residual d - q0 * scale is
+// exact in an FMA and RN(q0 + residual * rcp) is the correctly rounded
+// quotient, i.e. the same value as the IEEE division, for the normal-range
+// operands here (scale in [1e-5, 1e5]; a quotient too small to be normal
+// rounds to code 0 either way).  Three floating-point operations instead of a
+// division per element; tests/test_pack_gpu.py checks it against the IEEE
+// division bit for bit.
+__device__ __forceinline__ uint32_t asym_code_rcp(float x, float lo, float scale, float rcp, int bits) {
+  const float d = __fsub_rn(x, lo);
+  const float q0 = __fmul_rn(d, rcp);
+  const float r = __fmaf_rn(-q0, scale, d);
+  float c = rintf(__fmaf_rn(r, rcp, q0));  // round half to even
+  const float qmax = static_cast<float>((1 << bits) - 1);
+  c = fmaxf(c, 0.0f);
+  c = fminf(c, qmax);
+  return static_cast<uint32_t>(c);
+}
+
 template <typename F>
 __device__ __forceinline__ void dispatch_noop(F) {}
 

@@ -1,13 +1,16 @@
 // K1: page quantize + pack, and the history dequantizer.
 //
 // One CTA per (job, KV head).  The page's Key and Value tiles are staged in
-// shared memory as fp32 (exact for bf16/fp16/fp32 inputs), the per-channel
+// shared memory in their own dtype (16-byte streaming loads), the per-channel
 // Key statistics (one min/max per k_group tokens, layout.py:86-99) and the
-// per-token Value statistics (layout.py:122-129) are computed once, and every
-// output word of the history rows is then assembled by one thread and written
-// with coalesced stores.  Arithmetic is the reference's, bit for bit:
+// per-token Value statistics (layout.py:122-129) are computed once, every
+// element is replaced in place by its code (uniform work over the CTA), and
+// every output word of the history rows is then assembled from the codes by
+// one thread and written with coalesced stores.  Arithmetic is the reference's, bit for bit:
 // fp32 max/min, IEEE subtract and divide, clamp to [1e-5, 1e5], round half to
 // even, fp16 round-to-nearest-even of the stored scale/min (layout.py:12-18,98-99).
+
+#include <type_traits>
 
 #include "lf_common.cuh"
 
@@ -17,25 +20,33 @@ constexpr int kPackThreads = 256;
 
 struct PackSmem {
   // Byte offsets into dynamic shared memory.
-  int xk, xv, ksc, klo, vsc, vlo, slotmap, meta, total;
+  int xk, xv, ksc, klo, krc, vsc, vlo, vrc, slotmap, wdesc, meta, total;
 };
 
-__host__ __device__ inline PackSmem pack_smem(const lf_layout& L) {
+// The page's Key and Value tiles are staged in their own dtype (esz bytes per
+// element): 64 KB for a bf16 128 x 128 page pair, so three CTAs fit on an SM.
+__host__ __device__ inline PackSmem pack_smem(const lf_layout& L, int esz) {
   const int P = L.page_size, D = L.head_dim;
   const int G = P / L.k_group, NV = D / L.v_group;
   PackSmem s;
   int off = 0;
-  s.xk = off; off += P * D * 4;
-  s.xv = off; off += P * D * 4;
+  s.xk = off; off += (P * D * esz + 15) / 16 * 16;
+  s.xv = off; off += (P * D * esz + 15) / 16 * 16;
   s.ksc = off; off += G * D * 4;
   s.klo = off; off += G * D * 4;
+  s.krc = off; off += G * D * 4;
   s.vsc = off; off += P * NV * 4;
   s.vlo = off; off += P * NV * 4;
+  s.vrc = off; off += P * NV * 4;
   s.slotmap = off; off += 4 * D * 4;
+  s.wdesc = off; off += L.row_words * 4;
   s.meta = off; off += G * L.meta_halves * 2;
   s.total = (off + 15) / 16 * 16;
   return s;
 }
+
+// Row-word descriptors: kind (0-2 Key tier, 3 Value codes, 4 fp16 halves) | index << 3.
+enum { kWordValue = 3, kWordHalf = 4 };
 
 template <typename T>
 __global__ void __launch_bounds__(kPackThreads)
@@ -44,14 +55,17 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
                   int dst_batch, const int32_t* __restrict__ chan_code, int32_t* __restrict__ rows,
                   uint16_t* __restrict__ kmeta, int32_t* status) {
   extern __shared__ __align__(16) unsigned char smem[];
-  const PackSmem S = pack_smem(L);
-  float* xk = reinterpret_cast<float*>(smem + S.xk);
-  float* xv = reinterpret_cast<float*>(smem + S.xv);
+  const PackSmem S = pack_smem(L, sizeof(T));
+  T* xk = reinterpret_cast<T*>(smem + S.xk);
+  T* xv = reinterpret_cast<T*>(smem + S.xv);
   float* ksc = reinterpret_cast<float*>(smem + S.ksc);
   float* klo = reinterpret_cast<float*>(smem + S.klo);
+  float* krc = reinterpret_cast<float*>(smem + S.krc);  // RN(1 / scale)
   float* vsc = reinterpret_cast<float*>(smem + S.vsc);
   float* vlo = reinterpret_cast<float*>(smem + S.vlo);
+  float* vrc = reinterpret_cast<float*>(smem + S.vrc);
   int* slotmap = reinterpret_cast<int*>(smem + S.slotmap);
+  int* wdesc = reinterpret_cast<int*>(smem + S.wdesc);
   uint16_t* meta = reinterpret_cast<uint16_t*>(smem + S.meta);
 
   const int job = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
@@ -66,13 +80,42 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
     return;
   }
 
-  // Stage the page (fp32, exact) and initialise the channel map and meta rows.
+  // 1. Stage the page in its dtype: 16-byte streaming loads (all of a
+  // thread's loads issued before its stores) when the rows are aligned.
   const T* ksrc = src_k + src_seq * s_seq + h * s_head + static_cast<int64_t>(tok0) * s_tok;
   const T* vsrc = src_v + src_seq * s_seq + h * s_head + static_cast<int64_t>(tok0) * s_tok;
-  for (int i = tid; i < P * D; i += kPackThreads) {
-    const int t = i / D, c = i - t * D;
-    xk[i] = Scalar<T>::load(ksrc + t * s_tok + c);
-    xv[i] = Scalar<T>::load(vsrc + t * s_tok + c);
+  constexpr int kVec = 16 / sizeof(T);
+  const bool vec = (reinterpret_cast<uintptr_t>(ksrc) % 16 == 0) && (reinterpret_cast<uintptr_t>(vsrc) % 16 == 0) &&
+                   (s_tok * static_cast<int64_t>(sizeof(T))) % 16 == 0 && D % kVec == 0;
+  if (vec) {
+    const int vpr = D / kVec, nvec = P * vpr;
+    constexpr int kBatch = 8;
+    for (int base = tid; base < nvec; base += kPackThreads * kBatch) {
+      uint4 a[kBatch], c[kBatch];
+#pragma unroll
+      for (int r = 0; r < kBatch; ++r) {
+        const int i = base + r * kPackThreads;
+        if (i < nvec) {
+          const int t = i / vpr, e = (i - t * vpr) * kVec;
+          a[r] = __ldcs(reinterpret_cast<const uint4*>(ksrc + t * s_tok + e));
+          c[r] = __ldcs(reinterpret_cast<const uint4*>(vsrc + t * s_tok + e));
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kBatch; ++r) {
+        const int i = base + r * kPackThreads;
+        if (i < nvec) {
+          reinterpret_cast<uint4*>(xk)[i] = a[r];
+          reinterpret_cast<uint4*>(xv)[i] = c[r];
+        }
+      }
+    }
+  } else {
+    for (int i = tid; i < P * D; i += kPackThreads) {
+      const int t = i / D, e = i - t * D;
+      xk[i] = ksrc[t * s_tok + e];
+      xv[i] = vsrc[t * s_tok + e];
+    }
   }
   for (int i = tid; i < 4 * D; i += kPackThreads) slotmap[i] = -1;
   for (int i = tid; i < G * M; i += kPackThreads) {
@@ -83,44 +126,70 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
       is_scale |= (e >= L.scale_off[b] && e < L.scale_off[b] + L.width[b]);
     meta[i] = is_scale ? 0x3C00 : 0;
   }
+  for (int w = tid; w < R; w += kPackThreads) {
+    int d;
+    if (w < L.vcode_off) {
+      int b = 0;
+      while (b < 2 && w >= L.code_off[b] + L.words[b]) ++b;
+      d = b | ((w - L.code_off[b]) << 3);
+    } else if (w < L.half_off) {
+      d = kWordValue | ((w - L.vcode_off) << 3);
+    } else {
+      d = kWordHalf | ((w - L.half_off) << 3);
+    }
+    wdesc[w] = d;
+  }
   __syncthreads();
   for (int c = tid; c < D; c += kPackThreads) {
     const int code = chan_code[h * D + c];
     const int tier = code >> 16, local = code & 0xFFFF;
     if (tier >= 0 && tier < 4 && local < L.width[tier]) slotmap[tier * D + local] = c;
   }
-  // Key statistics: one (max, min) per channel per k_group tokens.
-  for (int i = tid; i < G * D; i += kPackThreads) {
-    const int g = i / D, c = i - g * D;
-    const int code = chan_code[h * D + c];
-    const int tier = code >> 16, local = code & 0xFFFF;
-    if (tier < 0 || tier > 2) continue;
-    const int bits = 2 << tier;
-    float hi = -INFINITY, lo = INFINITY;
-    for (int t = g * L.k_group; t < (g + 1) * L.k_group; ++t) {
-      const float x = xk[t * D + c];
-      hi = fmaxf(hi, x);
-      lo = fminf(lo, x);
+  // 2. Statistics, one work item per thread: (max, min) of a Key channel over
+  // k_group tokens (layout.py:86-99), or of a token over v_group Value
+  // channels (layout.py:122-129).
+  for (int i = tid; i < G * D + P * NV; i += kPackThreads) {
+    if (i < G * D) {
+      const int g = i / D, c = i - g * D;
+      const int code = chan_code[h * D + c];
+      const int tier = code >> 16, local = code & 0xFFFF;
+      if (tier < 0 || tier > 2) continue;
+      float hi = -INFINITY, lo = INFINITY;
+      const T* col = xk + g * L.k_group * D + c;
+#pragma unroll 8
+      for (int t = 0; t < L.k_group; ++t) {
+        const float x = Scalar<T>::load(col + t * D);
+        hi = fmaxf(hi, x);
+        lo = fminf(lo, x);
+      }
+      const float sc = asym_scale(hi, lo, 2 << tier);
+      ksc[i] = sc;
+      klo[i] = lo;
+      krc[i] = __frcp_rn(sc);
+      if (local < L.width[tier]) {
+        meta[g * M + L.scale_off[tier] + local] = float_to_half_bits(sc);
+        meta[g * M + L.min_off[tier] + local] = float_to_half_bits(lo);
+      }
+    } else {
+      const int j = i - G * D, t = j / NV, g = j - t * NV;
+      float hi = -INFINITY, lo = INFINITY;
+      const T* row = xv + t * D + g * L.v_group;
+      // Neighbouring threads take neighbouring tokens (rows D elements apart,
+      // the same bank): each starts at its own column so a warp's reads spread
+      // over the banks.  Max and min do not depend on the order.
+      int cc = t % L.v_group;
+#pragma unroll 8
+      for (int c = 0; c < L.v_group; ++c) {
+        const float x = Scalar<T>::load(row + cc);
+        hi = fmaxf(hi, x);
+        lo = fminf(lo, x);
+        if (++cc == L.v_group) cc = 0;
+      }
+      const float sc = asym_scale(hi, lo, L.bit_v);
+      vsc[j] = sc;
+      vlo[j] = lo;
+      vrc[j] = __frcp_rn(sc);
     }
-    const float sc = asym_scale(hi, lo, bits);
-    ksc[i] = sc;
-    klo[i] = lo;
-    if (local < L.width[tier]) {
-      meta[g * M + L.scale_off[tier] + local] = float_to_half_bits(sc);
-      meta[g * M + L.min_off[tier] + local] = float_to_half_bits(lo);
-    }
-  }
-  // Value statistics: one (max, min) per token per v_group channels.
-  for (int i = tid; i < P * NV; i += kPackThreads) {
-    const int t = i / NV, g = i - t * NV;
-    float hi = -INFINITY, lo = INFINITY;
-    for (int c = g * L.v_group; c < (g + 1) * L.v_group; ++c) {
-      const float x = xv[t * D + c];
-      hi = fmaxf(hi, x);
-      lo = fminf(lo, x);
-    }
-    vsc[i] = asym_scale(hi, lo, L.bit_v);
-    vlo[i] = lo;
   }
   __syncthreads();
   // Largest stored Key scale of each group over the head's INT2/INT4/INT8
@@ -133,41 +202,76 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
     meta[g * M + L.kmax_off] = mx;
   }
 
-  // Assemble every word of the page's rows.
+  // 3. Codes, in place: every staged Key element of an INT2/INT4/INT8
+  // channel and every Value element is replaced by its code (same thread
+  // reads and writes an element; uniform work across the CTA).
+  using U = typename std::conditional<sizeof(T) == 4, uint32_t, uint16_t>::type;
+  U* ck = reinterpret_cast<U*>(xk);
+  U* cv = reinterpret_cast<U*>(xv);
+  // Channel-major split of the threads: thread (c, r0) takes channel c of
+  // tokens r0, r0 + rows_step, ... (no division per element).
+  const int rows_step = D <= kPackThreads ? kPackThreads / D : 1;
+  const int r0 = D <= kPackThreads ? tid / D : 0;
+  for (int c = D <= kPackThreads ? tid % D : tid; c < D && r0 < rows_step; c += kPackThreads) {
+    const int tier = __ldg(chan_code + h * D + c) >> 16;
+    const bool keyed = tier >= 0 && tier <= 2;
+    const int bits = keyed ? 2 << tier : 2;
+    const int vg = c / L.v_group;
+    int g = 0, g_end = L.k_group;  // Key group of token t, stepped as t advances
+    for (int t = r0; t < P; t += rows_step) {
+      while (t >= g_end) {
+        ++g;
+        g_end += L.k_group;
+      }
+      const int e = t * D + c;
+      if (keyed) {
+        const int gi = g * D + c;
+        ck[e] = static_cast<U>(asym_code_rcp(Scalar<T>::load(xk + e), klo[gi], ksc[gi], krc[gi], bits));
+      }
+      const int vi = t * NV + vg;
+      cv[e] = static_cast<U>(asym_code_rcp(Scalar<T>::load(xv + e), vlo[vi], vsc[vi], vrc[vi], L.bit_v));
+    }
+  }
+  __syncthreads();
+  // 4. Assemble every word of the page's rows from the codes (consecutive
+  // threads write consecutive words of a token row).
   int32_t* out_rows = rows + ((static_cast<int64_t>(dst_seq) * H + h) * L.row_cap +
                               static_cast<int64_t>(dst_page) * P) * R;
-  for (int i = tid; i < P * R; i += kPackThreads) {
-    const int t = i / R, w = i - t * R;
+  const int warp = tid >> 5, lane = tid & 31;
+  for (int t = warp; t < P; t += kPackThreads / 32)  // a warp per token row, lanes over its words
+  for (int w = lane; w < R; w += 32) {
+    const int i = t * R + w;
+    const int desc = wdesc[w], kind = desc & 7, wi = desc >> 3;
     uint32_t word = 0;
-    if (w < L.vcode_off) {
-      int b = 0;
-      while (b < 2 && w >= L.code_off[b] + L.words[b]) ++b;
-      const int bits = 2 << b, per = 32 / bits, wi = w - L.code_off[b];
-      const int g = t / L.k_group;
-      for (int k = 0; k < per; ++k) {
-        const int slot = wi * per + k;
-        if (slot >= L.width[b]) break;
-        const int c = slotmap[b * D + slot];
-        if (c < 0) continue;  // padding slot: code 0 (layout.py:95-97)
-        const uint32_t q = asym_code(xk[t * D + c], klo[g * D + c], ksc[g * D + c], bits);
-        word |= q << (k * bits);
+    if (kind < kWordValue) {
+      const int bits = 2 << kind, per = 32 / bits;
+      const U* cr = ck + t * D;
+      const int* sm = slotmap + kind * D + wi * per;
+      const int nslot = min(per, L.width[kind] - wi * per);
+      for (int k = 0; k < nslot; ++k) {
+        const int c = sm[k];
+        if (c >= 0) word |= static_cast<uint32_t>(cr[c]) << (k * bits);  // padding slot: code 0 (layout.py:95-97)
       }
-    } else if (w < L.half_off) {
-      const int per = 32 / L.bit_v, wi = w - L.vcode_off;
-      for (int k = 0; k < per; ++k) {
-        const int d = wi * per + k;
-        if (d >= D) break;
-        const int g = d / L.v_group;
-        const uint32_t q = asym_code(xv[t * D + d], vlo[t * NV + g], vsc[t * NV + g], L.bit_v);
-        word |= q << (k * L.bit_v);
+    } else if (kind == kWordValue) {
+      const int per = 32 / L.bit_v, d0 = wi * per, nd = min(per, D - d0);
+      const U* cr = cv + t * D + d0;
+      if (sizeof(U) == 2 && L.bit_v == 2 && nd == 16 && D % 8 == 0) {  // 16-byte aligned rows
+        // 16 two-bit codes held as u16: two 16-byte reads, two codes per u32.
+        const uint4 a = *reinterpret_cast<const uint4*>(cr);
+        const uint4 b = *reinterpret_cast<const uint4*>(cr + 8);
+        const uint32_t u[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) word |= ((u[k] & 3u) | ((u[k] >> 14) & 0xCu)) << (4 * k);
+      } else {
+        for (int k = 0; k < nd; ++k) word |= static_cast<uint32_t>(cr[k]) << (k * L.bit_v);
       }
     } else {
       for (int e = 0; e < 2; ++e) {
-        const int hx = 2 * (w - L.half_off) + e;
+        const int hx = 2 * wi + e;
         uint32_t hv = 0;
         if (hx < L.width[3]) {
           const int c = slotmap[3 * D + hx];
-          if (c >= 0) hv = float_to_half_bits(xk[t * D + c]);  // layout.py:110
+          if (c >= 0) hv = float_to_half_bits(Scalar<T>::load(xk + t * D + c));  // layout.py:110
         } else if (hx < L.width[3] + NV) {
           hv = float_to_half_bits(vsc[t * NV + (hx - L.width[3])]);
         } else if (hx < L.width[3] + 2 * NV) {
@@ -229,7 +333,7 @@ static int launch_pack(const lf_layout& L, const void* k, const void* v, int64_t
                        int64_t s_head, int64_t s_tok, const int32_t* jobs, int n_jobs,
                        int dst_batch, const int32_t* chan_code, int32_t* rows, uint16_t* kmeta,
                        int32_t* status, cudaStream_t stream) {
-  const PackSmem S = pack_smem(L);
+  const PackSmem S = pack_smem(L, sizeof(T));
   auto kern = pack_pages_kernel<T>;
   // The limit is raised once per size, outside any later stream capture of
   // the launch.
@@ -258,7 +362,7 @@ extern "C" int lf_pack_pages(const lf_layout* layout, const void* src_k, const v
   LF_CHECK_ARG(src_k && src_v && jobs && chan_code && rows, "lf_pack_pages: null pointer");
   LF_CHECK_ARG(layout->meta_halves == 0 || kmeta, "lf_pack_pages: null kmeta");
   const lf_layout& L = *layout;
-  LF_CHECK_SUPPORTED(lf::pack_smem(L).total <= 227 * 1024,
+  LF_CHECK_SUPPORTED(lf::pack_smem(L, src_dtype == LF_F32 ? 4 : 2).total <= 227 * 1024,
                      "lf_pack_pages: page %d x head_dim %d does not fit shared memory", L.page_size,
                      L.head_dim);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);

@@ -174,3 +174,40 @@ def test_decode_flush_sequence():
     assert torch.equal(step.layers[0].rows[:, :, :n], bulk.layers[0].rows[:, :, :n])
     g = n // 128
     assert torch.equal(step.layers[0].kmeta[:, :, :g].view(torch.int16), bulk.layers[0].kmeta[:, :, :g].view(torch.int16))
+
+
+def test_codes_at_rounding_boundaries():
+    """Quotients (x - min) / scale placed within a few ulps of every half
+    integer, where rounding the quotient differently would flip the code: K1
+    (which divides by Markstein's method, RN(1/scale) and one FMA correction)
+    must give the oracle's IEEE-division codes bit for bit, for the Key tiers
+    and the Value codes."""
+    rng = np.random.default_rng(11)
+    H, D, P = 2, 64, 64
+    levels = np.tile(np.repeat(np.array([0, 1, 2, 3]), D // 4), (H, 1))
+    k = np.zeros((H, P, D), np.float32)
+    v = np.zeros((H, P, D), np.float32)
+    ulp_steps = np.array([-3, -2, -1, 0, 1, 2, 3], np.float32)
+    for h in range(H):
+        for c in range(D):
+            bits = (2, 4, 8, 8)[levels[h, c]]
+            qmax = np.float32(2 ** bits - 1)
+            hi = np.float32(rng.uniform(0.5, 40.0))
+            scale = np.float32(hi / qmax)
+            k[h, 0, c], k[h, 1, c] = 0.0, hi
+            half = (rng.integers(0, int(qmax), P - 2) + np.float32(0.5)).astype(np.float32)
+            x = (half * scale).astype(np.float32)
+            step = ulp_steps[rng.integers(0, len(ulp_steps), P - 2)]
+            k[h, 2:, c] = x + step * np.spacing(x).astype(np.float32)
+        for t in range(P):
+            hi = np.float32(rng.uniform(0.5, 40.0))
+            scale = np.float32(hi / np.float32(3))
+            v[h, t, 0], v[h, t, 1] = 0.0, hi
+            half = (rng.integers(0, 3, D - 2) + np.float32(0.5)).astype(np.float32)
+            x = (half * scale).astype(np.float32)
+            step = ulp_steps[rng.integers(0, len(ulp_steps), D - 2)]
+            v[h, t, 2:] = x + step * np.spacing(x).astype(np.float32)
+    k, v = k.astype(np.float32), v.astype(np.float32)
+    case = {"dtype": "float32", "n_q": 2, "n_kv": H, "head_dim": D, "page": P, "k_group": P, "v_group": D,
+            "levels": levels, "commits": [(k, v)]}
+    _check_store(manager_for(case), case)
