@@ -89,6 +89,8 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
                    (s_tok * static_cast<int64_t>(sizeof(T))) % 16 == 0 && D % kVec == 0;
   if (vec) {
     const int vpr = D / kVec, nvec = P * vpr;
+    const bool pow2 = (vpr & (vpr - 1)) == 0;
+    const int vshift = 31 - __clz(vpr);
     constexpr int kBatch = 8;
     for (int base = tid; base < nvec; base += kPackThreads * kBatch) {
       uint4 a[kBatch], c[kBatch];
@@ -96,7 +98,7 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
       for (int r = 0; r < kBatch; ++r) {
         const int i = base + r * kPackThreads;
         if (i < nvec) {
-          const int t = i / vpr, e = (i - t * vpr) * kVec;
+          const int t = pow2 ? i >> vshift : i / vpr, e = (i - t * vpr) * kVec;
           a[r] = __ldcs(reinterpret_cast<const uint4*>(ksrc + t * s_tok + e));
           c[r] = __ldcs(reinterpret_cast<const uint4*>(vsrc + t * s_tok + e));
         }
@@ -218,16 +220,19 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
     const int bits = keyed ? 2 << tier : 2;
     const int vg = c / L.v_group;
     int g = 0, g_end = L.k_group;  // Key group of token t, stepped as t advances
+    float g_lo = klo[c], g_sc = ksc[c], g_rc = krc[c];  // that group's statistics, in registers
     for (int t = r0; t < P; t += rows_step) {
-      while (t >= g_end) {
-        ++g;
-        g_end += L.k_group;
+      if (t >= g_end) {
+        while (t >= g_end) {
+          ++g;
+          g_end += L.k_group;
+        }
+        g_lo = klo[g * D + c];
+        g_sc = ksc[g * D + c];
+        g_rc = krc[g * D + c];
       }
       const int e = t * D + c;
-      if (keyed) {
-        const int gi = g * D + c;
-        ck[e] = static_cast<U>(asym_code_rcp(Scalar<T>::load(xk + e), klo[gi], ksc[gi], krc[gi], bits));
-      }
+      if (keyed) ck[e] = static_cast<U>(asym_code_rcp(Scalar<T>::load(xk + e), g_lo, g_sc, g_rc, bits));
       const int vi = t * NV + vg;
       cv[e] = static_cast<U>(asym_code_rcp(Scalar<T>::load(xv + e), vlo[vi], vsc[vi], vrc[vi], L.bit_v));
     }

@@ -8,6 +8,7 @@ kernels do not implement, ``ValueError`` for malformed inputs).
 from __future__ import annotations
 
 import ctypes
+import math
 
 import torch
 
@@ -29,9 +30,13 @@ def pages_per_split(cache: PackedKVCache, layer_idx: int = 0, q_len: int = 1) ->
     is cut into ceil(pages / pps) items, plus the short residual items that
     launch after all of them.  An item costs about pps pages plus a fixed
     start (query staging, first copy) worth ~1.5 pages; the choice minimises
-    (waves of resident CTAs) x (pps + 1.5), i.e. it balances the page items
-    over the SMs instead of just making the grid large.  Memoised per layer
-    by (pages, q_len)."""
+    (waves of page items) x (pps + 1.5), i.e. it balances the page items
+    over the SMs instead of just making the grid large.  A wave is three page
+    items per SM at most (fewer if fewer fit): measured on B200, a fourth
+    co-resident page item slows the other three (2.8 -> 3.2 us per page) and
+    takes the slot the residual items would use, so about three per SM ran
+    fastest at both 8k and 32k histories.  A wave overfull by up to 2 % still
+    counts as one.  Memoised per layer by (pages, q_len)."""
     layer = cache.layers[layer_idx]
     P = cache.page_size
     pages = int(layer.hist_len.max()) // P if layer.hist_len.size else 0
@@ -50,7 +55,8 @@ def pages_per_split(cache: PackedKVCache, layer_idx: int = 0, q_len: int = 1) ->
         if occ <= 0:
             continue
         ctas = pairs * (-(-pages // pps))
-        waves = -(-ctas // (sms * occ))
+        per_wave = sms * min(occ, 3)
+        waves = max(1, math.ceil(ctas / per_wave - 0.02))
         cost = waves * (pps + 1.5)
         if best_cost is None or cost < best_cost - 1e-9:
             best, best_cost = pps, cost
