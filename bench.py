@@ -468,6 +468,77 @@ def run_b200(args, cfg) -> None:
         dist.destroy_process_group()
 
 
+def run_model_decode(args) -> None:
+    """Model-level decode loop (a DeepSeek-R1-Distill-Qwen-7B-shaped Qwen2 with
+    random weights, batch 1): prefill ``--context`` tokens through the adapter,
+    then time greedy decode steps eagerly (the reference's sampling loop,
+    benchmarks/generate.py:28-57) and replayed from a CUDA graph
+    (GraphDecoder).  Prints one JSON line; not the driver's bench line."""
+    import torch
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    from logitfill_b200.adapter import DeepSeekQwenKVAdapter
+    from logitfill_b200.graph_decode import GraphDecoder
+    from logitfill_b200.synthetic import synthetic_levels
+
+    torch.manual_seed(0)
+    cfg = Qwen2Config(vocab_size=152064, hidden_size=3584, intermediate_size=18944, num_hidden_layers=28,
+                      num_attention_heads=28, num_key_value_heads=4, max_position_embeddings=32768,
+                      rope_theta=10000.0, attention_dropout=0.0)
+    cfg._attn_implementation = "sdpa"
+    with torch.device("cuda"):
+        model = Qwen2ForCausalLM(cfg).to(torch.bfloat16).eval()
+    levels = list(synthetic_levels(28, 4, 128, 2.5, seed=1))
+    ctx, n = args.context, args.steps
+    prompt = torch.randint(0, cfg.vocab_size, (1, ctx), generator=torch.Generator().manual_seed(1)).cuda()
+    adapter = DeepSeekQwenKVAdapter(model).attach()
+    adapter.set_k_levels(levels)
+
+    def timed(fn, count):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(count):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / count
+
+    # Eager loop (the adapter on every layer, host-side commits).
+    cache = adapter.make_cache()
+    cache.reset()
+    state = {}
+    with torch.inference_mode():
+        out = model(input_ids=prompt, use_cache=True, past_key_values=cache)
+        state["tok"] = out.logits[:, -1].argmax(-1, keepdim=True)
+
+        def eager():
+            o = model(input_ids=state["tok"], use_cache=True, past_key_values=cache)
+            state["tok"] = o.logits[:, -1].argmax(-1, keepdim=True)
+
+        for _ in range(args.warmup):
+            eager()
+        eager_ms = timed(eager, n)
+    # Graph loop.
+    adapter.set_k_levels(levels)
+    g = GraphDecoder(model, adapter, max_tokens=ctx + args.warmup + n + 8)
+    with torch.inference_mode():
+        state["tok"] = g.prefill(prompt).argmax(-1, keepdim=True)
+
+        def graphed():
+            state["tok"] = g.step(state["tok"]).argmax(-1, keepdim=True)
+
+        for _ in range(args.warmup):
+            graphed()
+        graph_ms = timed(graphed, n)
+    g.release()
+    print(json.dumps({
+        "mode": "model_decode", "model": "Qwen2, DeepSeek-R1-Distill-Qwen-7B shape, random bf16 weights",
+        "batch": 1, "context": ctx, "steps": n, "warmup": args.warmup, "policy_target_bit": 2.5,
+        "eager_ms_per_token": eager_ms, "graph_ms_per_token": graph_ms, "speedup": eager_ms / graph_ms,
+        "data": "synthetic"}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -480,13 +551,18 @@ def main() -> None:
                     help="override the config's Key policy budget (config 2 sweep: 2.25, 2.5, 3.0, 4.0)")
     ap.add_argument("--pps", type=int, default=None,
                     help="pages per K2 work item (default: the occupancy-aware planner)")
+    ap.add_argument("--model-decode", action="store_true",
+                    help="time the model-level decode loop, eager vs CUDA graph (not the driver's bench line)")
+    ap.add_argument("--context", type=int, default=8192, help="prompt length for --model-decode")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     cfg = dict(CONFIGS[args.config])
     if args.target_bit is not None:
         cfg["target_bit"] = args.target_bit
-    if args.impl == "reference":
+    if args.model_decode:
+        run_model_decode(args)
+    elif args.impl == "reference":
         run_reference(args, cfg)
     else:
         run_b200(args, cfg)

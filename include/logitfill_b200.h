@@ -93,9 +93,10 @@ LF_API int lf_layout_init(lf_layout* out, int kv_heads, int head_dim, int page_s
  * Bit-exact with the reference: IEEE fp32 divide, round-half-even, fp16 RNE.
  * src_k/src_v: [seq][head][token][D] with the given element strides (channel
  * stride 1), dtype src_dtype.  jobs (device int32 [n_jobs][4]):
- * {src_seq, src_token0, dst_seq, dst_page}.  dst_batch bounds dst_seq; a job
- * outside [0, dst_batch) x [0, row_cap/page_size) is skipped and
- * LF_ERR_OUT_OF_RANGE is or-ed into *status (device int32, may be NULL).
+ * {src_seq, src_token0, dst_seq, dst_page}; a job with src_seq = -1 packs
+ * nothing.  dst_batch bounds dst_seq; any other job outside [0, dst_batch) x
+ * [0, row_cap/page_size) is skipped and LF_ERR_OUT_OF_RANGE is written to
+ * *status (device int32, may be NULL).
  */
 LF_API int lf_pack_pages(const lf_layout* layout, const void* src_k, const void* src_v, int src_dtype,
                   int64_t src_seq_stride, int64_t src_head_stride, int64_t src_tok_stride,
@@ -110,6 +111,25 @@ LF_API int lf_pack_pages(const lf_layout* layout, const void* src_k, const void*
 LF_API int lf_dequantize(const lf_layout* layout, const int32_t* rows, const uint16_t* kmeta,
                   const int32_t* chan_code, int seq, int64_t tokens, float* out_k, float* out_v,
                   lf_stream_t stream);
+
+/*
+ * One decode token per sequence committed on the device (no counterpart in
+ * the reference, whose commit runs on the host, cache.py:48-62): the token's
+ * Key/Value (k_new/v_new [batch][H][D], strides new_seq_stride /
+ * new_head_stride, dtype = the residual page's) is appended to the residual
+ * page at tail_len[b]; a page that becomes full is quantized and packed into
+ * history page hist_tokens[b] / page_size (K1, bit-exact) and the residual
+ * page starts empty; then tail_len / hist_tokens are advanced on the device.
+ * Every position comes from the device lengths, so the call can be captured in
+ * a CUDA graph and replayed step after step.  jobs: device int32 scratch
+ * [batch][4].  A page that would pass row_cap is not packed and
+ * LF_ERR_OUT_OF_RANGE is written to *status.
+ */
+LF_API int lf_commit_token(const lf_layout* layout, int32_t* rows, uint16_t* kmeta, const int32_t* chan_code,
+                           void* tail_k, void* tail_v, int64_t tail_seq_stride, int64_t tail_head_stride,
+                           int32_t* hist_tokens, int32_t* tail_len, int dtype, const void* k_new,
+                           const void* v_new, int64_t new_seq_stride, int64_t new_head_stride, int batch,
+                           int32_t* jobs, int32_t* status, lf_stream_t stream);
 
 /* Resident K2 CTAs per SM for this layer and split size (occupancy of the
  * kernel lf_decode_partial would launch, capped by tensor-memory columns);

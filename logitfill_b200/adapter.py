@@ -135,6 +135,11 @@ def _packed_branch(attn, adapter, layer_idx, query, key, value, attention_mask, 
                     f"cache reports {seen} tokens but the packed history holds {past}; "
                     "pass past_key_values=adapter.make_cache()")
         out = manager.attend(layer_idx, query, key, value, attn.scaling).transpose(1, 2)
+        if adapter.graph_step and query.shape[2] == 1:
+            # A step being captured for replay (GraphDecoder): the token is
+            # committed on the device and the host lengths advance per replay.
+            manager.commit_token(layer_idx, key, value, advance_host=False)
+            return out
     manager.commit(layer_idx, key, value)
     if cache is not None and hasattr(cache, "note_layer"):
         cache.note_layer(layer_idx, manager.seq_len)
@@ -177,6 +182,7 @@ class DeepSeekQwenKVAdapter:
             raise NotImplementedError("the packed backend stores Value at 2 bits (bit_v=2)")
         self.capture = False
         self.skip_quant = False
+        self.graph_step = False  # set by GraphDecoder around its captured decode step
         self.captured: dict = {"Q": {}, "K": {}, "V": {}}
         self.k_overrides: Optional[dict] = None
         self.policy: Optional[PrecisionPolicy] = None

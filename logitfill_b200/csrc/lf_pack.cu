@@ -17,6 +17,7 @@
 namespace lf {
 
 constexpr int kPackThreads = 256;
+constexpr int kPackSkip = -1;  // src_seq of a job that packs nothing
 
 struct PackSmem {
   // Byte offsets into dynamic shared memory.
@@ -73,6 +74,7 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
   const int G = P / L.k_group, NV = D / L.v_group, H = L.kv_heads;
   const int src_seq = jobs[4 * job + 0], tok0 = jobs[4 * job + 1];
   const int dst_seq = jobs[4 * job + 2], dst_page = jobs[4 * job + 3];
+  if (src_seq == kPackSkip) return;  // a job slot left empty by the device-side commit
   if (dst_seq < 0 || dst_seq >= dst_batch || dst_page < 0 ||
       static_cast<int64_t>(dst_page + 1) * P > L.row_cap ||
       static_cast<int64_t>(dst_page + 1) * G > L.group_cap || src_seq < 0 || tok0 < 0) {
@@ -352,6 +354,24 @@ static int launch_pack(const lf_layout& L, const void* k, const void* v, int64_t
                                                  s_seq, s_head, s_tok, jobs, dst_batch, chan_code,
                                                  rows, kmeta, status);
   return launch_status("lf_pack_pages");
+}
+
+int launch_pack_rows(const lf_layout& L, const void* k, const void* v, int dtype, int64_t s_seq, int64_t s_head,
+                     int64_t s_tok, const int32_t* jobs, int n_jobs, int dst_batch, const int32_t* chan_code,
+                     int32_t* rows, uint16_t* kmeta, int32_t* status, cudaStream_t stream) {
+  LF_CHECK_SUPPORTED(pack_smem(L, dtype == LF_F32 ? 4 : 2).total <= 227 * 1024,
+                     "K1: page %d x head_dim %d does not fit shared memory", L.page_size, L.head_dim);
+  switch (dtype) {
+    case LF_F32:
+      return launch_pack<float>(L, k, v, s_seq, s_head, s_tok, jobs, n_jobs, dst_batch, chan_code, rows, kmeta,
+                                status, stream);
+    case LF_F16:
+      return launch_pack<__half>(L, k, v, s_seq, s_head, s_tok, jobs, n_jobs, dst_batch, chan_code, rows, kmeta,
+                                 status, stream);
+    default:
+      return launch_pack<__nv_bfloat16>(L, k, v, s_seq, s_head, s_tok, jobs, n_jobs, dst_batch, chan_code, rows,
+                                        kmeta, status, stream);
+  }
 }
 
 }  // namespace lf

@@ -135,6 +135,39 @@ class _Layer:
             self.tail_v[b, :, d0:d0 + n].copy_(value[i, :, s0:s0 + n])
         self.sync_lengths()
 
+    # -- device-side commit of one token per sequence --------------------
+    def commit_token_device(self, key: torch.Tensor, value: torch.Tensor) -> None:
+        """Launch ``lf_commit_token`` for ``key``/``value`` ``[B, H, D]`` (one
+        new token for every sequence of the cache): append to the residual
+        page, pack the page when it fills, advance the device lengths.  The
+        host lengths are not touched; :meth:`advance_host` mirrors the step.
+        Graph-capturable: no host decision depends on the lengths."""
+        c = self.cache
+        B, H, D = key.shape
+        if (B, H, D) != (c.batch, c.n_kv, c.head_dim) or value.shape != key.shape:
+            raise ValueError(f"token Key/Value must be [{c.batch}, {c.n_kv}, {c.head_dim}]")
+        self.ensure_residual(key.dtype)
+        value = value.to(key.dtype)
+        if key.stride() != value.stride() or key.stride(2) != 1:
+            key, value = key.contiguous(), value.contiguous()
+        if c._commit_jobs is None:
+            c._commit_jobs = torch.empty(4 * c.batch, dtype=torch.int32, device=c.device)
+        tk = self.tail_k
+        _lib.check(_lib.lib().lf_commit_token(
+            ctypes.byref(self.layout.c), _lib.ptr(self.rows), _lib.ptr(self.kmeta), _lib.ptr(self.layout.chan_code),
+            _lib.ptr(tk), _lib.ptr(self.tail_v), tk.stride(0), tk.stride(1), _lib.ptr(self.dev_hist),
+            _lib.ptr(self.dev_tail), _lib.dtype_code(key.dtype), _lib.ptr(key), _lib.ptr(value), key.stride(0),
+            key.stride(1), c.batch, _lib.ptr(c._commit_jobs), _lib.ptr(c.status), _lib.stream_handle(c.device)),
+            "lf_commit_token")
+
+    def advance_host(self) -> None:
+        """Mirror one device-side token commit in the host lengths."""
+        P = self.cache.page_size
+        t = self.tail_len + 1
+        full = t == P
+        self.hist_len[full] += P
+        self.tail_len[:] = np.where(full, 0, t)
+
     def dequantize(self, b: int):
         """cache.py:83-90 via the CUDA dequantizer: fp32 ``[H, hist_len, D]``."""
         c = self.cache
@@ -179,6 +212,7 @@ class PackedKVCache:
                 else torch.as_tensor(level, dtype=torch.int64).cpu()
             self.layers.append(_Layer(lv, self))
         self._workspace: Optional[torch.Tensor] = None
+        self._commit_jobs: Optional[torch.Tensor] = None  # device job rows of lf_commit_token
         # Device status word written by kernels whose bounded waits expire.
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
 
@@ -322,6 +356,28 @@ class PackedKVManager:
         self.cache.commit(layer_idx, key, value)
         if layer_idx == len(self.layers) - 1:
             self.seq_len = self.layers[layer_idx].length
+
+    def commit_token(self, layer_idx: int, key: torch.Tensor, value: torch.Tensor, advance_host: bool = True) -> None:
+        """Device-side commit of one token (``key``/``value`` ``[1, H, 1, D]``):
+        ``lf_commit_token``.  With ``advance_host=False`` the host lengths
+        stay as they are (a captured step; call :meth:`advance_host` after
+        each replay)."""
+        if key.shape[0] != 1 or key.shape[2] != 1:
+            raise NotImplementedError("commit_token takes one token of one sequence")
+        layer = self.cache.layers[layer_idx]
+        if layer.hist_len[0] + layer.tail_len[0] + 1 > self.cache.row_cap:
+            raise RuntimeError("packed history capacity exceeded; grow the cache before capturing")
+        layer.commit_token_device(key[:, :, 0], value[:, :, 0])
+        if advance_host:
+            layer.advance_host()
+            if layer_idx == len(self.layers) - 1:
+                self.seq_len = self.layers[layer_idx].length
+
+    def advance_host(self) -> None:
+        """Mirror one captured decode step (every layer) in the host lengths."""
+        for layer in self.cache.layers:
+            layer.advance_host()
+        self.seq_len = self.layers[-1].length
 
     def attend(self, layer_idx: int, query: torch.Tensor, key_new: torch.Tensor, value_new: torch.Tensor,
                scaling: float) -> torch.Tensor:
