@@ -261,10 +261,10 @@ def time_k1(cache, k, v, T: int, dev) -> dict:
     sequence re-packed into the slot it already occupies (the output bytes do
     not change).  Algorithmic bytes: the pages' Key and Value in their dtype
     plus the packed rows and meta rows written."""
+    import ctypes
+
     import numpy as np
     import torch
-
-    import ctypes
 
     from logitfill_b200 import _lib
     from logitfill_b200.packed.layout import pack_pages

@@ -49,15 +49,8 @@ __device__ __forceinline__ float asym_scale(float hi, float lo, int bits) {
   s = fminf(s, 1e5f);
   return s;
 }
-__device__ __forceinline__ uint32_t asym_code(float x, float lo, float scale, int bits) {
-  float c = rintf(__fdiv_rn(__fsub_rn(x, lo), scale));  // round half to even
-  const float qmax = static_cast<float>((1 << bits) - 1);
-  c = fmaxf(c, 0.0f);
-  c = fminf(c, qmax);
-  return static_cast<uint32_t>(c);
-}
-
-// asym_code with the division done by Markstein's method (P. Markstein,
+// Code of x: clamp(round_half_even((x - lo) / scale), 0, 2^bits - 1)
+// (layout.py:12-18), with the division done by Markstein's method (P. Markstein,
 // "Computation of elementary functions on the IBM RISC System/6000
 // processor", IBM J. Res. Develop. 34(1), 1990): with rcp = RN(1/scale) and
 // q0 = RN(d * rcp) within one ulp of d / scale, the residual d - q0 * scale is
