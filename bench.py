@@ -551,6 +551,8 @@ def main() -> None:
                     help="override the config's Key policy budget (config 2 sweep: 2.25, 2.5, 3.0, 4.0)")
     ap.add_argument("--pps", type=int, default=None,
                     help="pages per K2 work item (default: the occupancy-aware planner)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the config's sequences per GPU (small cases for profiling)")
     ap.add_argument("--model-decode", action="store_true",
                     help="time the model-level decode loop, eager vs CUDA graph (not the driver's bench line)")
     ap.add_argument("--context", type=int, default=8192, help="prompt length for --model-decode")
@@ -560,6 +562,8 @@ def main() -> None:
     cfg = dict(CONFIGS[args.config])
     if args.target_bit is not None:
         cfg["target_bit"] = args.target_bit
+    if args.batch is not None:
+        cfg["batch"] = args.batch
     if args.model_decode:
         run_model_decode(args)
     elif args.impl == "reference":
