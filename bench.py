@@ -403,23 +403,60 @@ def run_b200(args, cfg) -> None:
         k2_ms.extend(a.elapsed_time(b) for a, b in ev)
     k2_avg_ms = max_over_ranks(sum(k2_ms) / len(k2_ms), dev)
 
-    # End to end: pinned host inputs -> device, step, outputs -> host, every step.
+    # End to end: every step uploads its inputs from pinned host memory and reads
+    # its outputs back.  Two device buffer sets (and a graph bound to each) let
+    # step i+1's upload and step i's read-back run on a copy stream while the
+    # GPU computes; every copy is inside the timed region.
     hq, hk, hv = (x.cpu().pin_memory() for x in (q, kn, vn))
-    hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    q2, kn2, vn2, out2 = (torch.empty_like(x) for x in (q, kn, vn, out))
+    calls2 = [DecodeCall(cache, l, q2[l], kn2[l], vn2[l], scaling, out2[l], pps=args.pps) for l in range(L)]
+    graph2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph2, capture_error_mode="thread_local"):
+        for c in calls2:
+            c.launch()
+    sets = [(q, kn, vn, out, graph), (q2, kn2, vn2, out2, graph2)]
+    houts = [torch.empty(out.shape, dtype=out.dtype, pin_memory=True) for _ in range(2)]
+    cs = torch.cuda.Stream(dev)
+    uploaded = [torch.cuda.Event() for _ in range(2)]
+    computed = [torch.cuda.Event() for _ in range(2)]
+
+    def upload(i):
+        b = i % 2
+        with torch.cuda.stream(cs):
+            if i >= 2:
+                cs.wait_event(computed[b])  # the step that last read this set has finished
+            for dst, src in zip(sets[b][:3], (hq, hk, hv)):
+                dst.copy_(src, non_blocking=True)
+            uploaded[b].record(cs)
+
+    for i in range(2):  # one untimed pass over both sets
+        upload(i)
+        stream.wait_event(uploaded[i])
+        sets[i][4].replay()
+    torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
     e0.record(stream)
-    for _ in range(args.steps):
-        q.copy_(hq, non_blocking=True)
-        kn.copy_(hk, non_blocking=True)
-        vn.copy_(hv, non_blocking=True)
-        graph.replay()
-        hout.copy_(out, non_blocking=True)
+    upload(0)
+    for i in range(args.steps):
+        b = i % 2
+        stream.wait_event(uploaded[b])
+        sets[b][4].replay()
+        computed[b].record(stream)
+        if i + 1 < args.steps:
+            upload(i + 1)
+        with torch.cuda.stream(cs):
+            cs.wait_event(computed[b])
+            houts[b].copy_(sets[b][3], non_blocking=True)
+    read_back = torch.cuda.Event()
+    read_back.record(cs)
+    stream.wait_event(read_back)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, dev)
     h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
-    d2h = hout.numel() * hout.element_size()
+    d2h = houts[0].numel() * houts[0].element_size()
+    assert torch.equal(houts[(args.steps - 1) % 2], out.cpu() if (args.steps - 1) % 2 == 0 else out2.cpu())
 
     # Algorithmic bytes (reference layout) per step and per K2 launch.
     k2_bytes = []
@@ -462,7 +499,7 @@ def run_b200(args, cfg) -> None:
             "gpu_launches": args.steps * L * 2,
         }
         print(json.dumps(line), flush=True)
-    del graph
+    del graph, graph2
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
