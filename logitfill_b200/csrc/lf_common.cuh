@@ -74,6 +74,21 @@ __device__ __forceinline__ uint32_t asym_code_rcp(float x, float lo, float scale
 template <typename F>
 __device__ __forceinline__ void dispatch_noop(F) {}
 
+// Programmatic dependent launch.  K2 and K3 are launched with programmatic
+// stream serialization, so a grid may begin launching while the kernel before
+// it in the stream drains.  grid_dep_wait() returns once that kernel has
+// completed and its memory operations are visible (at once for a grid launched
+// without the attribute); every kernel here calls it before its first global
+// access.  grid_dep_trigger() lets the next programmatic launch begin: it runs
+// only after every CTA of this grid has started (or triggered), so the CTAs of
+// the dependent grid never hold an SM a CTA of this grid still needs.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// cudaLaunchKernelExC with programmatic stream serialization.
+cudaError_t launch_programmatic(const void* kern, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                void** args);
+
 }  // namespace lf
 
 #define LF_CHECK_ARG(cond, ...)                 \

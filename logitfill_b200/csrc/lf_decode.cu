@@ -64,6 +64,8 @@ decode_partial_simt(DecodeParams p) {
   const int tid = threadIdx.x;
   const int P = L.page_size, D = L.head_dim, R = L.row_words, H = L.kv_heads;
   const int GQ = p.cg;
+  grid_dep_wait();
+  grid_dep_trigger();
   const int pages = p.hist_tokens[b] / P;
   const int n_page_splits = (pages + p.pps - 1) / p.pps;
   if (s >= n_page_splits + residual_splits(P, p.q_len)) return;
@@ -248,6 +250,8 @@ decode_merge_kernel(const float* __restrict__ ws, const int32_t* __restrict__ hi
   const int lane = threadIdx.x & 31;
   const int task = blockIdx.x * kMergeWarps + (threadIdx.x >> 5);
   const int nv = n_q * q_len;  // virtual heads per sequence
+  grid_dep_wait();
+  grid_dep_trigger();
   if (task >= batch * nv) return;
   const int b = task / nv, vh = task - b * nv;
   const int VG = nv / kv_heads, h = vh / VG, v = vh - h * VG;  // virtual head v of KV head h
@@ -313,7 +317,13 @@ static int launch_partial(const DecodeParams& p, cudaStream_t stream) {
     return LF_ERR_UNSUPPORTED;
   }
   dim3 grid(p.max_splits, p.L.kv_heads * p.n_chunks, p.batch);
-  kern<<<grid, kDecThreads, S.total, stream>>>(p);
+  DecodeParams q = p;
+  void* args[] = {&q};
+  e = launch_programmatic(reinterpret_cast<const void*>(kern), grid, dim3(kDecThreads), S.total, stream, args);
+  if (e != cudaSuccess) {
+    set_error("lf_decode_partial: %s", cudaGetErrorString(e));
+    return LF_ERR_LAUNCH;
+  }
   return launch_status("lf_decode_partial");
 }
 
@@ -342,31 +352,26 @@ static int launch_merge(const float* workspace, const int32_t* hist_tokens, int 
                         int q_len, int head_dim, int page_size, int pages_per_split, int max_splits, void* out,
                         int out_dtype, int64_t out_seq_stride, int64_t out_head_stride, int64_t out_tok_stride,
                         cudaStream_t s) {
-  const int cg = chunk_heads(n_q / kv_heads, q_len);
+  int cg = chunk_heads(n_q / kv_heads, q_len);
   const int64_t tasks = static_cast<int64_t>(batch) * n_q * q_len;
   const dim3 grid(static_cast<unsigned>((tasks + kMergeWarps - 1) / kMergeWarps));
   const dim3 block(kMergeWarps * 32);
+  const void* kern = nullptr;
   switch (out_dtype) {
-    case LF_F32:
-      decode_merge_kernel<float><<<grid, block, 0, s>>>(workspace, hist_tokens, batch, kv_heads, n_q, q_len, cg,
-                                                        head_dim, page_size, pages_per_split, max_splits,
-                                                        static_cast<float*>(out), out_seq_stride, out_head_stride,
-                                                        out_tok_stride);
-      break;
-    case LF_F16:
-      decode_merge_kernel<__half><<<grid, block, 0, s>>>(workspace, hist_tokens, batch, kv_heads, n_q, q_len, cg,
-                                                         head_dim, page_size, pages_per_split, max_splits,
-                                                         static_cast<__half*>(out), out_seq_stride, out_head_stride,
-                                                         out_tok_stride);
-      break;
-    case LF_BF16:
-      decode_merge_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(
-          workspace, hist_tokens, batch, kv_heads, n_q, q_len, cg, head_dim, page_size, pages_per_split, max_splits,
-          static_cast<__nv_bfloat16*>(out), out_seq_stride, out_head_stride, out_tok_stride);
-      break;
+    case LF_F32: kern = reinterpret_cast<const void*>(decode_merge_kernel<float>); break;
+    case LF_F16: kern = reinterpret_cast<const void*>(decode_merge_kernel<__half>); break;
+    case LF_BF16: kern = reinterpret_cast<const void*>(decode_merge_kernel<__nv_bfloat16>); break;
     default:
       set_error("lf_decode_merge: out dtype %d", out_dtype);
       return LF_ERR_INVALID_ARGUMENT;
+  }
+  void* args[] = {&workspace, &hist_tokens, &batch, &kv_heads, &n_q, &q_len, &cg,
+                  &head_dim, &page_size, &pages_per_split, &max_splits, &out, &out_seq_stride,
+                  &out_head_stride, &out_tok_stride};
+  const cudaError_t e = launch_programmatic(kern, grid, block, 0, s, args);
+  if (e != cudaSuccess) {
+    set_error("lf_decode_merge: %s", cudaGetErrorString(e));
+    return LF_ERR_LAUNCH;
   }
   return launch_status("lf_decode_merge");
 }

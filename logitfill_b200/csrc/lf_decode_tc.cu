@@ -6,15 +6,15 @@
 // current page, TMEM lane t and row t of the PV result) and one control warp.
 //
 // Control warp: lane 0 issues the 1-D bulk copies (a page's row block and
-// meta row per stage) and the MMAs; the warp builds the QK B rows of K
-// positions 128 and up (wide layouts) between its PV issue and the next copy:
-// a proxy fence in the thread that issued a bulk copy waits for that copy.
+// meta row per stage) and the MMAs, and nothing else, so that each MMA starts
+// as soon as its operands are ready.
 // Compute warps, per page i:
 //   U_K  Key codes -> u8 in TMEM (A of QK, K-major), masked in place (INT2
 //        slot k of a byte as code * 4^k, INT4 as code * 16^k); the B row of QK
 //        for K position t (tier slot c, code weight w_c): for each q-head j the
 //        fixed point X = rint(q_j[c] scale_c 2^(29-Eq-Es) / w_c), offset by 2^30 and split into
-//        four unsigned limbs (bytes); Es is the page's Key-scale exponent, from
+//        four unsigned limbs (bytes); K positions 128 and up (wide layouts)
+//        take four lanes each, two q-heads per lane; Es is the page's Key-scale exponent, from
 //        the largest scale the packer stores in the meta row; partial sums of
 //        the Key-min bias sum_c q_j[c] min_c; the token's code sum n_t (the
 //        byte sum of its code words, which is the sum of its A row).
@@ -85,7 +85,7 @@ __host__ __device__ inline TcSmem tc_smem(const lf_layout& L) {
   int off = 0;
   s.bars = off; off += 128;
   s.red = off; off += 2 * 4 * 16 * 4;   // page maxima [stage][warp][16]
-  s.redb = off; off += 2 * 5 * kGQ * 4;  // bias partials [stage][4 compute warps + control][8]
+  s.redb = off; off += 2 * 4 * kGQ * 4;  // bias partials [stage][compute warp][8]
   s.redw = off; off += 4 * kGQ * 4;     // item-end sums
   s.q16 = off; off += ((L.width[3] > 0 ? L.width[3] : 1) * kGQ * 4 + 15) / 16 * 16;
   const int hi = s.kpad > kDecThreads ? s.kpad - kDecThreads : 0;  // K positions of the control warp
@@ -229,6 +229,18 @@ __device__ __forceinline__ void qk_b_row(unsigned char* bqk, int sbo, int pp, co
   *reinterpret_cast<uint4*>(dst + sbo) = c1;
 }
 
+// Two q-heads (2 hp, 2 hp + 1) of the B row of QK at K position pp: the
+// same limbs as qk_b_row, stored as one 16-bit pair per limb.
+__device__ __forceinline__ void hi_b_row_pair(unsigned char* bqk, int sbo, int pp, int hp, float2 qv, float sc) {
+  const uint32_t ua = static_cast<uint32_t>(__float2int_rn(qv.x * sc) + (1 << 30));
+  const uint32_t ub = static_cast<uint32_t>(__float2int_rn(qv.y * sc) + (1 << 30));
+  unsigned char* dst = bqk + (pp & 7) * 16 + (pp >> 3) * 128 + 2 * hp;
+  *reinterpret_cast<uint16_t*>(dst) = static_cast<uint16_t>(__byte_perm(ua, ub, 0x0040));
+  *reinterpret_cast<uint16_t*>(dst + 8) = static_cast<uint16_t>(__byte_perm(ua, ub, 0x0051));
+  *reinterpret_cast<uint16_t*>(dst + sbo) = static_cast<uint16_t>(__byte_perm(ua, ub, 0x0062));
+  *reinterpret_cast<uint16_t*>(dst + sbo + 8) = static_cast<uint16_t>(__byte_perm(ua, ub, 0x0073));
+}
+
 // K position descriptor: meta offsets of the slot's scale and min, and the
 // power of two its unpacked code carries.  The Key codes are masked in place
 // without shifting, so INT2 slot 4i + k of a word reaches the MMA as
@@ -263,6 +275,8 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
   const int h = blockIdx.x % p.L.kv_heads, b = blockIdx.x / p.L.kv_heads;
   const int lane = tid & 31, warp = tid >> 5;
   const int H = L.kv_heads, R = L.row_words, M = L.meta_halves;
+  grid_dep_wait();
+  grid_dep_trigger();
   const int pages = p.hist_tokens[b] / kP;
   const int n_page_splits = (pages + p.pps - 1) / p.pps;
   if (s >= n_page_splits + residual_splits(kP, p.q_len)) return;
@@ -286,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S.bars + 8 * kNumBars);
   volatile int* abort_s = reinterpret_cast<volatile int*>(smem + S.bars + 8 * kNumBars + 4);
   uint32_t* red_m = reinterpret_cast<uint32_t*>(smem + S.red);  // [stage][warp][16]: 8 score keys, vscale
-  float* red_b = reinterpret_cast<float*>(smem + S.redb);        // [stage][5][8] bias partials
+  float* red_b = reinterpret_cast<float*>(smem + S.redb);        // [stage][4][8] bias partials
   float* q16_s = reinterpret_cast<float*>(smem + S.q16);         // [FP16 slot][kGQ], times scaling*log2(e)
   float* qhi_s = reinterpret_cast<float*>(smem + S.qhi);         // K positions 128..: q_j[c] 2^(29-Eq) / w_c
   int* posoff_s = reinterpret_cast<int*>(smem + S.posoff);       // K positions 128..: scale | min << 16, or -1
@@ -301,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
   const int64_t head_meta = (static_cast<int64_t>(b) * H + h) * L.group_cap;
   const float c2 = p.scaling * kLog2e;
   const int kmax_off = L.kmax_off;
-  const int n_hi = S.kpad > kDecThreads ? (S.kpad - kDecThreads) / 32 : 0;  // K positions per control lane
+  const int n_hi = S.kpad > kDecThreads ? (S.kpad - kDecThreads) / 32 : 0;  // K positions 128.. per 4 lanes
 
   // Page pg of the item -> stage pg % 2 (row block + meta row); one thread.
   auto issue_page = [&](int pg) {
@@ -317,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     for (int i = 0; i < kStages; ++i) mbar_init(&bars[kBarFull + i], 1);
     mbar_init(&bars[kBarKReady], kDecThreads);
     mbar_init(&bars[kBarVReady], kDecThreads);
-    mbar_init(&bars[kBarQK], 2);  // the QK commit + the control warp's arrive after its B rows
+    mbar_init(&bars[kBarQK], 1);
     mbar_init(&bars[kBarPV], 1);
     *abort_s = 0;
     fence_mbar_init();
@@ -398,7 +412,6 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       const int ch = p.slot_chan[(3 * H + h) * kD + i / kGQ];
       q16_s[i] = ch < 0 ? 0.f : q_s[(i % kGQ) * kD + ch] * c2;
     }
-    if (tid < 2 * 5 * kGQ) red_b[tid] = 0.f;  // the control slots stay zero without K positions 128..
   }
   tc_fence_before();
   __syncthreads();
@@ -408,50 +421,11 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
 
   if (warp == 4) {
     // ------------------------------------------------------------ control warp
-    auto wait_all = [&](uint64_t* bar, uint32_t parity) {
-      if (*abort_s) return;
-      if (!mbar_wait_bounded(bar, parity, kLimit)) *abort_s = 1;
-    };
-    // B rows of K positions 128.. for page pg (none for narrow layouts) and
-    // their bias partials, then the release arrive on the QK barrier.  The
-    // proxy fence here also waits for this warp's own copies and MMAs still in
-    // flight, so it runs only when they have all completed: after the page's
-    // copy has landed and QK(pg - 1) has finished, before PV(pg - 1) is issued.
-    auto build_hi = [&](int pg) {
-      if (n_hi > 0) {
-        const uint16_t* meta = reinterpret_cast<const uint16_t*>(stage0 + (pg & 1) * S.stage_bytes + S.rows_bytes);
-        const float fsc = exp2i(-page_scale_exp(meta, kmax_off));
-        float bias[kGQ];
-#pragma unroll
-        for (int j = 0; j < kGQ; ++j) bias[j] = 0.f;
-#pragma unroll 1
-        for (int k = 0; k < 4; ++k) {
-          if (k >= n_hi) break;
-          const int r = 32 * k + lane;
-          const int o = posoff_s[r];
-          const float4 qa = *reinterpret_cast<const float4*>(qhi_s + r * kGQ);
-          const float4 qb = *reinterpret_cast<const float4*>(qhi_s + r * kGQ + 4);
-          const float qv[kGQ] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-          const float sc = o >= 0 ? half_bits_to_float(meta[pos_scale(o)]) * fsc : 0.f;
-          const float mn = o >= 0 ? half_bits_to_float(meta[pos_min(o)]) * exp2i(pos_lg(o)) : 0.f;
-          qk_b_row<GQ>(bqk, S.bqk_sbo, kDecThreads + r, qv, sc, mn, bias);
-        }
-        const float part = warp_sum8_scatter(bias, lane);
-        if ((lane & 3) == 0)
-          red_b[(pg & 1) * 40 + 32 + (((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1))] = part;
-        fence_proxy_async_smem();
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[kBarQK]);
-    };
-
     int issued0 = 1, issued1 = 0, qk_open = 0, pv_open = 0;
     const uint32_t n_ks = static_cast<uint32_t>(S.kpad / 32);
     const uint64_t bqk_desc0 = smem_desc(bqk, 128, S.bqk_sbo);
     const uint64_t apv_desc0 = smem_desc(apv, 128, 2048);
     const uint64_t bpv_desc0 = smem_desc(bpv, 128, 2048);
-    if (n_hi > 0) wait_all(&bars[kBarFull], 0);
-    build_hi(0);
     if (lane == 0 && npg > 1) {
       issue_page(1);
       issued1 = 1;
@@ -464,14 +438,6 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
           mma_u8_ts(tmem + S.tm_qk, tmem + 8 * ks, bqk_desc0 + 32 * ks, kIdescQK, ks > 0 ? 1u : 0u);
         mma_commit(&bars[kBarQK]);
         qk_open = i + 1;
-      }
-      __syncwarp();
-      if (i + 1 < npg) {
-        if (n_hi > 0) wait_all(&bars[kBarFull + ((i + 1) & 1)], ((i + 1) >> 1) & 1);
-        wait_all(&bars[kBarQK], i & 1);  // QK(i) has read the B rows; phase i + 1 may start
-        build_hi(i + 1);
-      }
-      if (lane == 0) {
         if (!*abort_s && !mbar_wait_bounded(&bars[kBarVReady], i & 1, kLimit)) *abort_s = 1;
         tc_fence_after();
 #pragma unroll
@@ -479,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
           mma_u8_ss(tmem + S.tm_pv, apv_desc0 + 32 * ks, bpv_desc0 + 32 * ks, kIdescPV, ks > 0 ? 1u : 0u);
         mma_commit(&bars[kBarPV]);
         pv_open = i + 1;
-        // Stage i % 2 has been read by U_K(i), S(i), U_V(i) and build_hi(i): it takes page i + 2.
+        // Stage i % 2 has been read by U_K(i), S(i) and U_V(i): it takes page i + 2.
         if (i + kStages < npg && !*abort_s) {
           issue_page(i + kStages);
           if (i & 1) ++issued1; else ++issued0;
@@ -518,6 +484,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     const float mmul = po >= 0 ? exp2i(pos_lg(po)) : 0.f;
     const float cf = c2 * exp2i(eq - 29);        // fixed-point unit 2^(Eq-29) -> log2-scaled score
     const int bslot = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+    const int hp = tid & 3;                      // q-head pair of the thread's K position 128 + (tid >> 2)
 
     // U_K(i): Key codes of the thread's token -> its TMEM lane (A of QK); the
     // B row of K position tid; bias partials; the token's code sum (every bit
@@ -569,10 +536,25 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
 #pragma unroll
         for (int j = 0; j < kGQ; ++j) bias[j] = 0.f;
         qk_b_row<GQ>(bqk, S.bqk_sbo, tid, qq, sc, mn, bias);
+        // K positions 128.. (wide layouts): four lanes per position, two
+        // q-heads per lane (qhi_s is zero for the heads >= GQ).
+#pragma unroll 1
+        for (int k = 0; k < n_hi; ++k) {
+          const int r = (tid >> 2) + 32 * k;
+          const int o = posoff_s[r];
+          const float2 qv = *reinterpret_cast<const float2*>(qhi_s + r * kGQ + 2 * hp);
+          const float sc2 = o >= 0 ? half_bits_to_float(meta[pos_scale(o)]) * fsc : 0.f;
+          const float mn2 = o >= 0 ? half_bits_to_float(meta[pos_min(o)]) * exp2i(pos_lg(o)) : 0.f;
+          hi_b_row_pair(bqk, S.bqk_sbo, kDecThreads + r, hp, qv, sc2);
+          const float b0 = qv.x * mn2, b1 = qv.y * mn2;
+#pragma unroll
+          for (int j = 0; j < kGQ; ++j)
+            if (j < GQ) bias[j] += (j >> 1) == hp ? ((j & 1) ? b1 : b0) : 0.f;
+        }
         const float part = warp_sum8_scatter(bias, lane);
-        if ((lane & 3) == 0) red_b[(i & 1) * 40 + warp * kGQ + bslot] = part;
+        if ((lane & 3) == 0) red_b[(i & 1) * 32 + warp * kGQ + bslot] = part;
       } else if ((lane & 3) == 0) {
-        red_b[(i & 1) * 40 + warp * kGQ + bslot] = 0.f;
+        red_b[(i & 1) * 32 + warp * kGQ + bslot] = 0.f;
       }
       tmem_wait_st();
       fence_proxy_async_smem();
@@ -643,8 +625,8 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       named_sync(1, kDecThreads);
       // Lane j (mod 8): statistics of q-head j.  The bias is the same for
       // every token of the page, so the page max is max(score) + bias.
-      const float* rb = red_b + st * 40 + l8;
-      const float bias = ((rb[0] + rb[8]) + (rb[16] + rb[24]) + rb[32]) * cf;
+      const float* rb = red_b + st * 32 + l8;
+      const float bias = ((rb[0] + rb[8]) + (rb[16] + rb[24])) * cf;
       const uint32_t km = max(max(rm[l8], rm[16 + l8]), max(rm[32 + l8], rm[48 + l8]));
       const uint32_t vk = max(max(rm[8], rm[24]), max(rm[40], rm[56]));
       const float mnew = fmaxf(m_l, order_key_to_float(km) + bias);
@@ -806,7 +788,7 @@ int launch_partial_tc(const DecodeParams& p, int resid_dtype, int q_dtype, cudaS
   }
   dim3 grid(q.L.kv_heads * q.batch, q.max_splits, q.n_chunks);
   void* args[] = {&q};
-  cudaError_t e = cudaLaunchKernel(kern, grid, dim3(tc::kThreads), args, S.total, stream);
+  cudaError_t e = launch_programmatic(kern, grid, dim3(tc::kThreads), S.total, stream, args);
   if (e != cudaSuccess) {
     set_error("lf_decode_partial (tcgen05): %s", cudaGetErrorString(e));
     return LF_ERR_LAUNCH;

@@ -35,6 +35,21 @@ cudaError_t raise_smem_limit(const void* kern, int bytes, bool max_carveout) {
   return e;
 }
 
+cudaError_t launch_programmatic(const void* kern, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                void** args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, kern, args);
+}
+
 int launch_status(const char* what) {
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) {
