@@ -59,6 +59,8 @@ constexpr int kStages = 2;
 constexpr int kThreads = kDecThreads + 32;  // 4 compute warps + 1 control warp
 constexpr int kMaxPagesPerItem = 64;
 
+constexpr int kNumBarsMax = 7;
+
 struct TcSmem {
   int bars, red, redb, redw, q16, qhi, posoff, stage0, bqk, bpv, apv, qs, total;
   int kpad, a_cols, tm_qk, tm_pv, tm_cols, bqk_sbo, rows_bytes, meta_bytes, stage_bytes;
@@ -81,14 +83,17 @@ __host__ __device__ inline TcSmem tc_smem(const lf_layout& L) {
   s.bqk_sbo = s.kpad * 16;
   s.rows_bytes = kP * L.row_words * 4;
   s.meta_bytes = L.meta_halves * 2;
-  s.stage_bytes = (s.rows_bytes + s.meta_bytes + 127) / 128 * 128;
+  s.stage_bytes = (s.rows_bytes + s.meta_bytes + 15) / 16 * 16;
+  // Four CTAs share an SM up to 57 344 B each (228 KB per SM, 1 KB reserved
+  // per CTA); a 160-position layout with 29-word rows needs exactly that.
   int off = 0;
-  s.bars = off; off += 128;
-  s.red = off; off += 2 * 4 * 16 * 4;   // page maxima [stage][warp][16]
+  s.bars = off; off += 8 * kNumBarsMax + 8;  // mbarriers, TMEM address, abort flag
+  s.red = off; off += 2 * 4 * 12 * 4;   // page maxima [stage][warp][12]: 8 score keys, Value-scale key
+  s.redw = s.red;                        // item-end sums (after the page loop, in place of the page maxima)
   s.redb = off; off += 2 * 4 * kGQ * 4;  // bias partials [stage][compute warp][8]
-  s.redw = off; off += 4 * kGQ * 4;     // item-end sums
   s.q16 = off; off += ((L.width[3] > 0 ? L.width[3] : 1) * kGQ * 4 + 15) / 16 * 16;
-  const int hi = s.kpad > kDecThreads ? s.kpad - kDecThreads : 0;  // K positions of the control warp
+  // K positions 128..159 live in registers; 160.. (K up to 256) here.
+  const int hi = s.kpad > kDecThreads + 32 ? s.kpad - kDecThreads - 32 : 0;
   s.qhi = off; off += hi * kGQ * 4;
   s.posoff = off; off += hi * 4;
   off = (off + 127) / 128 * 128;
@@ -204,6 +209,7 @@ __device__ __forceinline__ float exp2i(int e) { return __int_as_float((e + 127) 
 
 // Barrier slots in shared memory.
 enum { kBarFull = 0, kBarKReady = kStages, kBarVReady, kBarQK, kBarPV, kNumBars };
+static_assert(kNumBars <= kNumBarsMax, "barrier slots");
 
 // One B row of QK (K position pp; qv = q_j[c] 2^(29-Eq) / w_c, zero for a
 // padding position) and its Key-min bias terms.  X = rint(qv * scale) has
@@ -299,11 +305,11 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S.bars);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S.bars + 8 * kNumBars);
   volatile int* abort_s = reinterpret_cast<volatile int*>(smem + S.bars + 8 * kNumBars + 4);
-  uint32_t* red_m = reinterpret_cast<uint32_t*>(smem + S.red);  // [stage][warp][16]: 8 score keys, vscale
+  uint32_t* red_m = reinterpret_cast<uint32_t*>(smem + S.red);  // [stage][warp][12]: 8 score keys, vscale
   float* red_b = reinterpret_cast<float*>(smem + S.redb);        // [stage][4][8] bias partials
   float* q16_s = reinterpret_cast<float*>(smem + S.q16);         // [FP16 slot][kGQ], times scaling*log2(e)
-  float* qhi_s = reinterpret_cast<float*>(smem + S.qhi);         // K positions 128..: q_j[c] 2^(29-Eq) / w_c
-  int* posoff_s = reinterpret_cast<int*>(smem + S.posoff);       // K positions 128..: scale | min << 16, or -1
+  float* qhi_s = reinterpret_cast<float*>(smem + S.qhi);         // K positions 160..: q_j[c] 2^(29-Eq) / w_c
+  int* posoff_s = reinterpret_cast<int*>(smem + S.posoff);       // K positions 160..: pos_desc, or -1
   unsigned char* stage0 = smem + S.stage0;
   unsigned char* bqk = smem + S.bqk;
   unsigned char* bpv = smem + S.bpv;
@@ -343,15 +349,21 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     tmem_alloc(tmem_slot, S.tm_cols);
     tmem_relinquish();
   }
-  float qq[kGQ];   // compute thread: q_j[c] 2^(22-Eq) of its K position
-  int po = -1;     // compute thread: scale | min << 16 offsets of its K position, or -1
+  float qq[kGQ];   // compute thread: q_j[c] 2^(29-Eq) / w_c of its K position
+  int po = -1;     // compute thread: pos_desc of its K position, or -1
+  // Compute thread: q-heads 2 hp, 2 hp + 1 of K position 128 + (tid >> 2)
+  // (wide layouts) and that position's pos_desc.
+  const int hp = tid & 3;
+  float2 qv_hi = make_float2(0.f, 0.f);
+  int po_hi = -1;
   int eq = 0;
   if (tid < kDecThreads) {
     // Query group (thread = channel), its block exponent Eq
     // (max_j,c |q_j[c]| <= 2^Eq), and the scaled query of each K position.
     // Every global load of the prologue is issued here, before any use.
     const int e = tid < S.kpad ? kpos_entry(L, p.slot_chan, h, tid) : -1;
-    const int e2 = kDecThreads + tid < S.kpad ? kpos_entry(L, p.slot_chan, h, kDecThreads + tid) : -1;
+    const int e_hi = kDecThreads < S.kpad ? kpos_entry(L, p.slot_chan, h, kDecThreads + (tid >> 2)) : -1;
+    const int e2 = kDecThreads + 32 + tid < S.kpad ? kpos_entry(L, p.slot_chan, h, kDecThreads + 32 + tid) : -1;
     const int n16 = L.width[3] * kGQ;
     const int ch16 = tid < n16 ? p.slot_chan[(3 * H + h) * kD + tid / kGQ] : -1;
     float qc[kGQ];
@@ -398,8 +410,13 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     const float qs1 = po >= 0 ? qscale * exp2i(-pos_lg(po)) : 0.f;
 #pragma unroll
     for (int j = 0; j < kGQ; ++j) qq[j] = e >= 0 ? q_s[j * kD + (e & 0xFFFF)] * qs1 : 0.f;
-    // K positions 128.. (wide layouts, K <= 256): built by the control warp.
-    if (kDecThreads + tid < S.kpad) {
+    // K positions 128.. (wide layouts, K <= 256).
+    po_hi = pos_desc(L, e_hi);
+    if (e_hi >= 0) {
+      const float qsh = qscale * exp2i(-pos_lg(po_hi));
+      qv_hi = make_float2(q_s[2 * hp * kD + (e_hi & 0xFFFF)] * qsh, q_s[(2 * hp + 1) * kD + (e_hi & 0xFFFF)] * qsh);
+    }
+    if (kDecThreads + 32 + tid < S.kpad) {
       const int po2 = pos_desc(L, e2);
       const float qs2 = po2 >= 0 ? qscale * exp2i(-pos_lg(po2)) : 0.f;
 #pragma unroll
@@ -484,7 +501,6 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     const float mmul = po >= 0 ? exp2i(pos_lg(po)) : 0.f;
     const float cf = c2 * exp2i(eq - 29);        // fixed-point unit 2^(Eq-29) -> log2-scaled score
     const int bslot = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
-    const int hp = tid & 3;                      // q-head pair of the thread's K position 128 + (tid >> 2)
 
     // U_K(i): Key codes of the thread's token -> its TMEM lane (A of QK); the
     // B row of K position tid; bias partials; the token's code sum (every bit
@@ -537,19 +553,21 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
         for (int j = 0; j < kGQ; ++j) bias[j] = 0.f;
         qk_b_row<GQ>(bqk, S.bqk_sbo, tid, qq, sc, mn, bias);
         // K positions 128.. (wide layouts): four lanes per position, two
-        // q-heads per lane (qhi_s is zero for the heads >= GQ).
-#pragma unroll 1
-        for (int k = 0; k < n_hi; ++k) {
-          const int r = (tid >> 2) + 32 * k;
-          const int o = posoff_s[r];
-          const float2 qv = *reinterpret_cast<const float2*>(qhi_s + r * kGQ + 2 * hp);
+        // q-heads per lane (the query values are zero for the heads >= GQ).
+        auto hi_row = [&](int pp, float2 qv, int o) {
           const float sc2 = o >= 0 ? half_bits_to_float(meta[pos_scale(o)]) * fsc : 0.f;
           const float mn2 = o >= 0 ? half_bits_to_float(meta[pos_min(o)]) * exp2i(pos_lg(o)) : 0.f;
-          hi_b_row_pair(bqk, S.bqk_sbo, kDecThreads + r, hp, qv, sc2);
+          hi_b_row_pair(bqk, S.bqk_sbo, pp, hp, qv, sc2);
           const float b0 = qv.x * mn2, b1 = qv.y * mn2;
 #pragma unroll
           for (int j = 0; j < kGQ; ++j)
             if (j < GQ) bias[j] += (j >> 1) == hp ? ((j & 1) ? b1 : b0) : 0.f;
+        };
+        if (n_hi > 0) hi_row(kDecThreads + (tid >> 2), qv_hi, po_hi);
+#pragma unroll 1
+        for (int k = 1; k < n_hi; ++k) {
+          const int r = (tid >> 2) + 32 * (k - 1);
+          hi_row(kDecThreads + 32 + r, *reinterpret_cast<const float2*>(qhi_s + r * kGQ + 2 * hp), posoff_s[r]);
         }
         const float part = warp_sum8_scatter(bias, lane);
         if ((lane & 3) == 0) red_b[(i & 1) * 32 + warp * kGQ + bslot] = part;
@@ -616,19 +634,19 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
         key[j] = __reduce_max_sync(0xffffffffu, order_key(x[j]));
       }
       const uint32_t vkey = __reduce_max_sync(0xffffffffu, __float_as_uint(vs));
-      uint32_t* rm = red_m + st * 64;
+      uint32_t* rm = red_m + st * 48;
       if (lane == 0) {
 #pragma unroll
-        for (int j = 0; j < kGQ; ++j) rm[warp * 16 + j] = j < GQ ? key[j] : 0u;
-        rm[warp * 16 + 8] = vkey;
+        for (int j = 0; j < kGQ; ++j) rm[warp * 12 + j] = j < GQ ? key[j] : 0u;
+        rm[warp * 12 + 8] = vkey;
       }
       named_sync(1, kDecThreads);
       // Lane j (mod 8): statistics of q-head j.  The bias is the same for
       // every token of the page, so the page max is max(score) + bias.
       const float* rb = red_b + st * 32 + l8;
       const float bias = ((rb[0] + rb[8]) + (rb[16] + rb[24])) * cf;
-      const uint32_t km = max(max(rm[l8], rm[16 + l8]), max(rm[32 + l8], rm[48 + l8]));
-      const uint32_t vk = max(max(rm[8], rm[24]), max(rm[40], rm[56]));
+      const uint32_t km = max(max(rm[l8], rm[12 + l8]), max(rm[24 + l8], rm[36 + l8]));
+      const uint32_t vk = max(max(rm[8], rm[20]), max(rm[32], rm[44]));
       const float mnew = fmaxf(m_l, order_key_to_float(km) + bias);
       const float alpha = m_l == -INFINITY ? 0.f : ex2(m_l - mnew);
       m_l = mnew;

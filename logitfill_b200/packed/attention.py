@@ -32,11 +32,15 @@ def pages_per_split(cache: PackedKVCache, layer_idx: int = 0, q_len: int = 1) ->
     start (query staging, first copy) worth ~1.5 pages; the choice minimises
     (waves of page items) x (pps + 1.5), i.e. it balances the page items
     over the SMs instead of just making the grid large.  A wave is three page
-    items per SM at most (fewer if fewer fit): measured on B200, a fourth
-    co-resident page item slows the other three (2.8 -> 3.2 us per page) and
-    takes the slot the residual items would use, so about three per SM ran
-    fastest at both 8k and 32k histories.  A wave overfull by up to 2 % still
-    counts as one.  Memoised per layer by (pages, q_len)."""
+    items per SM at most (fewer if fewer fit) while the residual items are
+    many: measured on B200, a fourth co-resident page item slows the other
+    three and takes the slot the residual items would use, so with four
+    residual items per pair at 8k histories (B 16) three per SM ran fastest
+    (8 pages per item instead of 10: 8 % slower).  When the residual items
+    fit in a quarter of the slots, a wave is every slot: they then run on the
+    kernel's tail, and at 32k histories (B 8, 4 CTAs per SM) 15 pages per
+    item ran 3 % faster than 19.  A wave overfull by up to 2 % still counts
+    as one.  Memoised per layer by (pages, q_len)."""
     layer = cache.layers[layer_idx]
     P = cache.page_size
     pages = int(layer.hist_len.max()) // P if layer.hist_len.size else 0
@@ -49,13 +53,14 @@ def pages_per_split(cache: PackedKVCache, layer_idx: int = 0, q_len: int = 1) ->
     sms = torch.cuda.get_device_properties(cache.device).multi_processor_count
     gq = cache.n_q // cache.n_kv
     pairs = cache.batch * cache.n_kv * (gq * q_len // chunk_heads(gq, q_len))
+    resid_items = pairs * _lib.lib().lf_decode_max_splits_multi(0, 1, P, q_len)
     best, best_cost = 1, None
     for pps in range(1, min(pages, MAX_PAGES_PER_SPLIT) + 1):
         occ = so.lf_decode_occupancy(ctypes.byref(layer.layout.c), cache.n_q * q_len, pps)
         if occ <= 0:
             continue
         ctas = pairs * (-(-pages // pps))
-        per_wave = sms * min(occ, 3)
+        per_wave = sms * (occ if 4 * resid_items <= sms * occ else min(occ, 3))
         waves = max(1, math.ceil(ctas / per_wave - 0.02))
         cost = waves * (pps + 1.5)
         if best_cost is None or cost < best_cost - 1e-9:
