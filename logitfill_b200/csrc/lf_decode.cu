@@ -235,7 +235,7 @@ decode_partial_simt(DecodeParams p) {
 
 // K3: one warp per (sequence, virtual head).  Lane s (mod 32) reads split s's max
 // and sum; the global max, the weights exp(m_s - M) and the normaliser are
-// warp reductions; then every lane accumulates two channels per 64 over all
+// warp reductions; then every lane accumulates its four channels over all
 // splits, the weight of split s broadcast from the lane that computed it.
 // The partial records (GQ x (D + 2) floats) are 8-byte aligned, so the
 // values are read as float2.
@@ -267,39 +267,84 @@ decode_merge_kernel(const float* __restrict__ ws, const int32_t* __restrict__ hi
   const int64_t item = static_cast<int64_t>(cg) * (D + 2);
   const float* base = ws + ((static_cast<int64_t>(b) * kv_heads + h) * (VG / cg) + c) * max_splits * item;
   const float* mstat = base + static_cast<int64_t>(cg) * D + jj;  // split s: mstat[s * item], lstat[s * item]
-  float M = -INFINITY;
-  for (int s = lane; s < n_s; s += 32) M = fmaxf(M, mstat[s * item]);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  float Lsum = 0.f;
-  for (int s = lane; s < n_s; s += 32) {
-    const float ms = mstat[s * item];
-    if (ms != -INFINITY) Lsum = fmaf(expf(ms - M), mstat[s * item + cg], Lsum);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, o);
-  const float inv = Lsum > 0.f ? 1.0f / Lsum : 0.f;
   OT* o = out + b * out_seq_stride + qh * out_head_stride + qi * out_tok_stride;
   const float* vals = base + static_cast<int64_t>(jj) * D;
-  for (int d0 = 2 * lane; d0 < D; d0 += 64) {
-    float a0 = 0.f, a1 = 0.f;
+  // Lane d covers channels (2d, 2d + 1) and (2d + 64, 2d + 65).
+  const int d0 = 2 * lane, d1 = 2 * lane + 64;
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, Lsum = 0.f;
+  // Accumulates splits [s0, s0 + cnt) with weight wl of lane k for split s0 + k;
+  // eight splits' loads are issued before any of them is used.
+  auto accumulate = [&](int s0, int cnt, float wl) {
+    int k = 0;
+    for (; k + 8 <= cnt; k += 8) {
+      float2 v0[8], v1[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float* row = vals + static_cast<int64_t>(s0 + k + u) * item;
+        v0[u] = d0 < D ? *reinterpret_cast<const float2*>(row + d0) : make_float2(0.f, 0.f);
+        v1[u] = d1 < D ? *reinterpret_cast<const float2*>(row + d1) : make_float2(0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float w = __shfl_sync(0xffffffffu, wl, k + u);
+        a0 = fmaf(w, v0[u].x, a0);
+        a1 = fmaf(w, v0[u].y, a1);
+        a2 = fmaf(w, v1[u].x, a2);
+        a3 = fmaf(w, v1[u].y, a3);
+      }
+    }
+    for (; k < cnt; ++k) {
+      const float w = __shfl_sync(0xffffffffu, wl, k);
+      const float* row = vals + static_cast<int64_t>(s0 + k) * item;
+      if (d0 < D) {
+        const float2 v = *reinterpret_cast<const float2*>(row + d0);
+        a0 = fmaf(w, v.x, a0);
+        a1 = fmaf(w, v.y, a1);
+      }
+      if (d1 < D) {
+        const float2 v = *reinterpret_cast<const float2*>(row + d1);
+        a2 = fmaf(w, v.x, a2);
+        a3 = fmaf(w, v.y, a3);
+      }
+    }
+  };
+  if (n_s <= 32) {
+    // Every split's statistics in one lane, read once.
+    const float ms = lane < n_s ? mstat[lane * item] : -INFINITY;
+    const float ls = lane < n_s ? mstat[lane * item + cg] : 0.f;
+    float M = ms;
+#pragma unroll
+    for (int sh = 16; sh > 0; sh >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sh));
+    const float wl = ms == -INFINITY ? 0.f : expf(ms - M);
+    Lsum = wl * ls;
+    accumulate(0, n_s, wl);
+  } else {
+    float M = -INFINITY;
+    for (int s = lane; s < n_s; s += 32) M = fmaxf(M, mstat[s * item]);
+#pragma unroll
+    for (int sh = 16; sh > 0; sh >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sh));
     for (int s0 = 0; s0 < n_s; s0 += 32) {
       float wl = 0.f;
       if (s0 + lane < n_s) {
         const float ms = mstat[(s0 + lane) * item];
-        wl = ms == -INFINITY ? 0.f : expf(ms - M);
+        if (ms != -INFINITY) {
+          wl = expf(ms - M);
+          Lsum = fmaf(wl, mstat[(s0 + lane) * item + cg], Lsum);
+        }
       }
-      const int cnt = min(32, n_s - s0);
-#pragma unroll 4
-      for (int k = 0; k < cnt; ++k) {
-        const float w = __shfl_sync(0xffffffffu, wl, k);
-        const float2 v = *reinterpret_cast<const float2*>(vals + (s0 + k) * item + d0);
-        a0 = fmaf(w, v.x, a0);
-        a1 = fmaf(w, v.y, a1);
-      }
+      accumulate(s0, min(32, n_s - s0), wl);
     }
+  }
+#pragma unroll
+  for (int sh = 16; sh > 0; sh >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, sh);
+  const float inv = Lsum > 0.f ? 1.0f / Lsum : 0.f;
+  if (d0 < D) {
     Scalar<OT>::store(o + d0, a0 * inv);
     Scalar<OT>::store(o + d0 + 1, a1 * inv);
+  }
+  if (d1 < D) {
+    Scalar<OT>::store(o + d1, a2 * inv);
+    Scalar<OT>::store(o + d1 + 1, a3 * inv);
   }
 }
 
@@ -587,6 +632,7 @@ extern "C" int lf_decode_merge(const float* workspace, const int32_t* hist_token
                "lf_decode_merge: batch %d n_q %d kv_heads %d", batch, n_q, kv_heads);
   LF_CHECK_ARG(page_size > 0 && pages_per_split > 0 && max_splits > 0 && head_dim > 0 && head_dim % 2 == 0,
                "lf_decode_merge: bad sizes");
+  LF_CHECK_SUPPORTED(head_dim <= lf::kDecThreads, "lf_decode_merge: head_dim %d > %d", head_dim, lf::kDecThreads);
   return lf::launch_merge(workspace, hist_tokens, batch, kv_heads, n_q, 1, head_dim, page_size, pages_per_split,
                           max_splits, out, out_dtype, out_seq_stride, out_head_stride, 0,
                           reinterpret_cast<cudaStream_t>(stream));
