@@ -28,7 +28,8 @@
 //        code masked in place, so row t holds code * 4^k(t), k(t) = (t>>2)&3;
 //        C removes the power of two exactly.
 // Order: S(i), U_K(i+1), C(i), U_V(i+1).  QK(i+1) overlaps C(i) and U_V(i+1),
-// PV(i) overlaps U_K(i+1).
+// PV(i) overlaps U_K(i+1).  Stage i % 2 takes page i + 2 as soon as S(i) has
+// read its FP16 tier (the stage's last reader), before S(i)'s softmax.
 //
 // The integer products are exact; the fixed-point rounding is 2^-29 w_c (QK,
 // w_c <= 64) and 2^-23 (PV) of the block maxima (tests/kernel_model.py models
@@ -208,7 +209,7 @@ __device__ __forceinline__ int exp2_ceil(float x) {
 __device__ __forceinline__ float exp2i(int e) { return __int_as_float((e + 127) << 23); }
 
 // Barrier slots in shared memory.
-enum { kBarFull = 0, kBarKReady = kStages, kBarVReady, kBarQK, kBarPV, kNumBars };
+enum { kBarFull = 0, kBarKReady = kStages, kBarVReady, kBarQK, kBarPV, kBarFree, kNumBars };
 static_assert(kNumBars <= kNumBarsMax, "barrier slots");
 
 // One B row of QK (K position pp; qv = q_j[c] 2^(29-Eq) / w_c, zero for a
@@ -339,6 +340,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     mbar_init(&bars[kBarVReady], kDecThreads);
     mbar_init(&bars[kBarQK], 1);
     mbar_init(&bars[kBarPV], 1);
+    mbar_init(&bars[kBarFree], kDecThreads);  // the compute warps' last read of a stage
     *abort_s = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
@@ -455,6 +457,16 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
           mma_u8_ts(tmem + S.tm_qk, tmem + 8 * ks, bqk_desc0 + 32 * ks, kIdescQK, ks > 0 ? 1u : 0u);
         mma_commit(&bars[kBarQK]);
         qk_open = i + 1;
+        // Stage i % 2 has been read by U_K(i), U_V(i) and the FP16 tier of S(i):
+        // it takes page i + 2.
+        if (i + kStages < npg && !*abort_s) {
+          if (!mbar_wait_bounded(&bars[kBarFree], i & 1, kLimit)) {
+            *abort_s = 1;
+          } else {
+            issue_page(i + kStages);
+            if (i & 1) ++issued1; else ++issued0;
+          }
+        }
         if (!*abort_s && !mbar_wait_bounded(&bars[kBarVReady], i & 1, kLimit)) *abort_s = 1;
         tc_fence_after();
 #pragma unroll
@@ -462,11 +474,6 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
           mma_u8_ss(tmem + S.tm_pv, apv_desc0 + 32 * ks, bpv_desc0 + 32 * ks, kIdescPV, ks > 0 ? 1u : 0u);
         mma_commit(&bars[kBarPV]);
         pv_open = i + 1;
-        // Stage i % 2 has been read by U_K(i), S(i) and U_V(i): it takes page i + 2.
-        if (i + kStages < npg && !*abort_s) {
-          issue_page(i + kStages);
-          if (i & 1) ++issued1; else ++issued0;
-        }
       }
       __syncwarp();
     }
@@ -617,6 +624,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       }
       const float vs = half_bits_to_float(row16[w3]);
       const float vm = half_bits_to_float(row16[w3 + 1]);
+      mbar_arrive(&bars[kBarFree]);  // the last read of this page's stage
       const float f = cf * exp2i(esc), f16 = f * 65536.f, f24 = f * 16777216.f;
       const int off64 = 64 * nsum;  // offset 2^30 = 64 * 2^24 per unit of code
       wait(&bars[kBarQK], st);
