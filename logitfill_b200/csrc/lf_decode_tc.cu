@@ -552,12 +552,12 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       nsum = static_cast<int>(ns);
       const int esc = page_scale_exp(meta, kmax_off);
       const float fsc = exp2i(-esc);
+      float bias[kGQ];
+#pragma unroll
+      for (int j = 0; j < kGQ; ++j) bias[j] = 0.f;
       if (has_pos) {
         const float sc = po >= 0 ? half_bits_to_float(meta[soff]) * fsc : 0.f;
         const float mn = half_bits_to_float(meta[moff]) * mmul;
-        float bias[kGQ];
-#pragma unroll
-        for (int j = 0; j < kGQ; ++j) bias[j] = 0.f;
         qk_b_row<GQ>(bqk, S.bqk_sbo, tid, qq, sc, mn, bias);
         // K positions 128.. (wide layouts): four lanes per position, two
         // q-heads per lane (the query values are zero for the heads >= GQ).
@@ -576,15 +576,15 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
           const int r = (tid >> 2) + 32 * (k - 1);
           hi_row(kDecThreads + 32 + r, *reinterpret_cast<const float2*>(qhi_s + r * kGQ + 2 * hp), posoff_s[r]);
         }
-        const float part = warp_sum8_scatter(bias, lane);
-        if ((lane & 3) == 0) red_b[(i & 1) * 32 + warp * kGQ + bslot] = part;
-      } else if ((lane & 3) == 0) {
-        red_b[(i & 1) * 32 + warp * kGQ + bslot] = 0.f;
       }
       tmem_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&bars[kBarKReady]);
+      // The bias partials are read only by S(i), after its named barrier: the
+      // warp reduction runs after the arrive, off the path to the QK issue.
+      const float part = warp_sum8_scatter(bias, lane);
+      if ((lane & 3) == 0) red_b[(i & 1) * 32 + warp * kGQ + bslot] = part;
       return esc;
     };
     // U_V(i): Value codes of the thread's token -> row t of the Value tile.
