@@ -659,27 +659,16 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       const float alpha = m_l == -INFINITY ? 0.f : ex2(m_l - mnew);
       m_l = mnew;
       const float off = bias - mnew;
-      if (__any_sync(0xffffffffu, l8 < GQ && alpha != 1.f)) {
-#pragma unroll
-        for (int j = 0; j < GQ; ++j) {
-          const float aj = __shfl_sync(0xffffffffu, alpha, j);
-          og[j] *= aj;
-          lt[j] *= aj;
-          lvt[j] *= aj;
-        }
-      }
       const int ev = max(-60, min(60, exp2_ceil(__uint_as_float(vk))));
       const float vsc = vs * exp2i(23 - ev);
       uint32_t U[kGQ];
 #pragma unroll
       for (int j = 0; j < kGQ; ++j) {
         if (j < GQ) {
-          const float pj = ex2(x[j] + __shfl_sync(0xffffffffu, off, j));
-          lt[j] += pj;
-          lvt[j] = fmaf(pj, vm, lvt[j]);
+          x[j] = ex2(x[j] + __shfl_sync(0xffffffffu, off, j));  // p_tj
           // Y = rint(p * vs * 2^(23 - Ev)) in [0, 2^23]: the low 24 bits of the
           // fp32 sum 2^23 + Y are Y (2^24 itself has low bits 2^23).
-          U[j] = __float_as_uint(fmaf(pj, vsc, 8388608.0f));
+          U[j] = __float_as_uint(fmaf(x[j], vsc, 8388608.0f));
         } else {
           U[j] = 0u;
         }
@@ -694,6 +683,21 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&bars[kBarVReady]);
+      // The running sums are not read by PV: rescaled and extended after the arrive.
+      if (__any_sync(0xffffffffu, l8 < GQ && alpha != 1.f)) {
+#pragma unroll
+        for (int j = 0; j < GQ; ++j) {
+          const float aj = __shfl_sync(0xffffffffu, alpha, j);
+          og[j] *= aj;
+          lt[j] *= aj;
+          lvt[j] *= aj;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < GQ; ++j) {
+        lt[j] += x[j];
+        lvt[j] = fmaf(x[j], vm, lvt[j]);
+      }
       // U_K(i+1) while PV(i) runs.
       if (i + 1 < npg) {
         wait(&bars[kBarFull + (st ^ 1)], ((i + 1) >> 1) & 1);
