@@ -89,7 +89,7 @@ __host__ __device__ inline TcSmem tc_smem(const lf_layout& L) {
   // per CTA); a 160-position layout with 29-word rows needs exactly that.
   int off = 0;
   s.bars = off; off += 8 * kNumBarsMax + 8;  // mbarriers, TMEM address, abort flag
-  s.red = off; off += 2 * 4 * 12 * 4;   // page maxima [stage][warp][12]: 8 score keys, Value-scale key
+  s.red = off; off += 2 * 4 * 12 * 4;   // page maxima [stage][warp][12]: 8 score maxima, Value-scale bits
   s.redw = s.red;                        // item-end sums (after the page loop, in place of the page maxima)
   s.redb = off; off += 2 * 4 * kGQ * 4;  // bias partials [stage][compute warp][8]
   s.q16 = off; off += ((L.width[3] > 0 ? L.width[3] : 1) * kGQ * 4 + 15) / 16 * 16;
@@ -189,12 +189,11 @@ __device__ __forceinline__ float warp_sum8_scatter(const float (&v)[kGQ], int la
   return x;
 }
 
-__device__ __forceinline__ uint32_t order_key(float f) {
-  const uint32_t u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-__device__ __forceinline__ float order_key_to_float(uint32_t k) {
-  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+// Warp maximum of a float (redux.sync .f32, sm_100a).
+__device__ __forceinline__ float warp_max_f32(float v) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
 }
 // Smallest e with x <= 2^e for finite x > 0 (x = 1.f * 2^e' -> e' or e'+1);
 // 0 for x <= 0.  Subnormal x count as 2^-126.
@@ -306,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S.bars);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S.bars + 8 * kNumBars);
   volatile int* abort_s = reinterpret_cast<volatile int*>(smem + S.bars + 8 * kNumBars + 4);
-  uint32_t* red_m = reinterpret_cast<uint32_t*>(smem + S.red);  // [stage][warp][12]: 8 score keys, vscale
+  uint32_t* red_m = reinterpret_cast<uint32_t*>(smem + S.red);  // [stage][warp][12]: 8 score maxima (bits), vscale
   float* red_b = reinterpret_cast<float*>(smem + S.redb);        // [stage][4][8] bias partials
   float* q16_s = reinterpret_cast<float*>(smem + S.q16);         // [FP16 slot][kGQ], times scaling*log2(e)
   float* qhi_s = reinterpret_cast<float*>(smem + S.qhi);         // K positions 160..: q_j[c] 2^(29-Eq) / w_c
@@ -632,20 +631,20 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       uint32_t a[32];
       tmem_ld_x32_sync(tm_a + S.tm_qk, a);
       float x[GQ];
-      uint32_t key[GQ];
+      float key[GQ];
 #pragma unroll
       for (int j = 0; j < GQ; ++j) {
         const uint32_t lo = a[j] + (a[8 + j] << 8);
         const int hi = static_cast<int>(a[24 + j]) - off64;
         x[j] = fmaf(static_cast<float>(hi), f24,
                     fmaf(static_cast<float>(a[16 + j]), f16, fmaf(static_cast<float>(lo), f, s16[j])));
-        key[j] = __reduce_max_sync(0xffffffffu, order_key(x[j]));
+        key[j] = warp_max_f32(x[j]);
       }
       const uint32_t vkey = __reduce_max_sync(0xffffffffu, __float_as_uint(vs));
       uint32_t* rm = red_m + st * 48;
       if (lane == 0) {
 #pragma unroll
-        for (int j = 0; j < kGQ; ++j) rm[warp * 12 + j] = j < GQ ? key[j] : 0u;
+        for (int j = 0; j < kGQ; ++j) rm[warp * 12 + j] = j < GQ ? __float_as_uint(key[j]) : 0u;
         rm[warp * 12 + 8] = vkey;
       }
       named_sync(1, kDecThreads);
@@ -653,9 +652,10 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       // every token of the page, so the page max is max(score) + bias.
       const float* rb = red_b + st * 32 + l8;
       const float bias = ((rb[0] + rb[8]) + (rb[16] + rb[24])) * cf;
-      const uint32_t km = max(max(rm[l8], rm[12 + l8]), max(rm[24 + l8], rm[36 + l8]));
+      const float km = fmaxf(fmaxf(__uint_as_float(rm[l8]), __uint_as_float(rm[12 + l8])),
+                             fmaxf(__uint_as_float(rm[24 + l8]), __uint_as_float(rm[36 + l8])));
       const uint32_t vk = max(max(rm[8], rm[20]), max(rm[32], rm[44]));
-      const float mnew = fmaxf(m_l, order_key_to_float(km) + bias);
+      const float mnew = fmaxf(m_l, km + bias);
       const float alpha = m_l == -INFINITY ? 0.f : ex2(m_l - mnew);
       m_l = mnew;
       const float off = bias - mnew;
