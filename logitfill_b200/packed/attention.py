@@ -25,6 +25,28 @@ def chunk_heads(gq: int, q_len: int) -> int:
     return next((c for c in range(8, 1, -1) if n % c == 0), 1)
 
 
+def plan_pages_per_split(pages: int, pairs: int, resid_items: int, sms: int, occupancy) -> int:
+    """The planner's cost model, free of the GPU: ``pairs`` (sequence, KV head,
+    head chunk) histories of ``pages`` pages each, ``resid_items`` residual
+    items in all, ``sms`` SMs and ``occupancy(pps)`` the K2 CTAs per SM (<= 0:
+    pps not launchable).  Returns the pps of least (waves of page items) x
+    (pps + 1.5), see ``pages_per_split``."""
+    if pages <= 1:
+        return 1
+    best, best_cost = 1, None
+    for pps in range(1, min(pages, MAX_PAGES_PER_SPLIT) + 1):
+        occ = occupancy(pps)
+        if occ <= 0:
+            continue
+        ctas = pairs * (-(-pages // pps))
+        per_wave = sms * (occ if 4 * resid_items <= sms * occ else min(occ, 3))
+        waves = max(1, math.ceil(ctas / per_wave - 0.02))
+        cost = waves * (pps + 1.5)
+        if best_cost is None or cost < best_cost - 1e-9:
+            best, best_cost = pps, cost
+    return best
+
+
 def pages_per_split(cache: PackedKVCache, layer_idx: int = 0, q_len: int = 1) -> int:
     """Pages per K2 work item.  Every (sequence, KV head, head chunk) history
     is cut into ceil(pages / pps) items, plus the short residual items that
@@ -53,18 +75,12 @@ def pages_per_split(cache: PackedKVCache, layer_idx: int = 0, q_len: int = 1) ->
     sms = torch.cuda.get_device_properties(cache.device).multi_processor_count
     gq = cache.n_q // cache.n_kv
     pairs = cache.batch * cache.n_kv * (gq * q_len // chunk_heads(gq, q_len))
-    resid_items = pairs * _lib.lib().lf_decode_max_splits_multi(0, 1, P, q_len)
-    best, best_cost = 1, None
-    for pps in range(1, min(pages, MAX_PAGES_PER_SPLIT) + 1):
-        occ = so.lf_decode_occupancy(ctypes.byref(layer.layout.c), cache.n_q * q_len, pps)
-        if occ <= 0:
-            continue
-        ctas = pairs * (-(-pages // pps))
-        per_wave = sms * (occ if 4 * resid_items <= sms * occ else min(occ, 3))
-        waves = max(1, math.ceil(ctas / per_wave - 0.02))
-        cost = waves * (pps + 1.5)
-        if best_cost is None or cost < best_cost - 1e-9:
-            best, best_cost = pps, cost
+    resid_items = pairs * so.lf_decode_max_splits_multi(0, 1, P, q_len)
+
+    def occ_of(pps: int) -> int:
+        return so.lf_decode_occupancy(ctypes.byref(layer.layout.c), cache.n_q * q_len, pps)
+
+    best = plan_pages_per_split(pages, pairs, resid_items, sms, occ_of)
     layer.pps_memo[key] = best
     return best
 
