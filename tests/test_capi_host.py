@@ -107,6 +107,8 @@ def test_entry_points_validate_before_launch():
                               0, 0, fake, 2, 0, 0, 1, 32, 1.0, 1, 10, fake, None, None)
     assert st == _lib.LF_ERR_UNSUPPORTED
     assert so.lf_decode_merge(None, None, 1, 1, 1, 64, 64, 1, 1, None, 0, 0, 0, None) == _lib.LF_ERR_INVALID_ARGUMENT
+    # K2 writes partials for head_dim <= 128 only; the merge refuses larger ones
+    assert so.lf_decode_merge(fake, fake, 1, 1, 1, 256, 128, 1, 1, fake, 2, 0, 0, None) == _lib.LF_ERR_UNSUPPORTED
     assert so.lf_decode_max_splits(256, 16, 128) == 16 + 4
     assert so.lf_decode_max_splits_multi(256, 16, 128, 1) == 16 + 4
     assert so.lf_decode_max_splits_multi(256, 16, 128, 16) == 16 + 5   # 127 tail + 16 new rows
