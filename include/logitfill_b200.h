@@ -268,6 +268,17 @@ LF_API int lf_decode_noalloc(const lf_layout* layout, const int32_t* rows, const
  */
 LF_API int lf_selftest_wait(int32_t* status, int64_t limit_ns, int arrive, lf_stream_t stream);
 
+/*
+ * Self-test of K1's per-element arithmetic (no counterpart in the reference;
+ * it checks the restatement of layout.py:12-18).  For i < n (device arrays):
+ * quotient[i] = (x[i] - lo[i]) / scale[i] as K1 computes it (IEEE subtract,
+ * Markstein division with RN(1 / scale)) and code[i] =
+ * clamp(round_half_even(quotient[i]), 0, 2^bits - 1).  A test compares both
+ * with IEEE division bit for bit.
+ */
+LF_API int lf_selftest_divide(const float* x, const float* lo, const float* scale, int64_t n, int bits,
+                              float* quotient, uint32_t* code, lf_stream_t stream);
+
 /* Human-readable text of a status code; detail of the last failure on this thread. */
 LF_API const char* lf_status_string(int status);
 LF_API const char* lf_last_error(void);

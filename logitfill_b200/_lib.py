@@ -17,7 +17,7 @@ LF_F32, LF_F16, LF_BF16 = 0, 1, 2
 EXPORTS = (
     "lf_layout_init", "lf_pack_pages", "lf_dequantize", "lf_decode_workspace_bytes",
     "lf_decode_max_splits", "lf_decode_occupancy", "lf_decode_partial", "lf_decode_noalloc", "lf_decode_merge",
-    "lf_decode", "lf_decode_multi", "lf_decode_max_splits_multi", "lf_commit_token", "lf_selftest_wait",
+    "lf_decode", "lf_decode_multi", "lf_decode_max_splits_multi", "lf_commit_token", "lf_selftest_wait", "lf_selftest_divide",
     "lf_status_string", "lf_last_error",
 )
 
@@ -73,6 +73,7 @@ def lib() -> ctypes.CDLL:
         "lf_commit_token": (c_int, [L, P, P, P, P, P, c_int64, c_int64, P, P, c_int, P, P, c_int64, c_int64, c_int,
                                     P, P, P]),
         "lf_selftest_wait": (c_int, [P, c_int64, c_int, P]),
+        "lf_selftest_divide": (c_int, [P, P, P, c_int64, c_int, P, P, P]),
         "lf_status_string": (c_char_p, [c_int]),
         "lf_last_error": (c_char_p, []),
     }

@@ -60,14 +60,18 @@ __device__ __forceinline__ float asym_scale(float hi, float lo, int bits) {
 // rounds to code 0 either way).  Three floating-point operations instead of a
 // division per element; tests/test_pack_gpu.py checks it against the IEEE
 // division bit for bit.
-__device__ __forceinline__ uint32_t asym_code_rcp(float x, float lo, float scale, float rcp, int bits) {
-  const float d = __fsub_rn(x, lo);
+__device__ __forceinline__ float asym_quotient_rcp(float d, float scale, float rcp) {
   const float q0 = __fmul_rn(d, rcp);
   const float r = __fmaf_rn(-q0, scale, d);
-  float c = rintf(__fmaf_rn(r, rcp, q0));  // round half to even
+  return __fmaf_rn(r, rcp, q0);
+}
+__device__ __forceinline__ uint32_t asym_code_rcp(float x, float lo, float scale, float rcp, int bits) {
+  float c = rintf(asym_quotient_rcp(__fsub_rn(x, lo), scale, rcp));  // round half to even
   const float qmax = static_cast<float>((1 << bits) - 1);
-  c = fmaxf(c, 0.0f);
+  // Upper clamp first: an infinite x - lo leaves the Markstein residual NaN,
+  // and fminf(NaN, qmax) = qmax is the code the IEEE quotient +inf gets.
   c = fminf(c, qmax);
+  c = fmaxf(c, 0.0f);
   return static_cast<uint32_t>(c);
 }
 

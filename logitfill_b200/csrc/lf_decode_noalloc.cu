@@ -12,14 +12,19 @@
 // The array is a file-scope __device__ variable of kNoAllocScratchBytes (8 MiB):
 // every GPU on which the library's device code is loaded holds it until the
 // process exits.  Host code cannot use the variable's name as a device
-// address, so the first call on each device (with that device current) looks
-// the address up with cudaGetSymbolAddress and caches it; make that first
-// call before any stream capture.  All calls share the array: two calls whose
-// kernels overlap on the GPU (different streams, or different host threads
-// without ordering) race on it and must be serialised by the caller.  Nothing
-// in the array needs to start at zero: every partial the merge reads is
-// written earlier in the same call, so the contents left by the previous call
-// are never read.
+// address, so the address is looked up with cudaGetSymbolAddress, with the
+// device current, the first time a call runs in a CUDA context, and cached
+// per context: a context created later (cudaDeviceReset, a driver-API
+// context made current by the host) loads the module again, possibly at
+// another address, and gets its own lookup.  Make the first call in each
+// context before any stream capture.  All calls share the array: two calls
+// whose kernels overlap on the GPU (different streams, or different host
+// threads without ordering) race on it and must be serialised by the caller.
+// Nothing in the array needs to start at zero: every partial the merge reads
+// is written earlier in the same call, so the contents left by the previous
+// call are never read.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "lf_common.cuh"
@@ -31,10 +36,39 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
 
-static std::mutex g_noalloc_mutex;
-static float* g_noalloc_ptr[kMaxDevices] = {};
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
 
-// Device address of the scratch array on the current device (looked up once).
+struct NoAllocSlot {
+  unsigned long long ctx_id;  // unique over the process lifetime; 0 = empty
+  float* ptr;
+};
+
+static std::mutex g_noalloc_mutex;
+static NoAllocSlot g_noalloc_slot[kMaxDevices] = {};
+static CtxGetCurrentFn g_ctx_get_current = nullptr;
+static CtxGetIdFn g_ctx_get_id = nullptr;
+
+// Driver entry points through the runtime (the library does not link libcuda).
+static int driver_entry_points() {
+  if (g_ctx_get_current != nullptr && g_ctx_get_id != nullptr) return LF_OK;
+  void* cur = nullptr;
+  void* id = nullptr;
+  cudaDriverEntryPointQueryResult q1 = cudaDriverEntryPointSymbolNotFound, q2 = cudaDriverEntryPointSymbolNotFound;
+  if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &cur, cudaEnableDefault, &q1) != cudaSuccess ||
+      cudaGetDriverEntryPoint("cuCtxGetId", &id, cudaEnableDefault, &q2) != cudaSuccess ||
+      q1 != cudaDriverEntryPointSuccess || q2 != cudaDriverEntryPointSuccess || cur == nullptr || id == nullptr) {
+    cudaGetLastError();
+    set_error("lf_decode_noalloc: driver entry points cuCtxGetCurrent / cuCtxGetId unavailable");
+    return LF_ERR_LAUNCH;
+  }
+  g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(cur);
+  g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(id);
+  return LF_OK;
+}
+
+// Device address of the scratch array in the current context (looked up once
+// per context, with its device current).
 static int noalloc_scratch(float** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -47,16 +81,42 @@ static int noalloc_scratch(float** out) {
     return LF_ERR_UNSUPPORTED;
   }
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (g_noalloc_ptr[dev] == nullptr) {
-    void* ptr = nullptr;
-    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    if (e != cudaSuccess || ptr == nullptr) {
-      set_error("lf_decode_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+  int st = driver_entry_points();
+  if (st != LF_OK) return st;
+  auto lookup = [](void** ptr) -> int {
+    const cudaError_t err = cudaGetSymbolAddress(ptr, g_noalloc_scratch);
+    if (err != cudaSuccess || *ptr == nullptr) {
+      cudaGetLastError();
+      set_error("lf_decode_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(err));
       return LF_ERR_LAUNCH;
     }
-    g_noalloc_ptr[dev] = static_cast<float*>(ptr);
+    return LF_OK;
+  };
+  CUcontext ctx = nullptr;
+  void* fresh = nullptr;
+  if (g_ctx_get_current(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+  if (ctx == nullptr) {
+    // No context on this thread yet: the runtime binds the device's primary
+    // context on the lookup, which is then this context's.
+    st = lookup(&fresh);
+    if (st != LF_OK) return st;
+    if (g_ctx_get_current(&ctx) != CUDA_SUCCESS) ctx = nullptr;
   }
-  *out = g_noalloc_ptr[dev];
+  unsigned long long ctx_id = 0;
+  if (ctx == nullptr || g_ctx_get_id(ctx, &ctx_id) != CUDA_SUCCESS || ctx_id == 0) {
+    set_error("lf_decode_noalloc: cannot identify the current CUDA context");
+    return LF_ERR_LAUNCH;
+  }
+  NoAllocSlot& slot = g_noalloc_slot[dev];
+  if (slot.ctx_id != ctx_id || slot.ptr == nullptr) {
+    if (fresh == nullptr) {
+      st = lookup(&fresh);
+      if (st != LF_OK) return st;
+    }
+    slot.ctx_id = ctx_id;
+    slot.ptr = static_cast<float*>(fresh);
+  }
+  *out = slot.ptr;
   return LF_OK;
 }
 
@@ -72,6 +132,11 @@ extern "C" int lf_decode_noalloc(const lf_layout* layout, const int32_t* rows, c
                                  void* out, int out_dtype, int64_t out_seq_stride, int64_t out_head_stride,
                                  int32_t* status, lf_stream_t stream) {
   LF_CHECK_ARG(layout != nullptr, "lf_decode_noalloc: null layout");
+  // Output checks before anything is launched (lf_decode repeats them).
+  LF_CHECK_ARG(out != nullptr, "lf_decode_noalloc: null output");
+  LF_CHECK_ARG(out_dtype == LF_F32 || out_dtype == LF_F16 || out_dtype == LF_BF16,
+               "lf_decode_noalloc: out dtype %d", out_dtype);
+  LF_CHECK_ARG(layout->head_dim % 2 == 0, "lf_decode_noalloc: head_dim %d must be even", layout->head_dim);
   const size_t need = lf_decode_workspace_bytes(batch, layout->kv_heads, n_q, layout->head_dim, max_splits);
   LF_CHECK_ARG(need > 0, "lf_decode_noalloc: batch %d, n_q %d, max_splits %d give no partials", batch, n_q,
                max_splits);
@@ -80,13 +145,11 @@ extern "C" int lf_decode_noalloc(const lf_layout* layout, const int32_t* rows, c
                "fixed %zu-byte scratch; use lf_decode_partial/lf_decode_merge with a caller workspace",
                need, batch, layout->kv_heads, max_splits, lf::kNoAllocScratchBytes);
   float* scratch = nullptr;
-  int st = lf::noalloc_scratch(&scratch);
+  const int st = lf::noalloc_scratch(&scratch);
   if (st != LF_OK) return st;
-  st = lf_decode_partial(layout, rows, kmeta, slot_chan, hist_tokens, tail_k, tail_v, tail_seq_stride,
-                         tail_head_stride, tail_len, resid_dtype, k_new, v_new, new_seq_stride, new_head_stride, q,
-                         q_dtype, q_seq_stride, q_head_stride, batch, n_q, scaling, pages_per_split, max_splits,
-                         scratch, status, stream);
-  if (st != LF_OK) return st;
-  return lf_decode_merge(scratch, hist_tokens, batch, layout->kv_heads, n_q, layout->head_dim, layout->page_size,
-                         pages_per_split, max_splits, out, out_dtype, out_seq_stride, out_head_stride, stream);
+  // lf_decode validates every input before it launches K2, then launches K3.
+  return lf_decode(layout, rows, kmeta, slot_chan, hist_tokens, tail_k, tail_v, tail_seq_stride, tail_head_stride,
+                   tail_len, resid_dtype, k_new, v_new, new_seq_stride, new_head_stride, q, q_dtype, q_seq_stride,
+                   q_head_stride, batch, n_q, scaling, pages_per_split, max_splits, scratch, out, out_dtype,
+                   out_seq_stride, out_head_stride, status, stream);
 }

@@ -29,3 +29,35 @@ extern "C" int lf_selftest_wait(int32_t* status, int64_t limit_ns, int arrive, l
       status, static_cast<uint64_t>(limit_ns), arrive);
   return lf::launch_status("lf_selftest_wait");
 }
+
+// Self-test of K1's per-element division: for each (x, lo, scale) triple the
+// quotient (x - lo) / scale and the code exactly as pack_pages_kernel forms
+// them (IEEE subtract, Markstein division with rcp = RN(1 / scale), round
+// half to even, clamp to [0, 2^bits - 1]).
+namespace lf {
+
+__global__ void selftest_divide_kernel(const float* __restrict__ x, const float* __restrict__ lo,
+                                       const float* __restrict__ scale, int64_t n, int bits,
+                                       float* __restrict__ quot, uint32_t* __restrict__ code) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float s = scale[i], rcp = __frcp_rn(s);
+    quot[i] = asym_quotient_rcp(__fsub_rn(x[i], lo[i]), s, rcp);
+    code[i] = asym_code_rcp(x[i], lo[i], s, rcp, bits);
+  }
+}
+
+}  // namespace lf
+
+extern "C" int lf_selftest_divide(const float* x, const float* lo, const float* scale, int64_t n, int bits,
+                                  float* quotient, uint32_t* code, lf_stream_t stream) {
+  LF_CHECK_ARG(x && lo && scale && quotient && code, "lf_selftest_divide: null pointer");
+  LF_CHECK_ARG(n >= 0, "lf_selftest_divide: n %lld", static_cast<long long>(n));
+  LF_CHECK_ARG(bits == 2 || bits == 4 || bits == 8, "lf_selftest_divide: bits %d", bits);
+  if (n == 0) return LF_OK;
+  const int64_t blocks64 = (n + 255) / 256;
+  const int blocks = static_cast<int>(blocks64 < 148 * 32 ? blocks64 : 148 * 32);
+  lf::selftest_divide_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(x, lo, scale, n, bits,
+                                                                                         quotient, code);
+  return lf::launch_status("lf_selftest_divide");
+}

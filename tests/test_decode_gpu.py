@@ -218,3 +218,40 @@ def test_sharp_attention_tc_path(q_scale):
                                    vn[0, :, None].float().cpu().numpy(), D ** -0.5)
     ok, err, cos = attention_close(out[0].cpu().numpy(), want[:, 0], atol=5e-4)
     assert ok, (err, cos)
+
+
+def test_config4_geometry_16k_sampled():
+    """Config-4 geometry at its real length: 40 q / 8 KV heads (GQA 5),
+    16384-token packed history plus ragged 0-127 bf16 tails, target_bit 2.5;
+    sampled sequences against the oracle at two fixed split sizes and the
+    planner's own choice, and split-merge invariance between them."""
+    from logitfill_b200.packed.attention import pages_per_split
+
+    B, H, NQ, D, T = 3, 8, 40, 128, 16384
+    levels = synthetic_levels(1, H, D, 2.5, seed=4)[0]
+    tails = [0, 77, 127]
+    k, v = synthetic_kv(B, H, T + 128, D, seed=4, layer=0, device="cuda")
+    cache = PackedKVCache([levels], B, NQ, H, D, device="cuda", capacity=T + 128)
+    cache.prefill(0, k, v, [T + t for t in tails])
+    g = torch.Generator(device="cuda").manual_seed(6)
+    q = torch.randn(B, NQ, D, generator=g, device="cuda").to(torch.bfloat16)
+    kn = torch.stack([k[b, :, T + t] for b, t in enumerate(tails)]).contiguous()
+    vn = torch.stack([v[b, :, T + t] for b, t in enumerate(tails)]).contiguous()
+    plans = sorted({5, 32, pages_per_split(cache, 0)})
+    outs = {}
+    for pps in plans:
+        out = torch.empty(B, NQ, D, dtype=torch.float32, device="cuda")
+        decode_into(cache, 0, q, kn, vn, D ** -0.5, out, pps=pps)
+        outs[pps] = out
+    cache.check_status()
+    for o in outs.values():
+        assert float((o - outs[plans[0]]).abs().max()) < 1e-3
+    for b in (1, 2):
+        n = T + tails[b]
+        ref = orc.OracleLayer(levels, 128, 128, 128, 2)
+        ref.append(k[b, :, :n].float().cpu().numpy(), v[b, :, :n].float().cpu().numpy())
+        want = orc.reference_attention(ref, q[b, :, None].float().cpu().numpy(), kn[b, :, None].float().cpu().numpy(),
+                                       vn[b, :, None].float().cpu().numpy(), D ** -0.5)
+        for pps, o in outs.items():
+            ok, err, cos = attention_close(o[b].cpu().numpy(), want[:, 0])
+            assert ok, (b, pps, err, cos)
