@@ -1,7 +1,8 @@
 #!/usr/bin/env python
 """Benchmark of the packed decode-attention hot path (one JSON line).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 1|2|4] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 1|2|4]
+                    [--shard weak|batch|kv] [--k2 auto|tc|simt] [--impl b200|reference]
 
 A *step* is one decode step of attention for every layer of the model over a
 batch of sequences: for each of the L layers, K2 (split-K GQA decode over the
@@ -10,20 +11,37 @@ the metric the reference's ``packed`` backend would be measured on
 (``scripts/evaluate.py:1-6``): decode tokens/s = batch / step time, plus the
 HBM bandwidth it implies over the algorithmic bytes of the packed layout.
 
-Workload (default): Qwen2-7B geometry, 28 layers, 28 q /
+Main line (default): Qwen2-7B geometry, 28 layers, 28 q /
 4 KV heads, head_dim 128, batch 16 per GPU, 8192-token packed history plus a
 seeded U{0..127}-token bf16 residual per sequence, synthetic K/V with 5 %
 outlier Key channels, seeded policy at target_bit 2.5 (Key mean 3.0 bit).
 Per-GPU work is fixed as N grows (``scaling: weak``): every rank holds its own
-16 sequences, no collective on the data path.
+16 sequences, no collective on the data path.  The line also carries:
+
+* ``config2`` (N = 1): config 2, 32768-token histories, batch 8, target_bit 3.0
+  (the north star's >= 70 % HBM target is stated there), with its own
+  ``ms_per_step``, ``roofline`` and ``e2e``;
+* ``config4_kv``: config 4 (64 layers, 40 q / 8 KV heads, batch 64, 16384-token
+  histories, target_bit 2.5) sharded by KV head over the N ranks, each layer's
+  head-sharded output all-gathered over NCCL inside the timed step (strong
+  scaling: the total work is fixed);
+* ``config4_batch`` (N > 1): config 4 sharded by sequence (strong, no collective).
 
 Timing: W untimed warm-up steps, then K timed steps replayed from a CUDA graph
-of the L per-layer K2+K3 launches, bracketed by barrier + synchronize, timed
-with CUDA events on the launching stream, max over ranks.  The step's working
-set (~1.5 GB) is far larger than the 126 MB L2, so no flush is needed.
-``--impl reference`` times the reference algorithm on the host CPU instead
-(the numpy restatement in ``oracle/``; the reference itself is Python and
-cannot travel to the GPU box), on all host cores, one bounded sample per step.
+of the per-layer launches, bracketed by barrier + synchronize, timed with CUDA
+events on the launching stream, max over ranks.  Every step's working set
+(>= 1.5 GB) is far larger than the 126 MB L2, so no flush is needed.  K2's
+average launch duration comes from a second CUDA graph holding only the L K2
+launches (same programmatic launches, K3 left out), event-timed and divided
+by L, so it always fits inside the step.  ``e2e`` repeats the step through
+the public API with every step's query / new K/V uploaded from pinned host
+memory and the outputs read back, the copies inside the timed region and
+overlapped with the previous step's attention (a pipelined attention-only
+loop, not a model step).  ``cpu_baseline`` times the reference's algorithm on
+the host cores: a torch restatement of its dense packed path and the numpy
+oracle, one process per core (``oracle/``; the reference itself is Python and
+does not exist on the GPU box).  ``--impl reference`` times the torch
+restatement alone, rank 0 only.
 """
 from __future__ import annotations
 
@@ -32,6 +50,7 @@ import json
 import os
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -119,16 +138,16 @@ def algorithmic_bytes(widths_words, hist_tokens, tails, n_q, n_kv, head_dim, pag
 
 # ------------------------------------------------------------- clocks -------
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples during the timed region."""
+    """nvidia-smi clock / throttle-reason samples during the timed region
+    (written to a temporary file, read back by ``summary``)."""
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_gpu{index}.csv"
+        self.path = Path(tempfile.gettempdir()) / f"lf_bench_clocks_gpu{index}_{os.getpid()}.csv"
 
     def __enter__(self):
         try:
-            self.path.parent.mkdir(exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index),
@@ -169,19 +188,38 @@ class ClockSampler:
             for name, flag in zip(names, parts[5:9]):
                 if flag.lower() == "active":
                     reasons.add(name)
+        try:
+            self.path.unlink()
+        except OSError:
+            pass
         under_load = [x for x in sm if smax and x > 0.3 * smax] or sm
         return {"sm_mhz": statistics.median(under_load) if under_load else None, "sm_max_mhz": smax,
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
 # ------------------------------------------------------------ CPU legs ------
-def _cpu_sample_worker(args):
-    """Time the reference algorithm (oracle port) on one (sequence, layer) of the workload."""
-    cfg, layer, tail, budget_s = args
-    import numpy as np
+def host_cores() -> int:
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except AttributeError:
+        return max(1, os.cpu_count() or 1)
 
-    from oracle import packed_ref as orc
+
+def _cpu_sample_worker(args):
+    """Time the reference algorithm on one (sequence, layer) of the workload:
+    ``kind`` "torch" (restatement of the reference's torch path) or "numpy"
+    (the oracle).  One core per worker."""
+    cfg, layer, tail, budget_s, kind, n_steps = args
+    import numpy as np
+    import torch
+
+    torch.set_num_threads(1)
+    from threadpoolctl import threadpool_limits
+
+    threadpool_limits(1)
     from logitfill_b200.synthetic import synthetic_kv, synthetic_levels
+    from oracle import packed_ref as orc
+    from oracle import packed_ref_torch as orct
 
     D, H = cfg["head_dim"], cfg["n_kv"]
     levels = synthetic_levels(cfg["layers"], H, D, cfg["target_bit"], seed=cfg["seed"])[layer]
@@ -192,65 +230,66 @@ def _cpu_sample_worker(args):
     store.append(k[:, :n], v[:, :n])
     rng = np.random.default_rng(layer)
     q = rng.standard_normal((cfg["n_q"], 1, D)).astype(np.float32)
-    from threadpoolctl import threadpool_limits
+    fn = orct.reference_attention if kind == "torch" else orc.reference_attention
+    args = (store, q, k[:, n:n + 1], v[:, n:n + 1], D ** -0.5)
+    fn(*args)  # untimed first touch
+    per_step = []
+    for _ in range(n_steps):
+        times = []
+        t_end = time.perf_counter() + budget_s
+        while True:
+            t0 = time.perf_counter()
+            fn(*args)
+            times.append(time.perf_counter() - t0)
+            if time.perf_counter() > t_end:
+                break
+        per_step.append(times)
+    return per_step
 
-    threadpool_limits(1)  # one core per worker: `cores` counts workers
-    orc.reference_attention(store, q, k[:, n:n + 1], v[:, n:n + 1], D ** -0.5)  # untimed first touch
-    times = []
-    t_end = time.perf_counter() + budget_s
-    while True:
-        t0 = time.perf_counter()
-        orc.reference_attention(store, q, k[:, n:n + 1], v[:, n:n + 1], D ** -0.5)
-        times.append(time.perf_counter() - t0)
-        if time.perf_counter() > t_end:
-            break
-    return times
 
-
-def cpu_decode_rate(cfg: dict, budget_s: float, workers: int) -> dict:
-    """Decode tok/s of the reference algorithm on the host: one (seq, layer)
-    attention call takes t seconds, a step needs batch x layers of them."""
+def cpu_decode_rates(cfg: dict, budget_s: float, workers: int, kind: str, n_steps: int = 1) -> list[dict]:
+    """Decode tok/s of the reference algorithm on the host, per step: every
+    worker process (one core each) times its own (sequence, layer) attention
+    calls for ``budget_s``; the host completes ``workers / t_call`` calls per
+    second and one token per sequence needs ``layers`` of them."""
     import multiprocessing as mp
 
     tails = tails_for(cfg, 0)
-    jobs = [(cfg, (i * 7) % cfg["layers"], tails[i % len(tails)], budget_s) for i in range(workers)]
-    if workers == 1:
-        results = [_cpu_sample_worker(jobs[0])]
-    else:
-        with mp.get_context("spawn").Pool(workers) as pool:
-            results = pool.map(_cpu_sample_worker, jobs)
-    calls = sum(len(r) for r in results)
-    per_call = sum(sum(r) for r in results) / calls
-    # `workers` calls run concurrently: throughput = workers / per_call (seq, layer) calls/s.
-    calls_per_s = workers / per_call
-    tok_s = calls_per_s / cfg["layers"]   # one token per sequence needs `layers` calls
-    return {"value": tok_s, "unit": "tok/s", "cores": workers, "calls": calls,
-            "sec_per_call": per_call,
-            "sample": f"{calls} reference_attention calls (oracle port) on (seq, layer) samples of "
-                      f"{cfg['name']} ({cfg['history']}-token packed history + bf16 tail), "
-                      f"{workers} process(es), extrapolated to tok/s = {workers}/(t_call x {cfg['layers']} layers)"}
+    jobs = [(cfg, (i * 7) % cfg["layers"], tails[i % len(tails)], budget_s, kind, n_steps) for i in range(workers)]
+    with mp.get_context("spawn").Pool(workers) as pool:
+        results = pool.map(_cpu_sample_worker, jobs)
+    label = {"torch": "torch restatement of reference.py:30-56", "numpy": "numpy oracle"}[kind]
+    out = []
+    for s in range(n_steps):
+        calls = sum(len(r[s]) for r in results)
+        per_call = sum(sum(r[s]) for r in results) / calls
+        tok_s = workers / per_call / cfg["layers"]
+        out.append({"value": tok_s, "unit": "tok/s", "cores": workers, "kind": "port", "calls": calls,
+                    "sec_per_call": per_call,
+                    "sample": f"{calls} reference_attention calls ({label}) on {workers} (sequence, layer) samples "
+                              f"of {cfg['name']} ({cfg['history']}-token packed history + bf16 tail), one process "
+                              f"per core for {budget_s:.0f} s; tok/s = {workers} / (t_call x {cfg['layers']} layers)"})
+    return out
 
 
 def run_reference(args, cfg) -> None:
+    """The reference's algorithm on the host CPU (rank 0 only): the torch
+    restatement of its dense packed path, one process per core."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    workers = max(1, os.cpu_count() or 1)
-    budget = max(1.0, min(20.0, 60.0 / max(1, args.steps + args.warmup)))
-    values = []
-    for i in range(args.warmup + args.steps):
-        res = cpu_decode_rate(cfg, budget, workers)
-        if i >= args.warmup:
-            values.append(res)
-    tok_s = sum(r["value"] for r in values) / len(values)
-    ms = cfg["batch"] / tok_s * 1e3
+    workers = host_cores()
+    n = args.warmup + args.steps
+    budget = max(1.0, min(10.0, 120.0 / n))
+    rates = cpu_decode_rates(cfg, budget, workers, "torch", n_steps=n)[args.warmup:]
+    tok_s = sum(r["value"] for r in rates) / len(rates)
     line = {
         "impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": workload_config(cfg, args.gpus),
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": cfg["batch"] / tok_s * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(cfg, args.gpus, "weak"),
         "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": workers, "kind": "port",
-                         "sample": values[-1]["sample"]},
+                         "sample": rates[-1]["sample"] + f"; {args.steps} timed steps after {args.warmup} warm-up"},
         "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -301,121 +340,192 @@ def time_k1(cache, k, v, T: int, dev) -> dict:
             "bytes_per_launch": moved, "avg_launch_ms": ms, "achieved": moved / (ms * 1e-3) / 1e9}
 
 
-def workload_config(cfg: dict, n_gpus: int) -> dict:
+def workload_config(cfg: dict, n_gpus: int, shard: str) -> dict:
+    per_gpu = cfg["batch"] if shard in ("weak", "kv") else cfg["batch"] // n_gpus
+    par = {"weak": f"dp{n_gpus} (sequences sharded, {cfg['batch']} per GPU, no collective)",
+           "batch": f"dp{n_gpus} ({cfg['batch']} sequences split over the GPUs, no collective)",
+           "kv": f"kv{n_gpus} ({cfg['n_kv']} KV heads split over the GPUs, NCCL all-gather of each layer's "
+                 f"output)"}[shard]
     return {
         "workload": f"{cfg['name']}: {cfg['layers']} layers, {cfg['n_q']} q / {cfg['n_kv']} kv heads, "
-                    f"head_dim {cfg['head_dim']}, batch {cfg['batch']} per GPU, {cfg['history']}-token packed "
+                    f"head_dim {cfg['head_dim']}, batch {cfg['batch']}"
+                    + (" per GPU" if shard == "weak" else "") + f", {cfg['history']}-token packed "
                     f"history + U{{0..127}} bf16 residual + 1 new token, target_bit {cfg['target_bit']}",
-        "layers": cfg["layers"], "batch_per_gpu": cfg["batch"], "global_batch": cfg["batch"] * n_gpus,
+        "layers": cfg["layers"], "batch_per_gpu": per_gpu,
+        "global_batch": cfg["batch"] * n_gpus if shard == "weak" else cfg["batch"],
         "history_tokens": cfg["history"], "n_q": cfg["n_q"], "n_kv": cfg["n_kv"], "head_dim": cfg["head_dim"],
         "page_size": 128, "target_bit": cfg["target_bit"], "bit_v": 2,
         "l2": "no flush: per-step working set > 126 MB L2",
-        "parallelism": f"dp{n_gpus} (sequences sharded, no collective)",
+        "parallelism": par,
     }
 
 
 # ------------------------------------------------------------- GPU leg ------
-def run_b200(args, cfg) -> None:
-    import numpy as np
-    import torch
-    import torch.distributed as dist
+class Workload:
+    """One rank's share of a config: the packed caches of every layer,
+    per-step inputs, outputs and the per-layer decode calls."""
 
-    from logitfill_b200.packed import PackedKVCache
-    from logitfill_b200.packed.attention import DecodeCall
-    from logitfill_b200.synthetic import mean_key_bits, synthetic_kv, synthetic_levels
+    def __init__(self, cfg: dict, rank: int, world: int, shard: str, dev, pps=None, with_k1=False):
+        import torch
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
+        from logitfill_b200.packed import PackedKVCache
+        from logitfill_b200.packed.attention import DecodeCall
+        from logitfill_b200.sharding import kv_head_range, shard_levels
+        from logitfill_b200.synthetic import synthetic_kv, synthetic_levels
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        self.cfg, self.rank, self.world, self.shard, self.dev = cfg, rank, world, shard, dev
+        L, D, T = cfg["layers"], cfg["head_dim"], cfg["history"]
+        H, NQ, B = cfg["n_kv"], cfg["n_q"], cfg["batch"]
+        levels = list(synthetic_levels(L, H, D, cfg["target_bit"], seed=cfg["seed"]))
+        tails = tails_for(cfg, rank if shard == "weak" else 0)
+        if shard == "kv":
+            h0, h1, q0, q1 = kv_head_range(H, NQ, world, rank)
+            levels = shard_levels(levels, H, world, rank)
+            H, NQ = h1 - h0, q1 - q0
+        elif shard == "batch":
+            if B % world:
+                raise ValueError(f"batch {B} does not split over {world} GPUs")
+            per = B // world
+            tails = tails[rank * per:(rank + 1) * per]
+            B = per
+        self.L, self.B, self.NQ, self.H, self.D = L, B, NQ, H, D
+        self.levels = levels
+        lengths = [T + t for t in tails]
+        cache = PackedKVCache(levels, B, NQ, H, D, device=dev, capacity=T + 128)
+        self.k1 = None
+        for layer in range(L):
+            k, v = synthetic_kv(B, H, T + 128, D, seed=cfg["seed"] * 1000 + rank, layer=layer, device=dev)
+            cache.prefill(layer, k, v, lengths)
+            if layer == 0 and with_k1:
+                torch.cuda.synchronize()
+                self.k1 = time_k1(cache, k, v, T, dev)
+            del k, v
+        torch.cuda.synchronize()
+        cache.check_status()
+        self.cache = cache
+        gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+        self.q = torch.randn(L, B, NQ, D, generator=gen, device=dev).to(torch.bfloat16)
+        self.kn = torch.randn(L, B, H, D, generator=gen, device=dev).to(torch.bfloat16)
+        self.vn = torch.randn(L, B, H, D, generator=gen, device=dev).to(torch.bfloat16)
+        self.out = torch.empty(L, B, NQ, D, device=dev, dtype=torch.bfloat16)
+        self.gathered = None
+        if shard == "kv" and world > 1:
+            self.gathered = torch.empty(L, world, B, NQ, D, device=dev, dtype=torch.bfloat16)
+        self.scaling = D ** -0.5
+        self.calls = [DecodeCall(cache, l, self.q[l], self.kn[l], self.vn[l], self.scaling, self.out[l], pps=pps)
+                      for l in range(L)]
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
+    def step(self, calls=None, out=None, gathered=None):
+        from logitfill_b200.sharding import gather_heads
 
-    L, B, NQ, H, D = cfg["layers"], cfg["batch"], cfg["n_q"], cfg["n_kv"], cfg["head_dim"]
-    T = cfg["history"]
-    levels = synthetic_levels(L, H, D, cfg["target_bit"], seed=cfg["seed"])
-    tails = tails_for(cfg, rank)
-    lengths = [T + t for t in tails]
-    cache = PackedKVCache(list(levels), B, NQ, H, D, device=dev, capacity=T + 128)
-    for layer in range(L):
-        k, v = synthetic_kv(B, H, T + 128, D, seed=cfg["seed"] * 1000 + rank, layer=layer, device=dev)
-        cache.prefill(layer, k, v, lengths)
-        if layer == 0:
-            k1_src = (k, v)  # kept for the K1 timing below
-        del k, v
-    torch.cuda.synchronize()
-    k1 = time_k1(cache, *k1_src, T, dev)
-    del k1_src
-    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
-    q = torch.randn(L, B, NQ, D, generator=gen, device=dev).to(torch.bfloat16)
-    kn = torch.randn(L, B, H, D, generator=gen, device=dev).to(torch.bfloat16)
-    vn = torch.randn(L, B, H, D, generator=gen, device=dev).to(torch.bfloat16)
-    out = torch.empty(L, B, NQ, D, device=dev, dtype=torch.bfloat16)
-    scaling = D ** -0.5
-    calls = [DecodeCall(cache, l, q[l], kn[l], vn[l], scaling, out[l], pps=args.pps) for l in range(L)]
-
-    def step():
-        for c in calls:
+        calls = calls or self.calls
+        out = self.out if out is None else out
+        gathered = self.gathered if gathered is None else gathered
+        for l, c in enumerate(calls):
             c.launch()
+            if self.shard == "kv" and self.world > 1:
+                gather_heads(out[l], gathered[l])
 
-    # Warm-up (also configures kernels before capture).
-    for _ in range(max(args.warmup, 1)):
-        step()
+    def bytes_per_step(self):
+        k2_bytes, total = [], 0
+        for layer in self.cache.layers:
+            c = layer.layout.c
+            ww = (c.width[0], c.width[1], c.width[2], c.width[3], c.words[0], c.words[1], c.words[2])
+            kb, tb = algorithmic_bytes(ww, layer.hist_len.tolist(), layer.tail_len.tolist(), self.NQ, self.H, self.D)
+            k2_bytes.append(kb)
+            total += tb
+        return sum(k2_bytes) / len(k2_bytes), total
+
+
+def _graph(fn):
+    import torch
+
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, capture_error_mode="thread_local"):
+        fn()
+    return g
+
+
+def _timed_replays(graph, steps: int, stream, barrier, clocks=None) -> float:
+    """ms per replay of ``graph`` over ``steps`` replays (CUDA events on the
+    launching stream, barrier + synchronize on both sides)."""
+    import torch
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
     torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, capture_error_mode="thread_local"):
-        step()
-    for _ in range(args.warmup):
+    e0.record(stream)
+    for _ in range(steps):
+        graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    return e0.elapsed_time(e1) / steps
+
+
+def measure(w: Workload, steps: int, warmup: int, barrier, clocks_index=None, e2e=True) -> dict:
+    """Step time (graph replay), K2-only graph time, e2e, bytes and roofline
+    of one workload on this rank; times are maxima over ranks."""
+    import torch
+
+    dev = w.dev
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(warmup, 1)):  # eager warm-up (also configures the kernels before capture)
+        w.step()
+    torch.cuda.synchronize()
+    graph = _graph(w.step)
+    for _ in range(warmup):
         graph.replay()
     torch.cuda.synchronize()
-
-    stream = torch.cuda.current_stream(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        barrier()
-        torch.cuda.synchronize()
-        e0.record(stream)
-        for _ in range(args.steps):
-            graph.replay()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        barrier()
-    ms = e0.elapsed_time(e1) / args.steps
+    clocks = None
+    if clocks_index is not None:
+        with ClockSampler(clocks_index) as cs:
+            ms = _timed_replays(graph, steps, stream, barrier)
+        clocks = cs.summary()
+    else:
+        ms = _timed_replays(graph, steps, stream, barrier)
     ms_max = max_over_ranks(ms, dev)
 
-    # K2 launch durations over the same kind of timed steps (eager launches, events per K2).
-    k2_ms = []
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
-    for _ in range(args.steps):
-        for (a, b), c in zip(ev, calls):
-            a.record(stream)
-            c.launch_partial()
-            b.record(stream)
-            c.launch_merge()
-        torch.cuda.synchronize()
-        k2_ms.extend(a.elapsed_time(b) for a, b in ev)
-    k2_avg_ms = max_over_ranks(sum(k2_ms) / len(k2_ms), dev)
+    # K2 alone: a graph of the L K2 launches (programmatic launches as in the step).
+    k2_graph = _graph(lambda: [c.launch_partial() for c in w.calls])
+    for _ in range(warmup):
+        k2_graph.replay()
+    k2_step_ms = max_over_ranks(_timed_replays(k2_graph, steps, stream, barrier), dev)
+    k2_avg_ms = k2_step_ms / w.L
+    del k2_graph
 
-    # End to end: every step uploads its inputs from pinned host memory and reads
-    # its outputs back.  Two device buffer sets (and a graph bound to each) let
-    # step i+1's upload and step i's read-back run on a copy stream while the
-    # GPU computes; every copy is inside the timed region.
+    res = {"ms": ms_max, "ms_rank": ms, "k2_avg_ms": k2_avg_ms, "k2_graph_ms": k2_step_ms, "clocks": clocks}
+    if e2e:
+        res.update(measure_e2e(w, steps, barrier, graph))
+    del graph
+    k2_bytes_avg, step_bytes = w.bytes_per_step()
+    res["k2_bytes"], res["step_bytes"] = k2_bytes_avg, step_bytes
+    return res
+
+
+def measure_e2e(w: Workload, steps: int, barrier, graph) -> dict:
+    """The step through the public API with host buffers: every step uploads
+    its inputs from pinned host memory and reads its outputs back.  Two device
+    buffer sets (and a graph bound to each) let step i+1's upload and step i's
+    read-back run on a copy stream while the GPU computes; every copy is
+    inside the timed region."""
+    import torch
+
+    from logitfill_b200.packed.attention import DecodeCall
+
+    dev = w.dev
+    stream = torch.cuda.current_stream(dev)
+    q, kn, vn = w.q, w.kn, w.vn
+    result = w.gathered if w.gathered is not None else w.out
     hq, hk, hv = (x.cpu().pin_memory() for x in (q, kn, vn))
-    q2, kn2, vn2, out2 = (torch.empty_like(x) for x in (q, kn, vn, out))
-    calls2 = [DecodeCall(cache, l, q2[l], kn2[l], vn2[l], scaling, out2[l], pps=args.pps) for l in range(L)]
-    graph2 = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph2, capture_error_mode="thread_local"):
-        for c in calls2:
-            c.launch()
-    sets = [(q, kn, vn, out, graph), (q2, kn2, vn2, out2, graph2)]
-    houts = [torch.empty(out.shape, dtype=out.dtype, pin_memory=True) for _ in range(2)]
+    q2, kn2, vn2, out2 = (torch.empty_like(x) for x in (q, kn, vn, w.out))
+    g2 = torch.empty_like(w.gathered) if w.gathered is not None else None
+    calls2 = [DecodeCall(w.cache, l, q2[l], kn2[l], vn2[l], w.scaling, out2[l], pps=w.calls[l].pps)
+              for l in range(w.L)]
+    graph2 = _graph(lambda: w.step(calls2, out2, g2))
+    res2 = g2 if g2 is not None else out2
+    sets = [(q, kn, vn, result, graph), (q2, kn2, vn2, res2, graph2)]
+    houts = [torch.empty(result.shape, dtype=result.dtype, pin_memory=True) for _ in range(2)]
     cs = torch.cuda.Stream(dev)
     uploaded = [torch.cuda.Event() for _ in range(2)]
     computed = [torch.cuda.Event() for _ in range(2)]
@@ -436,14 +546,15 @@ def run_b200(args, cfg) -> None:
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     upload(0)
-    for i in range(args.steps):
+    for i in range(steps):
         b = i % 2
         stream.wait_event(uploaded[b])
         sets[b][4].replay()
         computed[b].record(stream)
-        if i + 1 < args.steps:
+        if i + 1 < steps:
             upload(i + 1)
         with torch.cuda.stream(cs):
             cs.wait_event(computed[b])
@@ -453,53 +564,131 @@ def run_b200(args, cfg) -> None:
     stream.wait_event(read_back)
     e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, dev)
-    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
-    d2h = houts[0].numel() * houts[0].element_size()
-    assert torch.equal(houts[(args.steps - 1) % 2], out.cpu() if (args.steps - 1) % 2 == 0 else out2.cpu())
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / steps, dev)
+    last = (steps - 1) % 2
+    assert torch.equal(houts[last], sets[last][3].cpu())
+    del graph2
+    return {"e2e_ms": e2e_ms, "h2d": sum(x.numel() * x.element_size() for x in (hq, hk, hv)),
+            "d2h": houts[0].numel() * houts[0].element_size()}
 
-    # Algorithmic bytes (reference layout) per step and per K2 launch.
-    k2_bytes = []
-    step_bytes = 0
-    for layer in cache.layers:
-        c = layer.layout.c
-        ww = (c.width[0], c.width[1], c.width[2], c.width[3], c.words[0], c.words[1], c.words[2])
-        kb, tb = algorithmic_bytes(ww, layer.hist_len.tolist(), layer.tail_len.tolist(), NQ, H, D)
-        k2_bytes.append(kb)
-        step_bytes += tb
-    k2_bytes_avg = sum(k2_bytes) / len(k2_bytes)
+
+def block(w: Workload, m: dict, config_id: int, traffic_ok: bool) -> dict:
+    """JSON fields of one measured workload (whole job over all ranks)."""
     peak, peak_kind = measured_peak_hbm()
-    achieved = k2_bytes_avg / (k2_avg_ms * 1e-3) / 1e9
-    step_gbs = step_bytes / (ms * 1e-3) / 1e9
+    cfg, world = w.cfg, w.world
+    seqs = cfg["batch"] * world if w.shard == "weak" else cfg["batch"]
+    achieved = m["k2_bytes"] / (m["k2_avg_ms"] * 1e-3) / 1e9
+    step_gbs = m["step_bytes"] / (m["ms"] * 1e-3) / 1e9
+    out = {
+        "value": seqs / (m["ms"] * 1e-3), "unit": "tok/s", "ms_per_step": m["ms"], "n_gpus": world,
+        "scaling": "weak" if w.shard == "weak" else "strong",
+        "config": workload_config(cfg, world, w.shard),
+        "hbm_gbs": step_gbs * world, "hbm_frac_of_peak_per_gpu": step_gbs / peak,
+        "pages_per_split": w.calls[0].pps,
+        "roofline": {"kernel": "lf_decode_partial (K2)", "bound": "hbm", "achieved": achieved, "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": ncu_traffic(config_id) if traffic_ok else None,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one K2 launch, "
+                                       "same config (committed capture summary)",
+                     "bytes_per_launch": m["k2_bytes"], "avg_launch_ms": m["k2_avg_ms"],
+                     "avg_launch_method": "CUDA graph of the L K2 launches alone (programmatic launches), "
+                                          "event-timed, divided by L",
+                     "k2_share_of_step": m["k2_graph_ms"] / m["ms"]},
+        "gpu_launches_per_step": w.L * 2,
+    }
+    if "e2e_ms" in m:
+        out["e2e"] = {"value": seqs / (m["e2e_ms"] * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": m["h2d"] * world,
+                      "d2h_bytes_per_step": m["d2h"] * world, "ms_per_step": m["e2e_ms"],
+                      "method": "pipelined attention-only loop: step i+1's inputs uploaded and step i's outputs read "
+                                "back on a copy stream while step i computes"}
+    if m.get("clocks") is not None:
+        out["clocks"] = m["clocks"]
+    return out
+
+
+def run_b200(args, cfg) -> None:
+    import gc
+
+    import torch
+    import torch.distributed as dist
+
+    if args.k2 != "auto":
+        os.environ["LF_K2_KERNEL"] = args.k2
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    cpu_rates = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # Host baselines first: their worker pools start (spawn) before this
+        # process's GPU work, and the GPU is idle meanwhile.
+        cores = host_cores()
+        cpu_rates = {kind: cpu_decode_rates(cfg, 10.0, cores, kind)[0] for kind in ("torch", "numpy")}
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    from logitfill_b200.synthetic import mean_key_bits
+
+    w = Workload(cfg, rank, world, args.shard, dev, pps=args.pps, with_k1=True)
+    m = measure(w, args.steps, args.warmup, barrier, clocks_index=local)
+    main = block(w, m, args.config, traffic_ok=args.target_bit is None and args.batch is None and world == 1
+                 and args.shard == "weak" and args.k2 != "simt")
+    k1 = w.k1
+    key_bits = mean_key_bits(w.levels if args.shard != "kv" else [lv.numpy() for lv in w.levels])
+    launches = args.steps * w.L * 2
+    del w
+    gc.collect()
+    torch.cuda.empty_cache()
+
+    extra = {}
+    if not args.no_blocks and args.config == 1 and args.shard == "weak":
+        if world == 1:
+            w2 = Workload(CONFIGS[2], rank, world, "weak", dev)
+            extra["config2"] = block(w2, measure(w2, args.steps, args.warmup, barrier), 2,
+                                     traffic_ok=args.k2 != "simt")
+            del w2
+            gc.collect()
+            torch.cuda.empty_cache()
+        steps4 = max(3, min(args.steps, 10))
+        shards = ["kv"] + (["batch"] if world > 1 else [])
+        for shard in shards:
+            w4 = Workload(CONFIGS[4], rank, world, shard, dev)
+            b4 = block(w4, measure(w4, steps4, args.warmup, barrier, e2e=False), 4, traffic_ok=False)
+            b4["steps"] = steps4
+            extra[f"config4_{shard}"] = b4
+            del w4
+            gc.collect()
+            torch.cuda.empty_cache()
 
     if rank == 0:
-        cpu = None
-        if world == 1 and not args.no_cpu_baseline:
-            cpu_res = cpu_decode_rate(cfg, budget_s=10.0, workers=1)
-            cpu = {"value": cpu_res["value"], "unit": "tok/s", "cores": 1, "kind": "port",
-                   "sample": cpu_res["sample"]}
         line = {
-            "metric": METRIC, "value": world * B / (ms_max * 1e-3), "unit": "tok/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": workload_config(cfg, world),
-            "hbm_gbs": step_gbs * world, "hbm_frac_of_peak_per_gpu": step_gbs / peak,
-            "key_mean_bits": mean_key_bits(levels),
-            "pages_per_split": calls[0].pps,
-            "roofline": {"kernel": "lf_decode_partial (K2)", "bound": "hbm", "achieved": achieved,
-                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                         "traffic": ncu_traffic(args.config) if args.target_bit is None else None,
-                         "traffic_source": f"ncu --set full, profiles/k2_decode_config{args.config}_ncu.md",
-                         "bytes_per_launch": k2_bytes_avg, "avg_launch_ms": k2_avg_ms},
-            "k1": dict(k1, peak=peak, frac=k1["achieved"] / peak),
-            "e2e": {"value": world * B / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-            "cpu_baseline": cpu,
-            "clocks": clocks.summary(),
-            "gpu_launches": args.steps * L * 2,
+            "metric": METRIC, "value": main["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": main["ms_per_step"], "higher_is_better": True,
+            "scaling": main["scaling"], "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": main["config"], "hbm_gbs": main["hbm_gbs"],
+            "hbm_frac_of_peak_per_gpu": main["hbm_frac_of_peak_per_gpu"], "key_mean_bits": key_bits,
+            "pages_per_split": main["pages_per_split"], "k2_kernel": args.k2,
+            "roofline": main["roofline"],
+            "k1": dict(k1, peak=main["roofline"]["peak"], frac=k1["achieved"] / main["roofline"]["peak"]),
+            "e2e": main["e2e"],
+            "cpu_baseline": None,
+            "clocks": main.get("clocks"),
+            "gpu_launches": launches,
         }
+        if cpu_rates is not None:
+            best = max(cpu_rates.values(), key=lambda r: r["value"])
+            line["cpu_baseline"] = {k: best[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            line["cpu_baselines"] = {kind: {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+                                     for kind, r in cpu_rates.items()}
+        line.update(extra)
         print(json.dumps(line), flush=True)
-    del graph, graph2
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -582,8 +771,14 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", type=int, default=1, choices=sorted(CONFIGS))
+    ap.add_argument("--shard", default="weak", choices=["weak", "batch", "kv"],
+                    help="weak: every GPU holds the config's batch; batch / kv: the config is split over the GPUs "
+                         "by sequence / by KV head (kv gathers each layer's output over NCCL)")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--k2", default="auto", choices=["auto", "tc", "simt"],
+                    help="K2 kernel: auto/tc = tensor-core kernel where the geometry allows, simt = CUDA-core kernel")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-blocks", action="store_true", help="only the main line (no config2 / config4 blocks)")
     ap.add_argument("--target-bit", type=float, default=None,
                     help="override the config's Key policy budget (config 2 sweep: 2.25, 2.5, 3.0, 4.0)")
     ap.add_argument("--pps", type=int, default=None,

@@ -13,6 +13,9 @@
 //   sum_t p_t v_t = sum_t (p_t s_t) code_t + (sum_t p_t m_t) 1
 // and the inner loops multiply raw integer codes by precomputed fp32 factors.
 
+#include <cstdlib>
+#include <cstring>
+
 #include "lf_decode_common.cuh"
 
 namespace lf {
@@ -21,6 +24,7 @@ namespace lf {
 bool tc_supported(const lf_layout& L, int gq, int pps);
 int launch_partial_tc(const DecodeParams& p, int resid_dtype, int q_dtype, cudaStream_t stream);
 int occupancy_tc(const lf_layout& L, int gq, int pps);
+bool tc_allowed();
 
 struct DecodeSmem {
   int q, qp, p, red, slot, slot16, region, rows_bytes, total;
@@ -426,7 +430,8 @@ static int launch_merge(const float* workspace, const int32_t* hist_tokens, int 
 extern "C" int lf_decode_occupancy(const lf_layout* layout, int n_q, int pages_per_split) {
   if (layout == nullptr || n_q <= 0 || pages_per_split <= 0 || n_q % layout->kv_heads) return 0;
   const int gq = lf::chunk_heads(n_q / layout->kv_heads, 1);
-  if (lf::tc_supported(*layout, gq, pages_per_split)) return lf::occupancy_tc(*layout, gq, pages_per_split);
+  if (lf::tc_allowed() && lf::tc_supported(*layout, gq, pages_per_split))
+    return lf::occupancy_tc(*layout, gq, pages_per_split);
   const lf::DecodeSmem S = lf::decode_smem(*layout, lf::n_slots_of(*layout));
   if (S.total > 227 * 1024) return 0;
   auto kern = lf::decode_partial_simt<__nv_bfloat16, __nv_bfloat16>;
@@ -547,9 +552,20 @@ static int prepare_decode(const char* who, const lf_layout* layout, const int32_
   return LF_OK;
 }
 
+// Whether the tensor-core kernel may serve the geometries it supports: yes,
+// unless the environment variable LF_K2_KERNEL is "simt" (read once), which
+// sends every call to the CUDA-core kernel for an A/B measurement of the two.
+bool tc_allowed() {
+  static const bool allowed = [] {
+    const char* e = getenv("LF_K2_KERNEL");
+    return !(e != nullptr && strcmp(e, "simt") == 0);
+  }();
+  return allowed;
+}
+
 // K2 on the kernel the geometry selects.
 static int launch_decode(const DecodeParams& p, cudaStream_t s) {
-  if (tc_supported(p.L, p.cg, p.pps)) return launch_partial_tc(p, p.resid_dtype, p.q_dtype, s);
+  if (tc_allowed() && tc_supported(p.L, p.cg, p.pps)) return launch_partial_tc(p, p.resid_dtype, p.q_dtype, s);
   LF_CHECK_SUPPORTED(decode_smem(p.L, p.n_slots).total <= 227 * 1024, "decode shared memory %d B too large",
                      decode_smem(p.L, p.n_slots).total);
   switch (p.resid_dtype) {

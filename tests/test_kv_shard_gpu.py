@@ -1,0 +1,103 @@
+"""KV-head sharding on 2 GPUs: the gathered output equals the 1-GPU output.
+
+Two NCCL ranks (child processes, one GPU each) hold 4 of the 8 KV heads of a
+config-4-shaped layer (40 q / 8 KV heads, GQA 5) with their 20 query heads,
+run K2 + K3 on them and all-gather the head-sharded outputs
+(``logitfill_b200.sharding.gather_heads``).  Rank 0 also decodes the whole
+layer on its GPU; the reassembled output must equal it (the same kernels run
+on the same heads with the same split plan; max-abs 1e-6 allowed for the
+wider tier padding of the full layer).  Skipped on a box with fewer than two
+GPUs.  NVLS is off for the collective (NCCL_NVLS_ENABLE=0).
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _data(dev):
+    from logitfill_b200.synthetic import synthetic_kv, synthetic_levels
+
+    B, H, NQ, D, T = 3, 8, 40, 128, 2048
+    levels = synthetic_levels(1, H, D, 2.5, seed=14)[0]
+    lengths = [T + 5, T - 128 * 3 + 64, 900]
+    k, v = synthetic_kv(B, H, T + 8, D, seed=14, layer=0, device=dev)
+    g = torch.Generator(device=dev).manual_seed(15)
+    q = torch.randn(B, NQ, D, generator=g, device=dev).to(torch.bfloat16)
+    kn = torch.stack([k[b, :, n] for b, n in enumerate(lengths)]).contiguous()
+    vn = torch.stack([v[b, :, n] for b, n in enumerate(lengths)]).contiguous()
+    return levels, lengths, k, v, q, kn, vn, (B, H, NQ, D, T)
+
+
+def _decode(levels, lengths, k, v, q, kn, vn, dims, dev, pps=4):
+    from logitfill_b200.packed import PackedKVCache
+    from logitfill_b200.packed.attention import decode_into
+
+    B, H, NQ, D, T = dims
+    cache = PackedKVCache([levels], B, NQ, H, D, device=dev, capacity=T + 128)
+    cache.prefill(0, k, v, lengths)
+    out = torch.empty(B, NQ, D, dtype=torch.float32, device=dev)
+    decode_into(cache, 0, q, kn, vn, D ** -0.5, out, pps=pps)
+    cache.check_status()
+    return out
+
+
+def _worker(rank: int, world: int, port: int, out) -> None:
+    import datetime
+
+    import torch.distributed as dist
+
+    from logitfill_b200.sharding import assemble_heads, gather_heads, kv_head_range
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        levels, lengths, k, v, q, kn, vn, dims = _data(dev)
+        B, H, NQ, D, T = dims
+        h0, h1, q0, q1 = kv_head_range(H, NQ, world, rank)
+        local = _decode(levels[h0:h1], lengths, k[:, h0:h1].contiguous(), v[:, h0:h1].contiguous(),
+                        q[:, q0:q1].contiguous(), kn[:, h0:h1].contiguous(), vn[:, h0:h1].contiguous(),
+                        (B, h1 - h0, q1 - q0, D, T), dev)
+        gathered = torch.empty((world,) + tuple(local.shape), dtype=local.dtype, device=dev)
+        gather_heads(local, gathered)
+        full_sharded = assemble_heads(gathered)
+        if rank == 0:
+            full = _decode(levels, lengths, k, v, q, kn, vn, dims, dev)
+            diff = float((full_sharded - full).abs().max())
+            out.put((rank, diff, bool(torch.equal(full_sharded, full))))
+        else:
+            out.put((rank, 0.0, True))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_kv_sharded_two_gpus_equals_one_gpu():
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = sorted(out.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    (_, diff, exact), _ = results
+    assert diff <= 1e-6, diff

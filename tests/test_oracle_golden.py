@@ -106,3 +106,26 @@ def test_oracle_pack_roundtrip_property():
             packed = orc.pack_ints(codes, bits)
             assert packed.shape[-1] == (n * bits + 31) // 32
             np.testing.assert_array_equal(orc.unpack_ints(packed, n, bits), codes)
+
+
+def test_torch_port_matches_reference_outputs(small, big):
+    """The torch restatement of reference.py:30-56 (what the CPU baseline
+    times) reproduces the reference's own stored attention outputs."""
+    from oracle import packed_ref_torch as orct
+    from tests.oracle_runner import oracle_layer_for
+
+    for name in ("cuda", "mixed"):
+        case = small_case(small, name)
+        layer = oracle_layer_for(case)
+        got = orct.reference_attention(layer, case["query"], case["key_new"], case["value_new"], case["scaling"])
+        assert np.allclose(got.numpy(), small[f"{name}_attn"], atol=1e-5, rtol=1e-5), name
+    case = cases.config0_like(1024, 37)
+    layer = oracle_layer_for(case)
+    got = orct.reference_attention(layer, case["query"], case["key_new"], case["value_new"], case["scaling"])
+    assert np.allclose(got.numpy(), big["config0_attn"], atol=1e-5, rtol=1e-5)
+    # the dequantized history equals the numpy oracle's bit for bit
+    kt = orct.dequantize_key(layer.hist_len, layer.table, layer.hist_k, layer.k_group_size).numpy()
+    kn, vn = layer.dequantize()
+    vt = orct.dequantize_value(layer.hist_v, layer.hist_len, 128, 2, 128).numpy()
+    assert_bit_equal(kt, kn, "torch deq k")
+    assert_bit_equal(vt, vn, "torch deq v")
