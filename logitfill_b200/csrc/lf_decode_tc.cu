@@ -12,13 +12,13 @@
 //   U_K  Key codes -> u8 in TMEM (A of QK, K-major), masked in place (INT2
 //        slot k of a byte as code * 4^k, INT4 as code * 16^k); the B row of QK
 //        for K position t (tier slot c, code weight w_c): for each q-head j the
-//        fixed point X = rint(q_j[c] scale_c 2^(29-Eq-Es) / w_c), offset by 2^30 and split into
-//        four unsigned limbs (bytes); K positions 128 and up (wide layouts)
+//        fixed point X = rint(q_j[c] scale_c 2^(29-Eq-Es) / w_c), offset by 2^30: its four
+//        bytes are the unsigned limbs, column 4 j + l of the row; K positions 128 and up (wide layouts)
 //        take four lanes each, two q-heads per lane; Es is the page's Key-scale exponent, from
 //        the largest scale the packer stores in the meta row; partial sums of
 //        the Key-min bias sum_c q_j[c] min_c; the token's code sum n_t (the
 //        byte sum of its code words, which is the sum of its A row).
-//   S    score_tj = 2^(Eq+Es-29) (acc0 + 2^8 acc1 + 2^16 acc2 + 2^24 (acc3 - 64 n_t))
+//   S    score_tj = 2^(Eq+Es-29) (acc0 + 2^8 acc1 + 2^16 (acc2 + 2^8 (acc3 - 64 n_t)))
 //        + FP16-tier part + bias_j; page max per q-head; online softmax with
 //        the per-q-head statistics held by lane j of every warp; the B row of
 //        PV for token t: rint(p_tj vscale_t 2^(23-Ev)) in three limbs, Ev the
@@ -139,28 +139,13 @@ __device__ __forceinline__ int kpos_entry(const lf_layout& L, const int32_t* slo
   return ch < 0 ? -1 : (ch | (tier << 16) | (slot << 18));
 }
 
-// Pack the bytes of U[0..7] into MN-major limb rows:
-// c0 = {byte0 of U0..U7, byte1 of U0..U7}, c1 = {byte2 of U0..U7, byte3 of U0..U7}.
-__device__ __forceinline__ void pack_limbs4(const uint32_t (&U)[kGQ], uint4& c0, uint4& c1) {
-  uint32_t b0[2], b1[2], b2[2], b3[2];
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const uint32_t t01 = __byte_perm(U[4 * h + 0], U[4 * h + 1], 0x5140);
-    const uint32_t t23 = __byte_perm(U[4 * h + 2], U[4 * h + 3], 0x5140);
-    const uint32_t s01 = __byte_perm(U[4 * h + 0], U[4 * h + 1], 0x7362);
-    const uint32_t s23 = __byte_perm(U[4 * h + 2], U[4 * h + 3], 0x7362);
-    b0[h] = __byte_perm(t01, t23, 0x5410);
-    b1[h] = __byte_perm(t01, t23, 0x7632);
-    b2[h] = __byte_perm(s01, s23, 0x5410);
-    b3[h] = __byte_perm(s01, s23, 0x7632);
-  }
-  c0 = make_uint4(b0[0], b0[1], b1[0], b1[1]);
-  c1 = make_uint4(b2[0], b2[1], b3[0], b3[1]);
-}
-// Bytes 0..2 of U[0..7] (the PV limbs): c1 = {byte2 of U0..U7, 0, 0}.
-__device__ __forceinline__ void pack_limbs(const uint32_t (&U)[kGQ], uint4& c0, uint4& c1) {
-  pack_limbs4(U, c0, c1);
-  c1.z = c1.w = 0u;
+// B rows of both MMAs order their 32 columns (q-head j, limb l) as n = 4 j + l:
+// a 32-byte row is the eight 32-bit words U[0..7] as they lie in registers
+// (byte l of U[j] is limb l), stored as two 16-byte halves (columns 0-15 and
+// 16-31 of the MN-major core matrices, sbo bytes apart).
+__device__ __forceinline__ void store_b_row(unsigned char* dst, int sbo, const uint32_t (&U)[kGQ]) {
+  *reinterpret_cast<uint4*>(dst) = make_uint4(U[0], U[1], U[2], U[3]);
+  *reinterpret_cast<uint4*>(dst + sbo) = make_uint4(U[4], U[5], U[6], U[7]);
 }
 
 // Warp reduce-scatter of 8 sums: returns the warp total of v[j] for
@@ -228,23 +213,16 @@ __device__ __forceinline__ void qk_b_row(unsigned char* bqk, int sbo, int pp, co
       U[j] = 1u << 30;  // X = 0
     }
   }
-  uint4 c0, c1;
-  pack_limbs4(U, c0, c1);
-  unsigned char* dst = bqk + (pp & 7) * 16 + (pp >> 3) * 128;
-  *reinterpret_cast<uint4*>(dst) = c0;
-  *reinterpret_cast<uint4*>(dst + sbo) = c1;
+  store_b_row(bqk + (pp & 7) * 16 + (pp >> 3) * 128, sbo, U);
 }
 
 // Two q-heads (2 hp, 2 hp + 1) of the B row of QK at K position pp: the
-// same limbs as qk_b_row, stored as one 16-bit pair per limb.
+// same words as qk_b_row, one 8-byte store (columns 8 hp .. 8 hp + 7).
 __device__ __forceinline__ void hi_b_row_pair(unsigned char* bqk, int sbo, int pp, int hp, float2 qv, float sc) {
   const uint32_t ua = static_cast<uint32_t>(__float2int_rn(qv.x * sc) + (1 << 30));
   const uint32_t ub = static_cast<uint32_t>(__float2int_rn(qv.y * sc) + (1 << 30));
-  unsigned char* dst = bqk + (pp & 7) * 16 + (pp >> 3) * 128 + 2 * hp;
-  *reinterpret_cast<uint16_t*>(dst) = static_cast<uint16_t>(__byte_perm(ua, ub, 0x0040));
-  *reinterpret_cast<uint16_t*>(dst + 8) = static_cast<uint16_t>(__byte_perm(ua, ub, 0x0051));
-  *reinterpret_cast<uint16_t*>(dst + sbo) = static_cast<uint16_t>(__byte_perm(ua, ub, 0x0062));
-  *reinterpret_cast<uint16_t*>(dst + sbo + 8) = static_cast<uint16_t>(__byte_perm(ua, ub, 0x0073));
+  unsigned char* dst = bqk + (pp & 7) * 16 + (pp >> 3) * 128 + (hp >= 2 ? sbo : 0) + 8 * (hp & 1);
+  *reinterpret_cast<uint2*>(dst) = make_uint2(ua, ub);
 }
 
 // K position descriptor: meta offsets of the slot's scale and min, and the
@@ -450,7 +428,9 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     }
     for (int i = 0; i < npg; ++i) {
       if (lane == 0) {
-        if (!*abort_s && !mbar_wait_bounded(&bars[kBarKReady], i & 1, kLimit)) *abort_s = 1;
+        if (!mbar_try_wait(&bars[kBarKReady], i & 1) && !*abort_s &&
+            !mbar_wait_bounded(&bars[kBarKReady], i & 1, kLimit))
+          *abort_s = 1;
         tc_fence_after();
         for (uint32_t ks = 0; ks < n_ks; ++ks)  // +512 B per K step = +32 in descriptor units
           mma_u8_ts(tmem + S.tm_qk, tmem + 8 * ks, bqk_desc0 + 32 * ks, kIdescQK, ks > 0 ? 1u : 0u);
@@ -466,7 +446,9 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
             if (i & 1) ++issued1; else ++issued0;
           }
         }
-        if (!*abort_s && !mbar_wait_bounded(&bars[kBarVReady], i & 1, kLimit)) *abort_s = 1;
+        if (!mbar_try_wait(&bars[kBarVReady], i & 1) && !*abort_s &&
+            !mbar_wait_bounded(&bars[kBarVReady], i & 1, kLimit))
+          *abort_s = 1;
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < kP / 32; ++ks)
@@ -494,7 +476,10 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     for (int j = 0; j < GQ; ++j) og[j] = lt[j] = lvt[j] = 0.f;
     float m_l = -INFINITY;  // running max of q-head (lane & 7), log2 units
     const int l8 = lane & 7;
+    // A wait whose phase has completed costs one try_wait; the abort flag is
+    // read only on the slow path.
     auto wait = [&](uint64_t* bar, uint32_t parity) {
+      if (mbar_try_wait(bar, parity)) return;
       if (*abort_s) return;
       if (!mbar_wait_bounded(bar, parity, kLimit)) *abort_s = 1;
     };
@@ -624,7 +609,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       const float vs = half_bits_to_float(row16[w3]);
       const float vm = half_bits_to_float(row16[w3 + 1]);
       mbar_arrive(&bars[kBarFree]);  // the last read of this page's stage
-      const float f = cf * exp2i(esc), f16 = f * 65536.f, f24 = f * 16777216.f;
+      const float f = cf * exp2i(esc), f16 = f * 65536.f;
       const int off64 = 64 * nsum;  // offset 2^30 = 64 * 2^24 per unit of code
       wait(&bars[kBarQK], st);
       tc_fence_after();
@@ -634,10 +619,10 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       float key[GQ];
 #pragma unroll
       for (int j = 0; j < GQ; ++j) {
-        const uint32_t lo = a[j] + (a[8 + j] << 8);
-        const int hi = static_cast<int>(a[24 + j]) - off64;
-        x[j] = fmaf(static_cast<float>(hi), f24,
-                    fmaf(static_cast<float>(a[16 + j]), f16, fmaf(static_cast<float>(lo), f, s16[j])));
+        // acc_l = column 4 j + l; limbs 0-1 and 2-3 joined exactly in 32 bits.
+        const uint32_t lo = a[4 * j] + (a[4 * j + 1] << 8);
+        const int hi = static_cast<int>(a[4 * j + 2]) + ((static_cast<int>(a[4 * j + 3]) - off64) << 8);
+        x[j] = fmaf(static_cast<float>(hi), f16, fmaf(static_cast<float>(lo), f, s16[j]));
         key[j] = warp_max_f32(x[j]);
       }
       const uint32_t vkey = __reduce_max_sync(0xffffffffu, __float_as_uint(vs));
@@ -668,18 +653,12 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
           x[j] = ex2(x[j] + __shfl_sync(0xffffffffu, off, j));  // p_tj
           // Y = rint(p * vs * 2^(23 - Ev)) in [0, 2^23]: the low 24 bits of the
           // fp32 sum 2^23 + Y are Y (2^24 itself has low bits 2^23).
-          U[j] = __float_as_uint(fmaf(x[j], vsc, 8388608.0f));
+          U[j] = __float_as_uint(fmaf(x[j], vsc, 8388608.0f)) & 0x00FFFFFFu;
         } else {
           U[j] = 0u;
         }
       }
-      {
-        uint4 c0, c1;
-        pack_limbs(U, c0, c1);
-        unsigned char* dst = bpv + (tid & 7) * 16 + (tid >> 3) * 128;
-        *reinterpret_cast<uint4*>(dst) = c0;
-        *reinterpret_cast<uint4*>(dst + 2048) = c1;
-      }
+      store_b_row(bpv + (tid & 7) * 16 + (tid >> 3) * 128, 2048, U);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&bars[kBarVReady]);
@@ -710,8 +689,8 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       const float sc = exp2i(ev - 23 - 2 * rk);
 #pragma unroll
       for (int j = 0; j < GQ; ++j) {
-        const uint32_t lo = a[j] + (a[8 + j] << 8);
-        const float v = fmaf(static_cast<float>(a[16 + j]), 65536.f, static_cast<float>(lo));
+        const uint32_t lo = a[4 * j] + (a[4 * j + 1] << 8);
+        const float v = fmaf(static_cast<float>(a[4 * j + 2]), 65536.f, static_cast<float>(lo));
         og[j] = fmaf(v, sc, og[j]);
       }
       // U_V(i+1): the Value tile is free once PV(i) has completed.
