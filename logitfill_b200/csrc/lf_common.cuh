@@ -75,6 +75,18 @@ __device__ __forceinline__ uint32_t asym_code_rcp(float x, float lo, float scale
   return static_cast<uint32_t>(c);
 }
 
+// Code of x as asym_code_rcp computes it (K1 uses this form), for x - lo >= 0 or
+// NaN, which the packer always has (lo is the group's minimum, so x - lo is a
+// non-negative number, +inf, or NaN).  For 0 <= q < 2^22 the float sum
+// RN(q + 1.5 * 2^23) holds round_half_even(q) in the low bits of its
+// significand; a larger, infinite or NaN quotient gives a bit pattern above
+// every code, which the unsigned min turns into qmax: the reference's clamp.
+__device__ __forceinline__ uint32_t pack_code(float x, float lo, float scale, float rcp, uint32_t qmax) {
+  const float q = asym_quotient_rcp(__fsub_rn(x, lo), scale, rcp);
+  const uint32_t r = __float_as_uint(__fadd_rn(q, 12582912.0f)) - 0x4B400000u;
+  return min(r, qmax);
+}
+
 template <typename F>
 __device__ __forceinline__ void dispatch_noop(F) {}
 

@@ -1,14 +1,19 @@
 // K1: page quantize + pack, and the history dequantizer.
 //
-// One CTA per (job, KV head).  The page's Key and Value tiles are staged in
-// shared memory in their own dtype (16-byte streaming loads), the per-channel
-// Key statistics (one min/max per k_group tokens, layout.py:86-99) and the
-// per-token Value statistics (layout.py:122-129) are computed once, every
-// element is replaced in place by its code (uniform work over the CTA), and
-// every output word of the history rows is then assembled from the codes by
-// one thread and written with coalesced stores.  Arithmetic is the reference's, bit for bit:
-// fp32 max/min, IEEE subtract and divide, clamp to [1e-5, 1e5], round half to
-// even, fp16 round-to-nearest-even of the stored scale/min (layout.py:12-18,98-99).
+// One CTA of 256 threads per (job, KV head).  The page's Key and Value tiles
+// are staged in shared memory in their own dtype (16-byte streaming loads,
+// rows padded to an odd number of 32-bit words so a warp reading one column
+// of 32 rows touches 32 banks).  Statistics: each Key channel's max / min over
+// its k_group tokens (layout.py:86-99) and each token's over its v_group Value
+// channels (layout.py:122-129), on packed 16-bit pairs.  Each Key tier slot
+// then gets a record {scale, RN(1/scale), min, channel offset}; codes and
+// words are formed one thread per token row and role (128 threads build the
+// Key tier words and the fp16 words of their rows, 128 the Value code words),
+// written to a staged copy of the page's rows and stored coalesced.
+// Arithmetic is the reference's, bit for bit: fp32 max/min, IEEE subtract and
+// divide, clamp to [1e-5, 1e5], round half to even, fp16 round-to-nearest-even
+// of the stored scale/min (layout.py:12-18,98-99); the per-element division is
+// Markstein's (lf_common.cuh) and the rounding a magic-number add (pack_code).
 
 #include <type_traits>
 
@@ -17,61 +22,191 @@
 namespace lf {
 
 constexpr int kPackThreads = 256;
-constexpr int kPackSkip = -1;  // src_seq of a job that packs nothing
+constexpr int kPackRole = kPackThreads / 2;  // threads per role: Key words / Value words
+constexpr int kPackRows = 128;               // token rows one pass of a role covers
+constexpr int kPackParts = kPackRole / kPackRows;  // threads of a role per token row
+constexpr int kPackSkip = -1;                 // src_seq of a job that packs nothing
 
+// Shared memory of one (job, KV head).  The page's Key and Value tiles are
+// staged in their own dtype with a row stride of `sw` 32-bit words: odd, so
+// the 32 rows a warp reads at one column lie in 32 banks, and at least one
+// word longer than the row, so every row ends in a zero word (`pad_off`,
+// the element a padding slot reads).
 struct PackSmem {
-  // Byte offsets into dynamic shared memory.
-  int xk, xv, ksc, klo, krc, vsc, vlo, vrc, slotmap, wdesc, meta, total;
+  int xk, xv, chan, slotmap, kslot, vstat, h16, out, meta, total;
+  int sw;      // staged row stride, 32-bit words
+  int pad_off; // byte offset of the zero word in a staged row
+  int nslot;   // Key tier slots the row words hold: 16 words0 + 8 words1 + 4 words2
+  int tbase1, tbase2;  // first slot of the INT4 / INT8 tiers
 };
 
-// The page's Key and Value tiles are staged in their own dtype (esz bytes per
-// element): 64 KB for a bf16 128 x 128 page pair, so three CTAs fit on an SM.
+__host__ __device__ inline int round16(int x) { return (x + 15) / 16 * 16; }
+
 __host__ __device__ inline PackSmem pack_smem(const lf_layout& L, int esz) {
-  const int P = L.page_size, D = L.head_dim;
-  const int G = P / L.k_group, NV = D / L.v_group;
+  const int P = L.page_size, D = L.head_dim, G = P / L.k_group, NV = D / L.v_group;
   PackSmem s;
+  const int data_words = (D * esz + 3) / 4;
+  s.sw = data_words + ((data_words & 1) ? 2 : 1);
+  s.pad_off = data_words * 4;
+  s.tbase1 = 16 * L.words[0];
+  s.tbase2 = s.tbase1 + 8 * L.words[1];
+  s.nslot = s.tbase2 + 4 * L.words[2];
   int off = 0;
-  s.xk = off; off += (P * D * esz + 15) / 16 * 16;
-  s.xv = off; off += (P * D * esz + 15) / 16 * 16;
-  s.ksc = off; off += G * D * 4;
-  s.klo = off; off += G * D * 4;
-  s.krc = off; off += G * D * 4;
-  s.vsc = off; off += P * NV * 4;
-  s.vlo = off; off += P * NV * 4;
-  s.vrc = off; off += P * NV * 4;
-  s.slotmap = off; off += 4 * D * 4;
-  s.wdesc = off; off += L.row_words * 4;
-  s.meta = off; off += G * L.meta_halves * 2;
-  s.total = (off + 15) / 16 * 16;
+  s.xk = off; off += round16(P * s.sw * 4);
+  s.xv = off; off += round16(P * s.sw * 4);
+  s.chan = off; off += round16(D * 4);
+  s.slotmap = off; off += round16(4 * D * 4);
+  s.kslot = off; off += G * (s.nslot > 0 ? s.nslot : 1) * 16;
+  s.vstat = off; off += P * NV * 16;
+  s.h16 = off; off += round16((L.width[3] > 0 ? L.width[3] : 1) * 4);
+  s.out = off; off += round16(P * L.row_words * 4);
+  s.meta = off; off += round16(G * L.meta_halves * 2);
+  s.total = off;
   return s;
 }
 
-// Row-word descriptors: kind (0-2 Key tier, 3 Value codes, 4 fp16 halves) | index << 3.
-enum { kWordValue = 3, kWordHalf = 4 };
+// Per-slot record of a Key tier slot (group g, tier slot): scale, RN(1/scale),
+// min, and the byte offset of the slot's channel in a staged row.  A padding
+// slot (past the head's channel count, or past the tier width) reads the zero
+// word of the row with scale 1, min 0: its code is 0 (layout.py:95-97).
+struct __align__(16) SlotRec {
+  float scale, rcp, lo;
+  int off;
+};
 
 template <typename T>
-__global__ void __launch_bounds__(kPackThreads)
+__device__ __forceinline__ float load_elem(const unsigned char* p) {
+  return Scalar<T>::load(reinterpret_cast<const T*>(p));
+}
+
+// Running max / min of two adjacent 16-bit elements (exact: the max of two
+// bf16 or fp16 values is the max of their fp32 values).
+template <typename T> struct Pair;
+template <> struct Pair<__nv_bfloat16> {
+  using V = __nv_bfloat162;
+  static __device__ __forceinline__ V lowest() { return __nv_bfloat162(__ushort_as_bfloat16(0xFF80), __ushort_as_bfloat16(0xFF80)); }
+  static __device__ __forceinline__ V highest() { return __nv_bfloat162(__ushort_as_bfloat16(0x7F80), __ushort_as_bfloat16(0x7F80)); }
+  static __device__ __forceinline__ V max(V a, V b) { return __hmax2(a, b); }
+  static __device__ __forceinline__ V min(V a, V b) { return __hmin2(a, b); }
+  static __device__ __forceinline__ float lo(V a) { return __low2float(a); }
+  static __device__ __forceinline__ float hi(V a) { return __high2float(a); }
+};
+template <> struct Pair<__half> {
+  using V = __half2;
+  static __device__ __forceinline__ V lowest() { return __half2(__ushort_as_half(0xFC00), __ushort_as_half(0xFC00)); }
+  static __device__ __forceinline__ V highest() { return __half2(__ushort_as_half(0x7C00), __ushort_as_half(0x7C00)); }
+  static __device__ __forceinline__ V max(V a, V b) { return __hmax2(a, b); }
+  static __device__ __forceinline__ V min(V a, V b) { return __hmin2(a, b); }
+  static __device__ __forceinline__ float lo(V a) { return __low2float(a); }
+  static __device__ __forceinline__ float hi(V a) { return __high2float(a); }
+};
+
+// Key statistics of channels c0 .. c0+n-1 (n = 2 for a 16-bit pair, 1 otherwise)
+// of group g over tokens [g kg, (g+1) kg), split over `split` consecutive
+// lanes of full warps: part h takes the stretch of span = kg / split tokens
+// starting at g kg + h span, beginning rot = (32 / split) h tokens in and
+// wrapping around (span >= 32 when split > 1), so the parts of one warp read
+// different banks.  Every lane of the split returns the combined max / min.
+template <typename T>
+__device__ __forceinline__ void key_stats(const unsigned char* xk, int sw, int g, int kg, int c0, int split, int h,
+                                          float (&hi)[2], float (&lo)[2]) {
+  const int span = kg / split, rot = (32 / split) * h;
+  const int t0 = g * kg + h * span;
+  const int stride = sw * 4;
+  if constexpr (sizeof(T) == 2) {
+    using PR = Pair<T>;
+    typename PR::V mx = PR::lowest(), mn = PR::highest();
+    const unsigned char* col = xk + c0 * 2 + t0 * stride;
+    auto scan = [&](int j0, int j1) {
+#pragma unroll 8
+      for (int j = j0; j < j1; ++j) {
+        const typename PR::V v = *reinterpret_cast<const typename PR::V*>(col + j * stride);
+        mx = PR::max(mx, v);
+        mn = PR::min(mn, v);
+      }
+    };
+    scan(rot, span);
+    scan(0, rot);
+    hi[0] = PR::lo(mx); hi[1] = PR::hi(mx);
+    lo[0] = PR::lo(mn); lo[1] = PR::hi(mn);
+  } else {
+    float mx = -INFINITY, mn = INFINITY;
+    const unsigned char* col = xk + c0 * 4 + t0 * stride;
+    auto scan = [&](int j0, int j1) {
+#pragma unroll 8
+      for (int j = j0; j < j1; ++j) {
+        const float v = *reinterpret_cast<const float*>(col + j * stride);
+        mx = fmaxf(mx, v);
+        mn = fminf(mn, v);
+      }
+    };
+    scan(rot, span);
+    scan(0, rot);
+    hi[0] = hi[1] = mx;
+    lo[0] = lo[1] = mn;
+  }
+  for (int o = 1; o < split; o <<= 1) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      hi[e] = fmaxf(hi[e], __shfl_xor_sync(0xffffffffu, hi[e], o));
+      lo[e] = fminf(lo[e], __shfl_xor_sync(0xffffffffu, lo[e], o));
+    }
+  }
+}
+
+// Two adjacent 16-bit elements (one 32-bit shared load) as fp32.
+template <typename T>
+__device__ __forceinline__ float2 load_pair(const unsigned char* p);
+template <>
+__device__ __forceinline__ float2 load_pair<__nv_bfloat16>(const unsigned char* p) {
+  const uint32_t u = *reinterpret_cast<const uint32_t*>(p);
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
+}
+template <>
+__device__ __forceinline__ float2 load_pair<__half>(const unsigned char* p) {
+  return __half22float2(*reinterpret_cast<const __half2*>(p));
+}
+template <>
+__device__ __forceinline__ float2 load_pair<float>(const unsigned char* p) {
+  return make_float2(*reinterpret_cast<const float*>(p), *reinterpret_cast<const float*>(p + 4));
+}
+
+// A Key word of token row `row`: BITS-bit codes of the slots rec[0 .. 32 / BITS).
+template <typename T, int BITS>
+__device__ __forceinline__ uint32_t key_word(const unsigned char* row, const SlotRec* rec) {
+  constexpr int kPer = 32 / BITS;
+  constexpr uint32_t kQmax = (1u << BITS) - 1u;
+  uint32_t word = 0;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const SlotRec r = rec[k];
+    // the fields are disjoint: adding is OR-ing (one shift-add)
+    word += pack_code(load_elem<T>(row + r.off), r.lo, r.scale, r.rcp, kQmax) << (k * BITS);
+  }
+  return word;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kPackThreads, 2)
 pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict__ src_v,
                   int64_t s_seq, int64_t s_head, int64_t s_tok, const int32_t* __restrict__ jobs,
                   int dst_batch, const int32_t* __restrict__ chan_code, int32_t* __restrict__ rows,
                   uint16_t* __restrict__ kmeta, int32_t* status) {
   extern __shared__ __align__(16) unsigned char smem[];
   const PackSmem S = pack_smem(L, sizeof(T));
-  T* xk = reinterpret_cast<T*>(smem + S.xk);
-  T* xv = reinterpret_cast<T*>(smem + S.xv);
-  float* ksc = reinterpret_cast<float*>(smem + S.ksc);
-  float* klo = reinterpret_cast<float*>(smem + S.klo);
-  float* krc = reinterpret_cast<float*>(smem + S.krc);  // RN(1 / scale)
-  float* vsc = reinterpret_cast<float*>(smem + S.vsc);
-  float* vlo = reinterpret_cast<float*>(smem + S.vlo);
-  float* vrc = reinterpret_cast<float*>(smem + S.vrc);
-  int* slotmap = reinterpret_cast<int*>(smem + S.slotmap);
-  int* wdesc = reinterpret_cast<int*>(smem + S.wdesc);
+  unsigned char* xk = smem + S.xk;
+  unsigned char* xv = smem + S.xv;
+  int* chan = reinterpret_cast<int*>(smem + S.chan);        // chan_code of the head
+  int* slotmap = reinterpret_cast<int*>(smem + S.slotmap);  // [tier][slot] -> channel or -1
+  SlotRec* kslot = reinterpret_cast<SlotRec*>(smem + S.kslot);
+  float4* vstat = reinterpret_cast<float4*>(smem + S.vstat);  // [token][v group]: scale, rcp, min
+  int* h16 = reinterpret_cast<int*>(smem + S.h16);          // FP16 slot -> byte offset in a row
+  uint32_t* out = reinterpret_cast<uint32_t*>(smem + S.out);
   uint16_t* meta = reinterpret_cast<uint16_t*>(smem + S.meta);
 
   const int job = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   const int P = L.page_size, D = L.head_dim, R = L.row_words, M = L.meta_halves;
-  const int G = P / L.k_group, NV = D / L.v_group, H = L.kv_heads;
+  const int kg = L.k_group, G = P / kg, NV = D / L.v_group, H = L.kv_heads;
   const int src_seq = jobs[4 * job + 0], tok0 = jobs[4 * job + 1];
   const int dst_seq = jobs[4 * job + 2], dst_page = jobs[4 * job + 3];
   if (src_seq == kPackSkip) return;  // a job slot left empty by the device-side commit
@@ -81,46 +216,80 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
     if (tid == 0 && status != nullptr) atomicExch(status, LF_ERR_OUT_OF_RANGE);
     return;
   }
+  const int sw = S.sw, sw4 = S.sw * 4;
 
-  // 1. Stage the page in its dtype: 16-byte streaming loads (all of a
-  // thread's loads issued before its stores) when the rows are aligned.
+  // 1. Stage the page in its dtype, rows sw words apart: 16-byte streaming
+  // loads (all of a thread's loads issued before its stores) when the rows
+  // are aligned, 32-bit shared stores; the zero word after every row.
   const T* ksrc = src_k + src_seq * s_seq + h * s_head + static_cast<int64_t>(tok0) * s_tok;
   const T* vsrc = src_v + src_seq * s_seq + h * s_head + static_cast<int64_t>(tok0) * s_tok;
   constexpr int kVec = 16 / sizeof(T);
   const bool vec = (reinterpret_cast<uintptr_t>(ksrc) % 16 == 0) && (reinterpret_cast<uintptr_t>(vsrc) % 16 == 0) &&
                    (s_tok * static_cast<int64_t>(sizeof(T))) % 16 == 0 && D % kVec == 0;
-  if (vec) {
-    const int vpr = D / kVec, nvec = P * vpr;
-    const bool pow2 = (vpr & (vpr - 1)) == 0;
-    const int vshift = 31 - __clz(vpr);
+  if (vec && kPackThreads % (D / kVec) == 0) {
+    // Each thread keeps one 16-byte column of the rows: no division per vector.
+    const int vpr = D / kVec, rstep = kPackThreads / vpr;
+    const int tr = tid / vpr, ec = (tid - tr * vpr) * kVec;
     constexpr int kBatch = 8;
-    for (int base = tid; base < nvec; base += kPackThreads * kBatch) {
+    for (int t0 = tr; t0 < P; t0 += rstep * kBatch) {
       uint4 a[kBatch], c[kBatch];
 #pragma unroll
       for (int r = 0; r < kBatch; ++r) {
-        const int i = base + r * kPackThreads;
-        if (i < nvec) {
-          const int t = pow2 ? i >> vshift : i / vpr, e = (i - t * vpr) * kVec;
-          a[r] = __ldcs(reinterpret_cast<const uint4*>(ksrc + t * s_tok + e));
-          c[r] = __ldcs(reinterpret_cast<const uint4*>(vsrc + t * s_tok + e));
+        const int t = t0 + r * rstep;
+        if (t < P) {
+          a[r] = __ldcs(reinterpret_cast<const uint4*>(ksrc + t * s_tok + ec));
+          c[r] = __ldcs(reinterpret_cast<const uint4*>(vsrc + t * s_tok + ec));
         }
       }
 #pragma unroll
       for (int r = 0; r < kBatch; ++r) {
-        const int i = base + r * kPackThreads;
-        if (i < nvec) {
-          reinterpret_cast<uint4*>(xk)[i] = a[r];
-          reinterpret_cast<uint4*>(xv)[i] = c[r];
+        const int t = t0 + r * rstep;
+        if (t < P) {
+          const int wo = t * sw + ec * static_cast<int>(sizeof(T)) / 4;
+          uint32_t* dk = reinterpret_cast<uint32_t*>(xk) + wo;
+          uint32_t* dv = reinterpret_cast<uint32_t*>(xv) + wo;
+          dk[0] = a[r].x; dk[1] = a[r].y; dk[2] = a[r].z; dk[3] = a[r].w;
+          dv[0] = c[r].x; dv[1] = c[r].y; dv[2] = c[r].z; dv[3] = c[r].w;
         }
       }
+    }
+  } else if (vec) {
+    const int vpr = D / kVec, nvec = P * vpr;
+    for (int i = tid; i < nvec; i += kPackThreads) {
+      const int t = i / vpr, e = (i - t * vpr) * kVec;
+      const uint4 a = __ldcs(reinterpret_cast<const uint4*>(ksrc + t * s_tok + e));
+      const uint4 c = __ldcs(reinterpret_cast<const uint4*>(vsrc + t * s_tok + e));
+      const int wo = t * sw + e * static_cast<int>(sizeof(T)) / 4;
+      uint32_t* dk = reinterpret_cast<uint32_t*>(xk) + wo;
+      uint32_t* dv = reinterpret_cast<uint32_t*>(xv) + wo;
+      dk[0] = a.x; dk[1] = a.y; dk[2] = a.z; dk[3] = a.w;
+      dv[0] = c.x; dv[1] = c.y; dv[2] = c.z; dv[3] = c.w;
     }
   } else {
     for (int i = tid; i < P * D; i += kPackThreads) {
       const int t = i / D, e = i - t * D;
-      xk[i] = ksrc[t * s_tok + e];
-      xv[i] = vsrc[t * s_tok + e];
+      reinterpret_cast<T*>(xk + t * sw4)[e] = ksrc[t * s_tok + e];
+      reinterpret_cast<T*>(xv + t * sw4)[e] = vsrc[t * s_tok + e];
     }
   }
+  {
+    const int data_words = S.pad_off / 4;
+    for (int t = tid; t < P; t += kPackThreads) {
+      for (int w = data_words; w < sw; ++w) {
+        reinterpret_cast<uint32_t*>(xk)[t * sw + w] = 0u;
+        reinterpret_cast<uint32_t*>(xv)[t * sw + w] = 0u;
+      }
+    }
+    // A 16-bit tile whose row has an odd number of elements: the half word
+    // after the last element is zeroed with the rest of the row's tail.
+    if (sizeof(T) == 2 && (D & 1)) {
+      for (int t = tid; t < P; t += kPackThreads) {
+        reinterpret_cast<uint16_t*>(xk + t * sw4)[D] = 0;
+        reinterpret_cast<uint16_t*>(xv + t * sw4)[D] = 0;
+      }
+    }
+  }
+  for (int c = tid; c < D; c += kPackThreads) chan[c] = chan_code[h * D + c];
   for (int i = tid; i < 4 * D; i += kPackThreads) slotmap[i] = -1;
   for (int i = tid; i < G * M; i += kPackThreads) {
     const int e = i % M;
@@ -130,166 +299,236 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
       is_scale |= (e >= L.scale_off[b] && e < L.scale_off[b] + L.width[b]);
     meta[i] = is_scale ? 0x3C00 : 0;
   }
-  for (int w = tid; w < R; w += kPackThreads) {
-    int d;
-    if (w < L.vcode_off) {
-      int b = 0;
-      while (b < 2 && w >= L.code_off[b] + L.words[b]) ++b;
-      d = b | ((w - L.code_off[b]) << 3);
-    } else if (w < L.half_off) {
-      d = kWordValue | ((w - L.vcode_off) << 3);
-    } else {
-      d = kWordHalf | ((w - L.half_off) << 3);
-    }
-    wdesc[w] = d;
-  }
+  for (int i = tid; i < G * S.nslot; i += kPackThreads) kslot[i] = SlotRec{1.0f, 1.0f, 0.0f, S.pad_off};
   __syncthreads();
   for (int c = tid; c < D; c += kPackThreads) {
-    const int code = chan_code[h * D + c];
+    const int code = chan[c];
     const int tier = code >> 16, local = code & 0xFFFF;
     if (tier >= 0 && tier < 4 && local < L.width[tier]) slotmap[tier * D + local] = c;
   }
-  // 2. Statistics, one work item per thread: (max, min) of a Key channel over
-  // k_group tokens (layout.py:86-99), or of a token over v_group Value
-  // channels (layout.py:122-129).
-  for (int i = tid; i < G * D + P * NV; i += kPackThreads) {
-    if (i < G * D) {
-      const int g = i / D, c = i - g * D;
-      const int code = chan_code[h * D + c];
-      const int tier = code >> 16, local = code & 0xFFFF;
-      if (tier < 0 || tier > 2) continue;
+  for (int i = tid; i < L.width[3]; i += kPackThreads) h16[i] = S.pad_off;
+  __syncthreads();
+  for (int i = tid; i < L.width[3]; i += kPackThreads) {
+    const int c = slotmap[3 * D + i];
+    if (c >= 0) h16[i] = c * static_cast<int>(sizeof(T));
+  }
+
+  // 2. Statistics.  Threads 0..127: Key channel (pairs of 16-bit elements)
+  // over each group of k_group tokens (layout.py:86-99); threads 128..255:
+  // Value token over each group of v_group channels (layout.py:122-129).
+  if (tid < kPackRole) {
+    const int cw = sizeof(T) == 2 ? 2 : 1;  // channels per task
+    const int tasks = G * ((D + cw - 1) / cw);
+    // Split a channel's tokens over 2 or 4 lanes when the tasks leave threads
+    // idle; a split runs on whole warps (its lanes shuffle) and leaves every
+    // part at least 32 tokens.
+    int split = 1;
+    for (int s2 = 4; s2 > 1; s2 >>= 1) {
+      if (tasks * s2 <= kPackRole && (tasks * s2) % 32 == 0 && kg % s2 == 0 && kg / s2 >= 32) {
+        split = s2;
+        break;
+      }
+    }
+    for (int i = tid; i < tasks * split; i += kPackRole) {
+      const int task = i / split, part = i - task * split;
+      const int g = task / ((D + cw - 1) / cw), c0 = (task - g * ((D + cw - 1) / cw)) * cw;
+      float hi[2], lo[2];
+      key_stats<T>(xk, sw, g, kg, c0, split, part, hi, lo);
+      if (part == 0) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          if (e >= cw || c0 + e >= D) continue;
+          const int code = chan[c0 + e];
+          const int tier = code >> 16, local = code & 0xFFFF;
+          if (tier < 0 || tier > 2 || local >= L.width[tier]) continue;
+          const float sc = asym_scale(hi[e], lo[e], 2 << tier);
+          const int base = tier == 0 ? 0 : tier == 1 ? S.tbase1 : S.tbase2;
+          kslot[g * S.nslot + base + local] = SlotRec{sc, __frcp_rn(sc), lo[e], (c0 + e) * static_cast<int>(sizeof(T))};
+          meta[g * M + L.scale_off[tier] + local] = float_to_half_bits(sc);
+          meta[g * M + L.min_off[tier] + local] = float_to_half_bits(lo[e]);
+        }
+      }
+    }
+  } else {
+    // Two lanes per (token, v group) when every lane has a partner: each
+    // scans half of the group's channel pairs, the second half starting 16
+    // words in, so the two lanes of a token read different banks.
+    const int vg = L.v_group, tasks = P * NV;
+    const bool pairs = sizeof(T) == 2 && vg % 4 == 0;
+    const int split = (pairs && tasks * 2 <= kPackRole && (tasks * 2) % 32 == 0) ? 2 : 1;
+    for (int i = tid - kPackRole; i < tasks * split; i += kPackRole) {
+      const int j = i / split, h = i - j * split;
+      const int t = j / NV, g = j - t * NV;
+      const unsigned char* row = xv + t * sw4 + g * vg * static_cast<int>(sizeof(T));
       float hi = -INFINITY, lo = INFINITY;
-      const T* col = xk + g * L.k_group * D + c;
+      if constexpr (sizeof(T) == 2) {
+        if (pairs) {
+          using PR = Pair<T>;
+          typename PR::V mx = PR::lowest(), mn = PR::highest();
+          const int nw = vg / 2 / split;                 // 32-bit words of this lane's part
+          const unsigned char* base = row + h * nw * 4;
+          const int rot = (h == 1 && nw >= 32) ? 16 : 0;
+          auto scan = [&](int k0, int k1) {
 #pragma unroll 8
-      for (int t = 0; t < L.k_group; ++t) {
-        const float x = Scalar<T>::load(col + t * D);
-        hi = fmaxf(hi, x);
-        lo = fminf(lo, x);
-      }
-      const float sc = asym_scale(hi, lo, 2 << tier);
-      ksc[i] = sc;
-      klo[i] = lo;
-      krc[i] = __frcp_rn(sc);
-      if (local < L.width[tier]) {
-        meta[g * M + L.scale_off[tier] + local] = float_to_half_bits(sc);
-        meta[g * M + L.min_off[tier] + local] = float_to_half_bits(lo);
-      }
-    } else {
-      const int j = i - G * D, t = j / NV, g = j - t * NV;
-      float hi = -INFINITY, lo = INFINITY;
-      const T* row = xv + t * D + g * L.v_group;
-      // Neighbouring threads take neighbouring tokens (rows D elements apart,
-      // the same bank): each starts at its own column so a warp's reads spread
-      // over the banks.  Max and min do not depend on the order.
-      int cc = t % L.v_group;
+            for (int k = k0; k < k1; ++k) {
+              const typename PR::V v = *reinterpret_cast<const typename PR::V*>(base + k * 4);
+              mx = PR::max(mx, v);
+              mn = PR::min(mn, v);
+            }
+          };
+          scan(rot, nw);
+          scan(0, rot);
+          hi = fmaxf(PR::lo(mx), PR::hi(mx));
+          lo = fminf(PR::lo(mn), PR::hi(mn));
+        } else {
+          for (int c = 0; c < vg; ++c) {
+            const float x = load_elem<T>(row + c * 2);
+            hi = fmaxf(hi, x);
+            lo = fminf(lo, x);
+          }
+        }
+      } else {
 #pragma unroll 8
-      for (int c = 0; c < L.v_group; ++c) {
-        const float x = Scalar<T>::load(row + cc);
-        hi = fmaxf(hi, x);
-        lo = fminf(lo, x);
-        if (++cc == L.v_group) cc = 0;
+        for (int c = 0; c < vg; ++c) {
+          const float x = load_elem<T>(row + c * 4);
+          hi = fmaxf(hi, x);
+          lo = fminf(lo, x);
+        }
       }
-      const float sc = asym_scale(hi, lo, L.bit_v);
-      vsc[j] = sc;
-      vlo[j] = lo;
-      vrc[j] = __frcp_rn(sc);
+      if (split == 2) {
+        hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, 1));
+        lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, 1));
+      }
+      if (h == 0) {
+        const float sc = asym_scale(hi, lo, L.bit_v);
+        vstat[j] = make_float4(sc, __frcp_rn(sc), lo, 0.f);
+      }
     }
   }
   __syncthreads();
   // Largest stored Key scale of each group over the head's INT2/INT4/INT8
-  // channels (positive fp16 values order as their bit patterns).
-  for (int g = tid; g < G; g += kPackThreads) {
-    uint16_t mx = 0;
+  // channels (positive fp16 values order as their bit patterns): one warp per
+  // group, lanes over the slots, then a warp maximum.
+  for (int g = tid >> 5; g < G; g += kPackThreads / 32) {
+    uint32_t mx = 0;
     for (int b = 0; b < 3; ++b)
-      for (int slot = 0; slot < L.width[b]; ++slot)
-        if (slotmap[b * D + slot] >= 0) mx = max(mx, meta[g * M + L.scale_off[b] + slot]);
-    meta[g * M + L.kmax_off] = mx;
+      for (int slot = tid & 31; slot < L.width[b]; slot += 32)
+        if (slotmap[b * D + slot] >= 0) mx = max(mx, static_cast<uint32_t>(meta[g * M + L.scale_off[b] + slot]));
+    mx = __reduce_max_sync(0xffffffffu, mx);
+    if ((tid & 31) == 0) meta[g * M + L.kmax_off] = static_cast<uint16_t>(mx);
   }
 
-  // 3. Codes, in place: every staged Key element of an INT2/INT4/INT8
-  // channel and every Value element is replaced by its code (same thread
-  // reads and writes an element; uniform work across the CTA).
-  using U = typename std::conditional<sizeof(T) == 4, uint32_t, uint16_t>::type;
-  U* ck = reinterpret_cast<U*>(xk);
-  U* cv = reinterpret_cast<U*>(xv);
-  // Channel-major split of the threads: thread (c, r0) takes channel c of
-  // tokens r0, r0 + rows_step, ... (no division per element).
-  const int rows_step = D <= kPackThreads ? kPackThreads / D : 1;
-  const int r0 = D <= kPackThreads ? tid / D : 0;
-  for (int c = D <= kPackThreads ? tid % D : tid; c < D && r0 < rows_step; c += kPackThreads) {
-    const int tier = __ldg(chan_code + h * D + c) >> 16;
-    const bool keyed = tier >= 0 && tier <= 2;
-    const int bits = keyed ? 2 << tier : 2;
-    const int vg = c / L.v_group;
-    int g = 0, g_end = L.k_group;  // Key group of token t, stepped as t advances
-    float g_lo = klo[c], g_sc = ksc[c], g_rc = krc[c];  // that group's statistics, in registers
-    for (int t = r0; t < P; t += rows_step) {
-      if (t >= g_end) {
-        while (t >= g_end) {
-          ++g;
-          g_end += L.k_group;
+  // 3. Codes and words, kPackParts threads per token row and role (every
+  // kPackParts-th word each): the first kPackRole threads the Key tier words
+  // and (last part of a row) the fp16 words (FP16 Key tier, Value scale and
+  // min), the others the Value code words.  Lanes are consecutive rows, so a
+  // warp reads one column of 32 rows (32 banks).  Each word goes to the row
+  // staged in `out`.
+  if (tid < kPackRole) {
+    const int part = tid / kPackRows;
+    const int nk0 = L.words[0], nk1 = L.words[1], nk = nk0 + nk1 + L.words[2];
+    const int half_part = kPackParts - 1;  // the part that also writes the fp16 words
+    for (int t = tid % kPackRows; t < P; t += kPackRows) {
+      const unsigned char* row = xk + t * sw4;
+      const SlotRec* rec = kslot + (t / kg) * S.nslot;
+      uint32_t* orow = out + t * R;
+      for (int w = part; w < nk; w += kPackParts) {
+        if (w < nk0) {
+          orow[L.code_off[0] + w] = key_word<T, 2>(row, rec + 16 * w);
+        } else if (w < nk0 + nk1) {
+          orow[L.code_off[1] + w - nk0] = key_word<T, 4>(row, rec + S.tbase1 + 8 * (w - nk0));
+        } else {
+          orow[L.code_off[2] + w - nk0 - nk1] = key_word<T, 8>(row, rec + S.tbase2 + 4 * (w - nk0 - nk1));
         }
-        g_lo = klo[g * D + c];
-        g_sc = ksc[g * D + c];
-        g_rc = krc[g * D + c];
       }
-      const int e = t * D + c;
-      if (keyed) ck[e] = static_cast<U>(asym_code_rcp(Scalar<T>::load(xk + e), g_lo, g_sc, g_rc, bits));
-      const int vi = t * NV + vg;
-      cv[e] = static_cast<U>(asym_code_rcp(Scalar<T>::load(xv + e), vlo[vi], vsc[vi], vrc[vi], L.bit_v));
+      if (part != half_part) continue;
+      const int w3 = L.width[3];
+      for (int w = L.half_off; w < R; ++w) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int hx = 2 * (w - L.half_off) + e;
+          uint32_t hv = 0;
+          if (hx < w3) {
+            hv = float_to_half_bits(load_elem<T>(row + h16[hx]));  // layout.py:110; padding reads 0
+          } else if (hx < w3 + NV) {
+            hv = float_to_half_bits(vstat[t * NV + hx - w3].x);
+          } else if (hx < w3 + 2 * NV) {
+            hv = float_to_half_bits(vstat[t * NV + hx - w3 - NV].z);
+          }
+          word |= hv << (16 * e);
+        }
+        orow[w] = word;
+      }
+    }
+  } else if (D % 16 == 0 && L.v_group % 16 == 0) {
+    // Value words, 16 channels each inside one v_group: the token's group
+    // statistics change at word boundaries only; elements read in pairs.
+    const int part = (tid - kPackRole) / kPackRows;
+    const int wpg = L.v_group / 16;  // words per Value group
+    for (int t = tid % kPackRows; t < P; t += kPackRows) {
+      const unsigned char* row = xv + t * sw4;
+      uint32_t* orow = out + t * R + L.vcode_off;
+      int gi = 0, wg = part;  // group of word w and w's position in it
+      while (wg >= wpg) {
+        wg -= wpg;
+        ++gi;
+      }
+      for (int w = part; w < L.vcode_words; w += kPackParts) {
+        const float4 st = vstat[t * NV + gi];
+        const unsigned char* src = row + 16 * w * static_cast<int>(sizeof(T));
+        uint32_t word = 0;
+#pragma unroll
+        for (int k = 0; k < 16; k += 2) {
+          const float2 x = load_pair<T>(src + k * static_cast<int>(sizeof(T)));
+          word += pack_code(x.x, st.z, st.x, st.y, 3u) << (2 * k);
+          word += pack_code(x.y, st.z, st.x, st.y, 3u) << (2 * k + 2);
+        }
+        orow[w] = word;
+        wg += kPackParts;
+        while (wg >= wpg) {
+          wg -= wpg;
+          ++gi;
+        }
+      }
+    }
+  } else {
+    const int vg = L.v_group;
+    for (int t = tid - kPackRole; t < P; t += kPackRole) {
+      const unsigned char* row = xv + t * sw4;
+      uint32_t* orow = out + t * R + L.vcode_off;
+      int g = 0, g_end = vg;
+      float4 st = vstat[t * NV];
+      for (int w = 0; w < L.vcode_words; ++w) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const int d = 16 * w + k;
+          if (d < D) {
+            if (d >= g_end) {
+              ++g;
+              g_end += vg;
+              st = vstat[t * NV + g];
+            }
+            word |= pack_code(load_elem<T>(row + d * static_cast<int>(sizeof(T))), st.z, st.x, st.y, 3u) << (2 * k);
+          }
+        }
+        orow[w] = word;
+      }
     }
   }
   __syncthreads();
-  // 4. Assemble every word of the page's rows from the codes (consecutive
-  // threads write consecutive words of a token row).
-  int32_t* out_rows = rows + ((static_cast<int64_t>(dst_seq) * H + h) * L.row_cap +
-                              static_cast<int64_t>(dst_page) * P) * R;
-  const int warp = tid >> 5, lane = tid & 31;
-  for (int t = warp; t < P; t += kPackThreads / 32)  // a warp per token row, lanes over its words
-  for (int w = lane; w < R; w += 32) {
-    const int i = t * R + w;
-    const int desc = wdesc[w], kind = desc & 7, wi = desc >> 3;
-    uint32_t word = 0;
-    if (kind < kWordValue) {
-      const int bits = 2 << kind, per = 32 / bits;
-      const U* cr = ck + t * D;
-      const int* sm = slotmap + kind * D + wi * per;
-      const int nslot = min(per, L.width[kind] - wi * per);
-      for (int k = 0; k < nslot; ++k) {
-        const int c = sm[k];
-        if (c >= 0) word |= static_cast<uint32_t>(cr[c]) << (k * bits);  // padding slot: code 0 (layout.py:95-97)
-      }
-    } else if (kind == kWordValue) {
-      const int per = 32 / L.bit_v, d0 = wi * per, nd = min(per, D - d0);
-      const U* cr = cv + t * D + d0;
-      if (sizeof(U) == 2 && L.bit_v == 2 && nd == 16 && D % 8 == 0) {  // 16-byte aligned rows
-        // 16 two-bit codes held as u16: two 16-byte reads, two codes per u32.
-        const uint4 a = *reinterpret_cast<const uint4*>(cr);
-        const uint4 b = *reinterpret_cast<const uint4*>(cr + 8);
-        const uint32_t u[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-        for (int k = 0; k < 8; ++k) word |= ((u[k] & 3u) | ((u[k] >> 14) & 0xCu)) << (4 * k);
-      } else {
-        for (int k = 0; k < nd; ++k) word |= static_cast<uint32_t>(cr[k]) << (k * L.bit_v);
-      }
-    } else {
-      for (int e = 0; e < 2; ++e) {
-        const int hx = 2 * wi + e;
-        uint32_t hv = 0;
-        if (hx < L.width[3]) {
-          const int c = slotmap[3 * D + hx];
-          if (c >= 0) hv = float_to_half_bits(Scalar<T>::load(xk + t * D + c));  // layout.py:110
-        } else if (hx < L.width[3] + NV) {
-          hv = float_to_half_bits(vsc[t * NV + (hx - L.width[3])]);
-        } else if (hx < L.width[3] + 2 * NV) {
-          hv = float_to_half_bits(vlo[t * NV + (hx - L.width[3] - NV)]);
-        }
-        word |= hv << (16 * e);
-      }
-    }
-    out_rows[i] = static_cast<int32_t>(word);
+
+  // 4. The page's rows (contiguous in the history) and meta rows, coalesced.
+  const int64_t row0 = (static_cast<int64_t>(dst_seq) * H + h) * L.row_cap + static_cast<int64_t>(dst_page) * P;
+  int32_t* out_rows = rows + row0 * R;
+  const int nw = P * R;
+  if ((reinterpret_cast<uintptr_t>(out_rows) % 16) == 0 && nw % 4 == 0) {
+    for (int i = tid; i < nw / 4; i += kPackThreads)
+      reinterpret_cast<uint4*>(out_rows)[i] = reinterpret_cast<const uint4*>(out)[i];
+  } else {
+    for (int i = tid; i < nw; i += kPackThreads) out_rows[i] = static_cast<int32_t>(out[i]);
   }
-  __syncthreads();  // the group maxima
   uint16_t* out_meta = kmeta + ((static_cast<int64_t>(dst_seq) * H + h) * L.group_cap +
                                 static_cast<int64_t>(dst_page) * G) * M;
   for (int i = tid; i < G * M; i += kPackThreads) out_meta[i] = meta[i];

@@ -33,7 +33,7 @@ extern "C" int lf_selftest_wait(int32_t* status, int64_t limit_ns, int arrive, l
 // Self-test of K1's per-element division: for each (x, lo, scale) triple the
 // quotient (x - lo) / scale and the code exactly as pack_pages_kernel forms
 // them (IEEE subtract, Markstein division with rcp = RN(1 / scale), round
-// half to even, clamp to [0, 2^bits - 1]).
+// half to even by the magic-number add, clamp to [0, 2^bits - 1]).
 namespace lf {
 
 __global__ void selftest_divide_kernel(const float* __restrict__ x, const float* __restrict__ lo,
@@ -43,7 +43,7 @@ __global__ void selftest_divide_kernel(const float* __restrict__ x, const float*
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const float s = scale[i], rcp = __frcp_rn(s);
     quot[i] = asym_quotient_rcp(__fsub_rn(x[i], lo[i]), s, rcp);
-    code[i] = asym_code_rcp(x[i], lo[i], s, rcp, bits);
+    code[i] = pack_code(x[i], lo[i], s, rcp, (1u << bits) - 1u);
   }
 }
 
