@@ -39,7 +39,7 @@ from typing import Optional
 from torch import nn
 
 from logitfill_b200.packed.cache import LogitFillCache, PackedKVManager
-from logitfill_b200.policy import PrecisionPolicy
+from logitfill_b200.policy import KeyPolicy, check_model_fit, policy_tables, read_policy
 
 _CACHE_KEYS = ("past_key_value", "past_key_values")
 
@@ -185,7 +185,7 @@ class DeepSeekQwenKVAdapter:
         self.graph_step = False  # set by GraphDecoder around its captured decode step
         self.captured: dict = {"Q": {}, "K": {}, "V": {}}
         self.k_overrides: Optional[dict] = None
-        self.policy: Optional[PrecisionPolicy] = None
+        self.policy: Optional[KeyPolicy] = None
         self._levels: list = [None] * self.n_layers
         self._originals: list = []
         self._attached = False
@@ -242,14 +242,20 @@ class DeepSeekQwenKVAdapter:
             layer.self_attn.k_levels = level
         self._packed = None
 
-    def load_policy(self, directory) -> PrecisionPolicy:
-        policy = PrecisionPolicy.load(directory)
-        policy.validate_model(self.model)
-        if int(policy.metadata.get("bit_v", self.bit_v)) != self.bit_v:
-            raise ValueError(f"policy bit_v={policy.metadata.get('bit_v')} but adapter bit_v={self.bit_v}")
+    def load_policy(self, directory) -> KeyPolicy:
+        """Read a policy directory (deepseek_qwen.py:111-121): check it fits
+        the model and the adapter's Value bits, install its Key tier maps and
+        build their device tier tables (shared with every cache that uses
+        them)."""
+        policy = read_policy(directory)
+        check_model_fit(policy, self.model.config)
+        bit_v = int(policy.metadata.get("bit_v", self.bit_v))
+        if bit_v != self.bit_v:
+            raise ValueError(f"the policy was calibrated with Value at {bit_v} bits, the adapter stores {self.bit_v}")
         self.policy = policy
         if self._attached:
             self.set_k_levels(policy.levels)
+            policy_tables(policy, next(self.model.parameters()).device)
         return policy
 
     # -- packed store (deepseek_qwen.py:123-146) -----------------------------

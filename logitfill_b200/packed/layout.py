@@ -1,8 +1,9 @@
 """Packed layout: tier tables, the B200 history layout and reference views.
 
 Mirrors ``src/logitfill/packed/layout.py`` of the reference.  The channel
-tables (:func:`tier_tables`) are built on the host exactly as the reference
-builds them (layout.py:49-68).  Storage differs: instead of per-tier tensors
+tables (:func:`tier_tables`, layout.py:49-68) are built once per level map
+and device, with vectorised torch, by :class:`logitfill_b200.policy.TierTables`
+and shared by every layer and cache that uses the map.  Storage differs: instead of per-tier tensors
 concatenated on every flush (cache.py:64-81), one layer keeps two
 preallocated buffers per batch,
 
@@ -25,6 +26,7 @@ import numpy as np
 import torch
 
 from logitfill_b200 import _lib
+from logitfill_b200.policy import TierTables
 
 TIER_BITS = ((0, 2), (1, 4), (2, 8))
 
@@ -32,31 +34,16 @@ TIER_BITS = ((0, 2), (1, 4), (2, 8))
 def tier_tables(levels: torch.Tensor) -> dict:
     """layout.py:49-68: per tier ``index`` (channels ascending, padded to the
     tier ``width``), ``count`` per head, ``local`` position of each channel in
-    its tier (-1 elsewhere); ``tier`` = the levels as int32."""
+    its tier (-1 elsewhere); ``tier`` = the levels as int32.  Built by the
+    shared :class:`~logitfill_b200.policy.TierTables` on the levels' device."""
     lv = torch.as_tensor(levels)
-    heads, dim = lv.shape
-    host = lv.detach().to("cpu", torch.int64).numpy()
-    if host.size and (host.min() < 0 or host.max() > 3):
-        raise ValueError("levels must be in {0, 1, 2, 3}")
-    tables = {}
-    for code in (0, 1, 2, 3):
-        rows = [np.nonzero(host[h] == code)[0] for h in range(heads)]
-        width = max((len(r) for r in rows), default=0)
-        index = np.zeros((heads, width), np.int32)
-        count = np.zeros(heads, np.int32)
-        local = np.full((heads, dim), -1, np.int32)
-        for h, row in enumerate(rows):
-            count[h] = len(row)
-            index[h, : len(row)] = row
-            local[h, row] = np.arange(len(row), dtype=np.int32)
-        tables[code] = {"index": torch.from_numpy(index).to(lv.device),
-                        "count": torch.from_numpy(count).to(lv.device),
-                        "local": torch.from_numpy(local).to(lv.device), "width": width}
-    return {"tiers": tables, "tier": lv.to(torch.int32)}
+    tt = TierTables.get(lv.detach().cpu(), lv.device)
+    return {"tiers": {t: dict(tt.table[t]) for t in range(4)}, "tier": tt.table["tier"]}
 
 
 class LayerLayout:
-    """History layout of one layer plus its device channel tables."""
+    """History layout of one layer plus its device channel tables (shared,
+    per level map and device, through :class:`~logitfill_b200.policy.TierTables`)."""
 
     def __init__(self, levels, *, head_dim: int, page_size: int, k_group_size: int,
                  v_group_size: int, bit_v: int, row_cap: int, device):
@@ -64,35 +51,22 @@ class LayerLayout:
         lv = torch.as_tensor(levels, dtype=torch.int64)
         if lv.dim() != 2 or lv.shape[1] != head_dim:
             raise ValueError(f"levels must be [n_kv, {head_dim}], got {tuple(lv.shape)}")
-        built = tier_tables(lv.cpu())
-        self.levels = lv.cpu()
+        tables = TierTables.get(lv.cpu(), self.device)
+        self.tables = tables
+        self.levels = tables.levels
         self.kv_heads = int(lv.shape[0])
         self.head_dim = int(head_dim)
         self.page_size = int(page_size)
         self.k_group_size = int(k_group_size)
         self.v_group_size = int(v_group_size)
         self.bit_v = int(bit_v)
-        counts = np.stack([built["tiers"][c]["count"].numpy() for c in range(4)]).astype(np.int32)
-        self._counts = np.ascontiguousarray(counts)
+        self._counts = tables.counts
         self.c = _lib.LfLayout()
         self.set_capacity(row_cap)
-        # Device channel tables.
-        H, D = self.kv_heads, self.head_dim
-        chan_code = np.zeros((H, D), np.int32)
-        slot_chan = np.full((4, H, D), -1, np.int32)
-        for code in range(4):
-            t = built["tiers"][code]
-            for h in range(H):
-                n = int(t["count"][h])
-                idx = t["index"][h, :n].numpy()
-                slot_chan[code, h, :n] = idx
-                chan_code[h, idx] = (code << 16) | np.arange(n)
-        self.chan_code = torch.from_numpy(chan_code).to(self.device)
-        self.slot_chan = torch.from_numpy(slot_chan).to(self.device)
-        # Host copy of the reference-shaped tables (layout.py:49-68 + cache.py:22-24).
-        self.table = {code: {k: (v.to(self.device) if torch.is_tensor(v) else v)
-                             for k, v in built["tiers"][code].items()} for code in range(4)}
-        self.table["tier"] = built["tier"].to(self.device)
+        self.chan_code = tables.chan_code
+        self.slot_chan = tables.slot_chan
+        # Reference-shaped tables (layout.py:49-68 + cache.py:22-24).
+        self.table = tables.table
 
     def set_capacity(self, row_cap: int) -> None:
         if row_cap % self.page_size:

@@ -10,13 +10,18 @@ the same comparisons through the CUDA kernels.
 """
 from __future__ import annotations
 
+from pathlib import Path
+
 import numpy as np
 import pytest
 import torch
 
+from oracle import packed_ref as orc
+
 from logitfill_b200.adapter import DeepSeekQwenKVAdapter
 from logitfill_b200.packed.cache import LogitFillCache
-from logitfill_b200.policy import PrecisionPolicy
+from logitfill_b200.policy import (KeyPolicy, TierTables, check_model_fit, key_budget_report, read_policy,
+                                   write_policy)
 from logitfill_b200.synthetic import synthetic_levels
 from tests.qwen_cases import OracleManager, adapter_logits, fake_quant_logits, stock_logits, tiny_qwen2
 
@@ -78,24 +83,52 @@ def test_policy_round_trip_and_checks(tmp_path):
     model = tiny_qwen2(layers=2, n_q=4, n_kv=2, head_dim=128, vocab=64)
     levels = synthetic_levels(2, 2, 128, 2.5, seed=3)
     meta = {"n_layers": 2, "n_kv": 2, "head_dim": 128, "target_bit": 2.5, "bit_v": 2}
-    PrecisionPolicy(levels, meta, {"d2": np.ones(levels.shape)}).save(tmp_path / "p")
-    pol = PrecisionPolicy.load(tmp_path / "p")
+    write_policy(tmp_path / "p", KeyPolicy(levels, meta, {"d2": np.ones(levels.shape)}))
+    pol = read_policy(tmp_path / "p")
     assert np.array_equal(pol.levels, levels) and pol.metadata == meta and set(pol.curves) == {"d2"}
     a = DeepSeekQwenKVAdapter(model).attach()
     a.load_policy(tmp_path / "p")
     assert np.array_equal(np.asarray(model.model.layers[1].self_attn.k_levels), levels[1])
     with pytest.raises(ValueError):                   # over the per-head Key budget
-        PrecisionPolicy(np.full((2, 2, 128), 2), meta)
+        KeyPolicy(np.full((2, 2, 128), 2), meta)
+    KeyPolicy(np.full((2, 2, 128), 2), dict(meta, enforce_budget=False))  # budget check switched off
     with pytest.raises(ValueError):                   # metadata disagrees with the map
-        PrecisionPolicy(levels, dict(meta, n_kv=3))
+        KeyPolicy(levels, dict(meta, n_kv=3))
     with pytest.raises(ValueError):
-        PrecisionPolicy(np.full((2, 2, 128), 4), {})
+        KeyPolicy(np.full((2, 2, 128), 4), {})
+    with pytest.raises(ValueError):
+        KeyPolicy(levels, meta, {"d4": np.ones((2, 2))})  # extra array of another shape
     other = tiny_qwen2(layers=1, n_q=4, n_kv=2, head_dim=128, vocab=64)
     with pytest.raises(ValueError):
-        pol.validate_model(other)
-    PrecisionPolicy(levels, dict(meta, bit_v=3, enforce_budget=False)).save(tmp_path / "q")
+        check_model_fit(pol, other.config)
+    write_policy(tmp_path / "q", KeyPolicy(levels, dict(meta, bit_v=3, enforce_budget=False)))
     with pytest.raises(ValueError):
         a.load_policy(tmp_path / "q")
+
+
+def test_reference_written_policy_loads_and_tables_match_oracle():
+    """tests/golden/policy_ref was written by the reference's own
+    build_policy(...).save(...); it loads, its budget check passes, and the
+    vectorised tier tables (built once per map and device) equal the
+    reference-restated tables of layout.py:49-68."""
+    pol = read_policy(Path(__file__).resolve().parent / "golden" / "policy_ref")
+    assert pol.levels.shape == (2, 2, 128) and pol.metadata["model_id"] == "tiny-qwen2-test"
+    assert set(pol.curves) == {"d2"}
+    report = key_budget_report(pol.levels, pol.metadata["target_bit"], pol.metadata["bit_v"])
+    assert report["max_extra_bits"] <= report["allowed_extra_bits"] == pol.metadata["extra_budget_per_head"]
+    for i in range(2):
+        tt = TierTables.get(pol.levels[i], "cpu")
+        assert TierTables.get(torch.as_tensor(pol.levels[i]), "cpu") is tt
+        ref = orc.tier_tables(pol.levels[i])
+        for t in range(4):
+            assert tt.table[t]["width"] == ref[t]["width"]
+            for key in ("index", "count", "local"):
+                assert np.array_equal(tt.table[t][key].numpy(), ref[t][key]), (i, t, key)
+        assert np.array_equal(tt.counts, np.stack([ref[t]["count"] for t in range(4)]))
+        chan = tt.chan_code.numpy()
+        for c in range(128):
+            tier = int(pol.levels[i][0, c])
+            assert chan[0, c] == (tier << 16) | int(ref[tier]["local"][0, c])
 
 
 def test_cache_handle_under_installed_transformers():

@@ -136,3 +136,27 @@ def test_head_chunks():
 
     assert [chunk_heads(7, 1), chunk_heads(7, 2), chunk_heads(7, 16), chunk_heads(16, 1)] == [7, 7, 8, 8]
     assert [chunk_heads(5, 3), chunk_heads(1, 11), chunk_heads(1, 1), chunk_heads(3, 4)] == [5, 1, 1, 6]
+
+
+def test_device_tables_are_int32_and_match_the_loop_construction():
+    """The kernels read chan_code [H][D] and slot_chan [4][H][D] as int32:
+    the vectorised TierTables give exactly the per-head construction
+    (channel list of each tier in ascending order), in int32."""
+    from logitfill_b200.policy import TierTables
+
+    for seed, (H, D) in enumerate([(4, 128), (2, 64), (3, 8)]):
+        levels = np.random.default_rng(seed).integers(0, 4, size=(H, D))
+        tt = TierTables(levels, "cpu")
+        assert tt.chan_code.dtype == torch.int32 and tt.slot_chan.dtype == torch.int32
+        assert tt.counts.dtype == np.int32
+        ref = orc.tier_tables(levels)
+        chan_code = np.zeros((H, D), np.int32)
+        slot_chan = np.full((4, H, D), -1, np.int32)
+        for t in range(4):
+            for h in range(H):
+                n = int(ref[t]["count"][h])
+                idx = ref[t]["index"][h, :n]
+                slot_chan[t, h, :n] = idx
+                chan_code[h, idx] = (t << 16) | np.arange(n)
+        assert np.array_equal(tt.chan_code.numpy(), chan_code)
+        assert np.array_equal(tt.slot_chan.numpy(), slot_chan)
