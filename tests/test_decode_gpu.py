@@ -90,6 +90,7 @@ def test_gqa5_ragged_batch():
     for pps in (1, 3, 16):
         out = torch.empty(B, NQ, D, dtype=torch.float32, device="cuda")
         decode_into(cache, 0, q, kn, vn, D ** -0.5, out, pps=pps)
+        cache.check_status()  # no device-side wait ran out
         for b in range(B):
             ref = orc.OracleLayer(levels, 128, 128, 128, 2)
             ref.append(k[b, :, :lengths[b]].float().cpu().numpy(), v[b, :, :lengths[b]].float().cpu().numpy())
@@ -115,6 +116,7 @@ def test_config1_geometry_sampled(target_bit):
     kn = torch.stack([k[b, :, T + t] for b, t in enumerate(tails)])
     vn = torch.stack([v[b, :, T + t] for b, t in enumerate(tails)])
     out = packed_attention_batched(cache, 0, q, kn, vn, D ** -0.5, out_dtype=torch.float32)
+    cache.check_status()
     for b in (0, 3):
         ref = orc.OracleLayer(levels, 128, 128, 128, 2)
         n = T + tails[b]
@@ -142,6 +144,7 @@ def test_long_context_split_merge_property():
         out = torch.empty(B, NQ, D, dtype=torch.float32, device="cuda")
         decode_into(cache, 0, q, kn, vn, D ** -0.5, out, pps=pps)
         outs.append(out)
+    cache.check_status()
     # fp32 accumulation order differs between split sizes (one split sums up
     # to 32k tokens serially); the results agree far inside the 2e-3 bound.
     for o in outs[1:]:
