@@ -237,7 +237,6 @@ __device__ __forceinline__ void load_vec_to_float_rt(const void* src, int dtype,
 // accumulates channel d in acc; the chunk's probability sum is added to lt of
 // thread 0 only.  When load_q is set the query group is fetched here, after
 // the row loads are issued, so the two global-memory latencies overlap.
-template <int kPasses = 1>
 static __device__ __forceinline__ void residual_chunk(const DecodeParams& p, int b, int h, int vc, int chunk,
                                                       float* q_s, bool load_q, unsigned char* region,
                                                       float (&m)[kGQ], float (&acc)[kGQ], float (&lt)[kGQ]) {
@@ -265,18 +264,14 @@ static __device__ __forceinline__ void residual_chunk(const DecodeParams& p, int
   const char* nv = p.v_new != nullptr
                        ? static_cast<const char*>(p.v_new) + (b * p.new_seq_stride + h * p.new_head_stride) * RS_
                        : nullptr;
-  // 1. Rows -> fp32 in shared memory; every thread issues all its loads
-  // (of one pass, kPasses passes) first.
+  // 1. Rows -> fp32 in shared memory; every thread issues all its loads first.
   const int vec_per_row = D / 8;
   const int nvec = kResChunk * vec_per_row;  // <= 512
-  constexpr int kAllVec = kResChunk * 128 / 8 / kDecThreads;  // 4
-  constexpr int kMaxVec = kAllVec / kPasses;
-#pragma unroll
-  for (int pass = 0; pass < kPasses; ++pass) {
+  constexpr int kMaxVec = kResChunk * 128 / 8 / kDecThreads;  // 4
   float kv[kMaxVec][8], vv[kMaxVec][8];
 #pragma unroll
   for (int r = 0; r < kMaxVec; ++r) {
-    const int i = tid + (pass * kMaxVec + r) * kDecThreads;
+    const int i = tid + r * kDecThreads;
     const int t = i / vec_per_row, c = i - t * vec_per_row;
     const int tok = t0 + t;
     if (i < nvec && t < ntok) {
@@ -289,17 +284,16 @@ static __device__ __forceinline__ void residual_chunk(const DecodeParams& p, int
       for (int e = 0; e < 8; ++e) kv[r][e] = vv[r][e] = 0.f;
     }
   }
-  if (load_q && pass == 0) load_query_group_rt(p, b, h, vc, q_s);
+  if (load_q) load_query_group_rt(p, b, h, vc, q_s);
 #pragma unroll
   for (int r = 0; r < kMaxVec; ++r) {
-    const int i = tid + (pass * kMaxVec + r) * kDecThreads;
+    const int i = tid + r * kDecThreads;
     if (i >= nvec) break;
     const int t = i / vec_per_row, c = i - t * vec_per_row;
 #pragma unroll
     for (int e = 0; e < 8; ++e) k_s[t * (D + 1) + c * 8 + e] = kv[r][e];
     *reinterpret_cast<float4*>(v_s + t * D + c * 8) = make_float4(vv[r][0], vv[r][1], vv[r][2], vv[r][3]);
     *reinterpret_cast<float4*>(v_s + t * D + c * 8 + 4) = make_float4(vv[r][4], vv[r][5], vv[r][6], vv[r][7]);
-  }
   }
   named_sync(1, kDecThreads);
   // 2. Partial scores: lane = token, warp = quarter of the head dim; four

@@ -39,8 +39,6 @@
 // barriers, so nothing deadlocks), drains its own copies and MMAs, frees its
 // TMEM and returns.
 #include <algorithm>
-#include <cstdlib>
-#include <cstring>
 
 #include "lf_decode_common.cuh"
 #include "lf_tcgen05.cuh"
@@ -717,609 +715,6 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
   }
 }
 
-
-// ---------------------------------------------------------------------------
-// Warp-specialised form of the same decode (one page in flight per group):
-//   warps 0-3  producer: U_K(i) (Key codes -> TMEM A of QK, the B rows of QK,
-//              the Key-min bias partials), then U_V(i) (Value codes -> the
-//              A tile of PV);
-//   warps 4-7  softmax: S(i) (QK readback, FP16 tier, page max, online
-//              softmax, the B rows of PV), then C(i-1) (PV readback of the
-//              previous page, scaled by this page's rescale factor);
-//   warp 8     control: bulk copies and the MMAs.
-// The producer works on page i+1 while the softmax warps work on page i.
-// Every operand is single-buffered and guarded by a full / free barrier pair;
-// each wait is on a barrier whose producer cannot run two phases ahead of the
-// waiter (the producer's next arrival needs an event that follows the wait).
-namespace ws {
-
-constexpr int kWarps = 9;
-constexpr int kThreads = 32 * kWarps;
-constexpr int kCtl = 8;              // control warp
-constexpr int kGroup = 128;          // threads of the producer / softmax group
-enum {
-  bFull0, bFull1,    // stage loaded (transaction count)
-  bFree0, bFree1,    // stage read by both groups
-  bKReady,           // A and B of QK(i) written, bias partials stored
-  bVAReady0, bVAReady1,  // A of PV(i) written, pages with parity 0 / 1
-  bVReady,           // B of PV(i) written
-  bQKFree,           // QK accumulator read
-  bPVFree,           // PV accumulator read
-  bQK,               // QK completion (tcgen05.commit)
-  bPV0, bPV1,        // PV completion of pages with parity 0 / 1 (tcgen05.commit)
-  bBias0, bBias1,    // bias partials of pages with parity 0 / 1
-  kNBars
-};
-
-// Barrier region: the barriers, then the TMEM address, abort flag and query exponent.
-constexpr int kBarBytes = 8 * 20;
-static_assert(8 * kNBars + 12 <= kBarBytes, "barrier region");
-
-struct WsSmem {
-  int bars, red, redb, nsum, q16, qhi, posoff, stage0, bqk, bpv, apv, qs, total;
-  int kpad, a_cols, tm_qk, tm_pv, tm_cols, bqk_sbo, rows_bytes, meta_bytes, stage_bytes;
-};
-
-__host__ __device__ inline WsSmem ws_smem(const lf_layout& L) {
-  WsSmem s;
-  const int ns = n_slots_of(L);
-  s.kpad = ns == 0 ? 32 : (ns + 31) / 32 * 32;
-  s.a_cols = s.kpad / 4;
-  s.tm_qk = (s.a_cols + 31) / 32 * 32;
-  s.tm_pv = s.tm_qk + 32;
-  int need = s.tm_pv + 32, cols = 32;
-  while (cols < need) cols *= 2;
-  s.tm_cols = cols;
-  s.bqk_sbo = s.kpad * 16;
-  s.rows_bytes = kP * L.row_words * 4;
-  s.meta_bytes = L.meta_halves * 2;
-  s.stage_bytes = (s.rows_bytes + s.meta_bytes + 15) / 16 * 16;
-  int off = 0;
-  s.bars = off; off += kBarBytes;               // barriers, TMEM address, abort flag, query exponent
-  s.red = off; off += 2 * 4 * 12 * 4;           // page maxima [stage][softmax warp][12]; end-of-item sums
-  s.redb = off; off += 2 * 4 * kGQ * 4;         // bias partials [page parity][producer warp][8]
-  s.nsum = off; off += 2 * kP * 4;              // code byte sums [page parity][token]
-  s.q16 = off; off += ((L.width[3] > 0 ? L.width[3] : 1) * kGQ * 4 + 15) / 16 * 16;
-  const int hi = s.kpad > kDecThreads + 32 ? s.kpad - kDecThreads - 32 : 0;
-  s.qhi = off; off += hi * kGQ * 4;
-  s.posoff = off; off += hi * 4;
-  off = (off + 127) / 128 * 128;
-  s.stage0 = off; off += kStages * s.stage_bytes;
-  s.bqk = off; off += s.kpad * 32;
-  s.bpv = off; off += kP * 32;
-  s.apv = off; off += 2 * kP * kD;              // Value tile of PV, one per page parity
-  const int resid_end = s.stage0 + resid_smem(kD).total;
-  s.qs = (s.apv + 2 * kP * kD - kGQ * kD * 4);
-  if (s.qs < resid_end) s.qs = (resid_end + 15) / 16 * 16;
-  if (s.qs + kGQ * kD * 4 > off) off = s.qs + kGQ * kD * 4;
-  s.total = (off + 127) / 128 * 128;
-  return s;
-}
-
-template <int GQ>
-__global__ void __launch_bounds__(kThreads, 3) decode_partial_ws(DecodeParams p) {
-  extern __shared__ __align__(1024) unsigned char smem[];
-  const lf_layout& L = p.L;
-  const WsSmem S = ws_smem(L);
-  const int s = blockIdx.y, vc = blockIdx.z, tid = threadIdx.x;
-  const int h = blockIdx.x % p.L.kv_heads, b = blockIdx.x / p.L.kv_heads;
-  const int lane = tid & 31, warp = tid >> 5;
-  const int H = L.kv_heads, R = L.row_words, M = L.meta_halves;
-  grid_dep_wait();
-  grid_dep_trigger();
-  const int pages = p.hist_tokens[b] / kP;
-  const int n_page_splits = (pages + p.pps - 1) / p.pps;
-  if (s >= n_page_splits + residual_splits(kP, p.q_len)) return;
-
-  float* q_s = reinterpret_cast<float*>(smem + S.qs);
-  if (s >= n_page_splits) {  // residual splits: tail rows + new token, fp32 (producer warps)
-    if (warp >= 4) return;
-    float m[kGQ], o[kGQ], lt[kGQ];
-#pragma unroll
-    for (int j = 0; j < kGQ; ++j) {
-      m[j] = -INFINITY;
-      o[j] = lt[j] = 0.f;
-    }
-    residual_chunk<2>(p, b, h, vc, s - n_page_splits, q_s, true, smem + S.stage0, m, o, lt);
-    write_partial_resid(p, item_index(p, b, h, vc, s), o, m, lt);
-    return;
-  }
-
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S.bars);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S.bars + 8 * kNBars);
-  volatile int* abort_s = reinterpret_cast<volatile int*>(smem + S.bars + 8 * kNBars + 4);
-  int* eq_s = reinterpret_cast<int*>(smem + S.bars + 8 * kNBars + 8);
-  uint32_t* red_m = reinterpret_cast<uint32_t*>(smem + S.red);
-  float* red_b = reinterpret_cast<float*>(smem + S.redb);
-  int* nsum_s = reinterpret_cast<int*>(smem + S.nsum);
-  float* q16_s = reinterpret_cast<float*>(smem + S.q16);
-  float* qhi_s = reinterpret_cast<float*>(smem + S.qhi);
-  int* posoff_s = reinterpret_cast<int*>(smem + S.posoff);
-  unsigned char* stage0 = smem + S.stage0;
-  unsigned char* bqk = smem + S.bqk;
-  unsigned char* bpv = smem + S.bpv;
-  unsigned char* apv = smem + S.apv;
-
-  const int pg0 = s * p.pps;
-  const int npg = min(pages, pg0 + p.pps) - pg0;
-  const int64_t head_row = (static_cast<int64_t>(b) * H + h) * L.row_cap;
-  const int64_t head_meta = (static_cast<int64_t>(b) * H + h) * L.group_cap;
-  const float c2 = p.scaling * kLog2e;
-  const int kmax_off = L.kmax_off;
-  const int n_hi = S.kpad > kDecThreads ? (S.kpad - kDecThreads) / 32 : 0;
-  const uint64_t kLimit = kWaitLimitNs;
-
-  auto issue_page = [&](int pg) {
-    unsigned char* dst = stage0 + (pg & 1) * S.stage_bytes;
-    uint64_t* full = &bars[bFull0 + (pg & 1)];
-    mbar_arrive_expect_tx(full, static_cast<uint32_t>(S.rows_bytes + S.meta_bytes));
-    bulk_g2s(dst, p.rows + (head_row + static_cast<int64_t>(pg0 + pg) * kP) * R, S.rows_bytes, full);
-    bulk_g2s(dst + S.rows_bytes, p.kmeta + (head_meta + pg0 + pg) * M, S.meta_bytes, full);
-  };
-  // A wait whose phase has completed costs one try_wait; the abort flag is
-  // read only on the slow path.  After an abort every wait returns at once.
-  auto wait = [&](int bar, uint32_t parity) {
-    if (mbar_try_wait(&bars[bar], parity)) return;
-    if (*abort_s) return;
-    if (!mbar_wait_bounded(&bars[bar], parity, kLimit)) *abort_s = 1;
-  };
-
-  if (tid == kCtl * 32) {
-    mbar_init(&bars[bFull0], 1);
-    mbar_init(&bars[bFull1], 1);
-    mbar_init(&bars[bFree0], 2 * kGroup);
-    mbar_init(&bars[bFree1], 2 * kGroup);
-    mbar_init(&bars[bKReady], kGroup);
-    mbar_init(&bars[bVAReady0], kGroup);
-    mbar_init(&bars[bVAReady1], kGroup);
-    mbar_init(&bars[bVReady], kGroup);
-    mbar_init(&bars[bQKFree], kGroup);
-    mbar_init(&bars[bPVFree], kGroup);
-    mbar_init(&bars[bQK], 1);
-    mbar_init(&bars[bPV0], 1);
-    mbar_init(&bars[bPV1], 1);
-    mbar_init(&bars[bBias0], kGroup);
-    mbar_init(&bars[bBias1], kGroup);
-    *abort_s = 0;
-    fence_mbar_init();
-    fence_proxy_async_smem();
-    issue_page(0);
-    if (npg > 1) issue_page(1);
-  }
-  if (warp == kCtl) {
-    tmem_alloc(tmem_slot, S.tm_cols);
-    tmem_relinquish();
-  }
-
-  // Producer-thread state (K position tid; positions 128.. as in the fused kernel).
-  float qq[kGQ];
-  int po = -1;
-  const int hp = tid & 3;
-  float2 qv_hi = make_float2(0.f, 0.f);
-  int po_hi = -1;
-  if (tid < kGroup) {
-    const int e = tid < S.kpad ? kpos_entry(L, p.slot_chan, h, tid) : -1;
-    const int e_hi = kDecThreads < S.kpad ? kpos_entry(L, p.slot_chan, h, kDecThreads + (tid >> 2)) : -1;
-    const int e2 = kDecThreads + 32 + tid < S.kpad ? kpos_entry(L, p.slot_chan, h, kDecThreads + 32 + tid) : -1;
-    const int n16 = L.width[3] * kGQ;
-    const int ch16 = tid < n16 ? p.slot_chan[(3 * H + h) * kD + tid / kGQ] : -1;
-    float qc[kGQ];
-    {
-      const int v0 = vc * GQ;
-      const int jh0 = v0 / p.q_len, ii0 = v0 - jh0 * p.q_len;
-      const int64_t qb = b * p.q_seq_stride + static_cast<int64_t>(h) * p.gq * p.q_head_stride + tid;
-      auto gather = [&](auto load) {
-        int jh = jh0, ii = ii0;
-#pragma unroll
-        for (int j = 0; j < kGQ; ++j) {
-          qc[j] = j < GQ ? load(qb + jh * p.q_head_stride + ii * p.q_tok_stride) : 0.f;
-          if (++ii == p.q_len) {
-            ii = 0;
-            ++jh;
-          }
-        }
-      };
-      if (p.q_dtype == LF_F32) {
-        const float* qp = static_cast<const float*>(p.q);
-        gather([&](int64_t o) { return qp[o]; });
-      } else if (p.q_dtype == LF_F16) {
-        const __half* qp = static_cast<const __half*>(p.q);
-        gather([&](int64_t o) { return __half2float(qp[o]); });
-      } else {
-        const __nv_bfloat16* qp = static_cast<const __nv_bfloat16*>(p.q);
-        gather([&](int64_t o) { return __bfloat162float(qp[o]); });
-      }
-    }
-    float qmax = 0.f;
-#pragma unroll
-    for (int j = 0; j < kGQ; ++j) {
-      q_s[j * kD + tid] = qc[j];
-      qmax = fmaxf(qmax, fabsf(qc[j]));
-    }
-    const uint32_t wmax = __reduce_max_sync(0xffffffffu, __float_as_uint(qmax));
-    if (lane == 0) red_m[warp] = wmax;
-    named_sync(1, kGroup);
-    const uint32_t mx = max(max(red_m[0], red_m[1]), max(red_m[2], red_m[3]));
-    const int eq = max(-60, min(60, exp2_ceil(__uint_as_float(mx))));
-    if (tid == 0) *eq_s = eq;
-    const float qscale = exp2i(29 - eq);
-    po = pos_desc(L, e);
-    const float qs1 = po >= 0 ? qscale * exp2i(-pos_lg(po)) : 0.f;
-#pragma unroll
-    for (int j = 0; j < kGQ; ++j) qq[j] = e >= 0 ? q_s[j * kD + (e & 0xFFFF)] * qs1 : 0.f;
-    po_hi = pos_desc(L, e_hi);
-    if (e_hi >= 0) {
-      const float qsh = qscale * exp2i(-pos_lg(po_hi));
-      qv_hi = make_float2(q_s[2 * hp * kD + (e_hi & 0xFFFF)] * qsh, q_s[(2 * hp + 1) * kD + (e_hi & 0xFFFF)] * qsh);
-    }
-    if (kDecThreads + 32 + tid < S.kpad) {
-      const int po2 = pos_desc(L, e2);
-      const float qs2 = po2 >= 0 ? qscale * exp2i(-pos_lg(po2)) : 0.f;
-#pragma unroll
-      for (int j = 0; j < kGQ; ++j) qhi_s[tid * kGQ + j] = e2 >= 0 ? q_s[j * kD + (e2 & 0xFFFF)] * qs2 : 0.f;
-      posoff_s[tid] = po2;
-    }
-    if (tid < n16) q16_s[tid] = ch16 < 0 ? 0.f : q_s[(tid % kGQ) * kD + ch16] * c2;
-    for (int i = tid + kGroup; i < n16; i += kGroup) {
-      const int ch = p.slot_chan[(3 * H + h) * kD + i / kGQ];
-      q16_s[i] = ch < 0 ? 0.f : q_s[(i % kGQ) * kD + ch] * c2;
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == kCtl) {
-    // ------------------------------------------------------------ control warp
-    // Per page i: QK(i+1) as soon as its operands are written and the QK
-    // accumulator has been read; the copy of page i+2 once stage i is free;
-    // PV(i) once its operands are written and the PV accumulator has been read.
-    int issued0 = npg > 0 ? 1 : 0, issued1 = npg > 1 ? 1 : 0, qk_open = 0, pv_open = 0;
-    const uint32_t n_ks = static_cast<uint32_t>(S.kpad / 32);
-    const uint64_t bqk_desc0 = smem_desc(bqk, 128, S.bqk_sbo);
-    const uint64_t apv_desc[2] = {smem_desc(apv, 128, 2048), smem_desc(apv + kP * kD, 128, 2048)};
-    const uint64_t bpv_desc0 = smem_desc(bpv, 128, 2048);
-    auto issue_qk = [&](int i) {
-      for (uint32_t ks = 0; ks < n_ks; ++ks)
-        mma_u8_ts(tmem + S.tm_qk, tmem + 8 * ks, bqk_desc0 + 32 * ks, kIdescQK, ks > 0 ? 1u : 0u);
-      mma_commit(&bars[bQK]);
-      qk_open = i + 1;
-    };
-    if (lane == 0 && npg > 0) {
-      wait(bKReady, 0);
-      tc_fence_after();
-      issue_qk(0);
-    }
-    for (int i = 0; i < npg; ++i) {
-      if (lane == 0) {
-        if (i + 1 < npg) {
-          wait(bKReady, (i + 1) & 1);
-          wait(bQKFree, i & 1);
-          tc_fence_after();
-          issue_qk(i + 1);
-        }
-        if (i + kStages < npg) {
-          wait(bFree0 + (i & 1), (i >> 1) & 1);
-          if (!*abort_s) {
-            issue_page(i + kStages);
-            if (i & 1) ++issued1; else ++issued0;
-          }
-        }
-        wait(bVAReady0 + (i & 1), (i >> 1) & 1);
-        wait(bVReady, i & 1);
-        if (i > 0) wait(bPVFree, (i - 1) & 1);
-        tc_fence_after();
-#pragma unroll
-        for (int ks = 0; ks < kP / 32; ++ks)
-          mma_u8_ss(tmem + S.tm_pv, apv_desc[i & 1] + 32 * ks, bpv_desc0 + 32 * ks, kIdescPV, ks > 0 ? 1u : 0u);
-        mma_commit(&bars[bPV0 + (i & 1)]);
-        pv_open = i + 1;
-      }
-      __syncwarp();
-    }
-    if (lane == 0 && *abort_s) {
-      // Drain this CTA's copies and MMAs before its shared memory and TMEM go away.
-      if (issued0) mbar_wait_bounded(&bars[bFull0], (issued0 - 1) & 1, kLimit);
-      if (issued1) mbar_wait_bounded(&bars[bFull1], (issued1 - 1) & 1, kLimit);
-      if (qk_open) mbar_wait_bounded(&bars[bQK], (qk_open - 1) & 1, kLimit);
-      if (pv_open) mbar_wait_bounded(&bars[bPV0 + ((pv_open - 1) & 1)], ((pv_open - 1) >> 1) & 1, kLimit);
-      if (p.status != nullptr) atomicExch(p.status, LF_ERR_DEVICE_TIMEOUT);
-    }
-    __syncwarp();
-  } else if (warp < 4) {
-    // ----------------------------------------------------------- producer warps
-    const uint32_t tm_a = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    for (int c = n_slots_of(L) / 4; c < S.a_cols; ++c) tmem_st_x1(tm_a + c, 0u);  // A padding columns
-    const int wd0 = L.words[0], wd1 = L.words[1], wd2 = L.words[2];
-    const int co0 = L.code_off[0], co1 = L.code_off[1], co2 = L.code_off[2], vco = L.vcode_off;
-    const int row_off = tid * R;
-    const bool has_pos = tid < S.kpad;
-    const int soff = po >= 0 ? pos_scale(po) : 0, moff = po >= 0 ? pos_min(po) : 0;
-    const float mmul = po >= 0 ? exp2i(pos_lg(po)) : 0.f;
-    const int bslot = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
-    for (int i = 0; i < npg; ++i) {
-      const int st = i & 1;
-      const unsigned char* stage = stage0 + st * S.stage_bytes;
-      wait(bFull0 + st, (i >> 1) & 1);
-      if (i > 0) wait(bQK, (i - 1) & 1);  // QK(i-1) has read A and B of QK
-      tc_fence_after();
-      // U_K(i)
-      const uint32_t* rowp = reinterpret_cast<const uint32_t*>(stage) + row_off;
-      const uint16_t* meta = reinterpret_cast<const uint16_t*>(stage + S.rows_bytes);
-      uint32_t col = tm_a, ns = 0u;
-      {
-        const uint32_t* src = rowp + co0;
-#pragma unroll 2
-        for (int w = 0; w < wd0; ++w) {
-          const uint32_t x = src[w];
-          tmem_st_x4(col + 4 * w, x & kM2, x & (kM2 << 2), x & (kM2 << 4), x & (kM2 << 6));
-          ns = __dp4a(x, 0x01010101u, ns);
-        }
-        col += 4 * wd0;
-      }
-      {
-        const uint32_t* src = rowp + co1;
-#pragma unroll 2
-        for (int w = 0; w < wd1; ++w) {
-          const uint32_t x = src[w];
-          tmem_st_x2(col + 2 * w, x & kM4, x & (kM4 << 4));
-          ns = __dp4a(x, 0x01010101u, ns);
-        }
-        col += 2 * wd1;
-      }
-      {
-        const uint32_t* src = rowp + co2;
-#pragma unroll 2
-        for (int w = 0; w < wd2; ++w) {
-          const uint32_t x = src[w];
-          tmem_st_x1(col + w, x);
-          ns = __dp4a(x, 0x01010101u, ns);
-        }
-      }
-      nsum_s[st * kP + tid] = static_cast<int>(ns);
-      const int esc = page_scale_exp(meta, kmax_off);
-      const float fsc = exp2i(-esc);
-      float bias[kGQ];
-#pragma unroll
-      for (int j = 0; j < kGQ; ++j) bias[j] = 0.f;
-      if (has_pos) {
-        const float sc = po >= 0 ? half_bits_to_float(meta[soff]) * fsc : 0.f;
-        const float mn = half_bits_to_float(meta[moff]) * mmul;
-        qk_b_row<GQ>(bqk, S.bqk_sbo, tid, qq, sc, mn, bias);
-        auto hi_row = [&](int pp, float2 qv, int o) {
-          const float sc2 = o >= 0 ? half_bits_to_float(meta[pos_scale(o)]) * fsc : 0.f;
-          const float mn2 = o >= 0 ? half_bits_to_float(meta[pos_min(o)]) * exp2i(pos_lg(o)) : 0.f;
-          hi_b_row_pair(bqk, S.bqk_sbo, pp, hp, qv, sc2);
-          const float b0 = qv.x * mn2, b1 = qv.y * mn2;
-#pragma unroll
-          for (int j = 0; j < kGQ; ++j)
-            if (j < GQ) bias[j] += (j >> 1) == hp ? ((j & 1) ? b1 : b0) : 0.f;
-        };
-        if (n_hi > 0) hi_row(kDecThreads + (tid >> 2), qv_hi, po_hi);
-#pragma unroll 1
-        for (int k = 1; k < n_hi; ++k) {
-          const int r = (tid >> 2) + 32 * (k - 1);
-          hi_row(kDecThreads + 32 + r, *reinterpret_cast<const float2*>(qhi_s + r * kGQ + 2 * hp), posoff_s[r]);
-        }
-      }
-      tmem_wait_st();
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(&bars[bKReady]);
-      const float part = warp_sum8_scatter(bias, lane);
-      if ((lane & 3) == 0) red_b[st * 32 + warp * kGQ + bslot] = part;
-      mbar_arrive(&bars[bBias0 + st]);  // bias partials and code sums of page i stored
-      // U_V(i) into the Value tile of page parity i & 1, free once PV(i-2) has
-      // completed (the producer's wait on QK(i-1) above follows PV(i-2)'s issue
-      // in the control warp, but not its completion).
-      if (i > 1) wait(bPV0 + st, ((i - 2) >> 1) & 1);
-      {
-        const uint32_t* src = rowp + vco;
-        uint32_t vw[kD / 16];
-#pragma unroll
-        for (int w = 0; w < kD / 16; ++w) vw[w] = src[w];
-        unsigned char* dst = apv + st * kP * kD + (tid & 7) * 16 + (tid >> 3) * 128;
-#pragma unroll
-        for (int w = 0; w < kD / 16; ++w) {
-          const uint32_t x = vw[w];
-          *reinterpret_cast<uint4*>(dst + w * 2048) =
-              make_uint4(x & kM2, x & (kM2 << 2), x & (kM2 << 4), x & (kM2 << 6));
-        }
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(&bars[bVAReady0 + st]);
-      mbar_arrive(&bars[bFree0 + st]);  // the producer's last read of stage i
-    }
-  } else {
-    // ------------------------------------------------------------ softmax warps
-    const int t = tid - kGroup;                  // token (TMEM lane, PV row) of this thread
-    const uint32_t tm_a = tmem + (static_cast<uint32_t>((warp - 4) * 32) << 16);
-    const int sw = warp - 4;                     // softmax warp 0..3
-    const int eq = *eq_s;
-    const float cf = c2 * exp2i(eq - 29);        // fixed-point unit 2^(Eq-29) -> log2-scaled score
-    const int row_off = t * R;
-    const int rk = (t >> 2) & 3;                 // PV row t carries code * 4^rk
-    const int w3 = L.width[3];
-    const int l8 = lane & 7;
-    float og[GQ], lt[GQ], lvt[GQ];
-#pragma unroll
-    for (int j = 0; j < GQ; ++j) og[j] = lt[j] = lvt[j] = 0.f;
-    float m_l = -INFINITY;  // running max of q-head l8, log2 units
-    int ev_prev = 0;        // Value-scale exponent of the previous page
-    // C(i-1): accumulate PV row t of the previous page, times alpha of this
-    // page's max update (held by lane j for q-head j).
-    auto accumulate_pv = [&](int ev, float alpha_lane) {
-      const float sc = exp2i(ev - 23 - 2 * rk);
-      tc_fence_after();
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        if (half * 4 >= GQ) break;
-        uint32_t a[16];
-        tmem_ld_x16_sync(tm_a + S.tm_pv + 16 * half, a);
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const int j = 4 * half + jj;
-          if (j >= GQ) break;
-          const float aj = __shfl_sync(0xffffffffu, alpha_lane, j);
-          const uint32_t lo = a[4 * jj] + (a[4 * jj + 1] << 8);
-          const float v = fmaf(static_cast<float>(a[4 * jj + 2]), 65536.f, static_cast<float>(lo));
-          og[j] = fmaf(v, sc * aj, og[j]);
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&bars[bPVFree]);
-    };
-    for (int i = 0; i < npg; ++i) {
-      const int st = i & 1;
-      const unsigned char* stage = stage0 + st * S.stage_bytes;
-      // FP16 Key tier and the token's Value scale / min from the stage first,
-      // so the QK readback below can be combined as it arrives.
-      wait(bFull0 + st, (i >> 1) & 1);
-      const uint16_t* meta = reinterpret_cast<const uint16_t*>(stage + S.rows_bytes);
-      const int esc = page_scale_exp(meta, kmax_off);
-      const uint16_t* row16 = reinterpret_cast<const uint16_t*>(stage) + 2 * (row_off + L.half_off);
-      float x[GQ];
-#pragma unroll
-      for (int j = 0; j < GQ; ++j) x[j] = 0.f;
-#pragma unroll 2
-      for (int c = 0; c < w3; ++c) {
-        const float kv = half_bits_to_float(row16[c]);
-        const float4 qa = *reinterpret_cast<const float4*>(q16_s + c * kGQ);
-        const float4 qb = *reinterpret_cast<const float4*>(q16_s + c * kGQ + 4);
-        const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-#pragma unroll
-        for (int j = 0; j < GQ; ++j) x[j] = fmaf(qv[j], kv, x[j]);
-      }
-      const float vs = half_bits_to_float(row16[w3]);
-      const float vm = half_bits_to_float(row16[w3 + 1]);
-      mbar_arrive(&bars[bFree0 + st]);  // the softmax warps' last read of stage i
-      const float f = cf * exp2i(esc), f16 = f * 65536.f;
-      wait(bQK, i & 1);
-      wait(bBias0 + st, (i >> 1) & 1);
-      tc_fence_after();
-      const float* rb = red_b + st * 32 + l8;
-      const float bias = ((rb[0] + rb[8]) + (rb[16] + rb[24])) * cf;
-      const int off64 = 64 * nsum_s[st * kP + t];
-      // QK accumulator, columns 4 j + l, in two halves (q-heads 0-3, 4-7).
-      float key[GQ];
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        if (half * 4 >= GQ) break;
-        uint32_t a[16];
-        tmem_ld_x16_sync(tm_a + S.tm_qk + 16 * half, a);
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const int j = 4 * half + jj;
-          if (j >= GQ) break;
-          const uint32_t lo = a[4 * jj] + (a[4 * jj + 1] << 8);
-          const int hi = static_cast<int>(a[4 * jj + 2]) + ((static_cast<int>(a[4 * jj + 3]) - off64) << 8);
-          x[j] = fmaf(static_cast<float>(hi), f16, fmaf(static_cast<float>(lo), f, x[j]));
-          key[j] = warp_max_f32(x[j]);
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&bars[bQKFree]);
-      const uint32_t vkey = __reduce_max_sync(0xffffffffu, __float_as_uint(vs));
-      uint32_t* rm = red_m + st * 48;
-      if (lane == 0) {
-#pragma unroll
-        for (int j = 0; j < kGQ; ++j) rm[sw * 12 + j] = j < GQ ? __float_as_uint(key[j]) : 0u;
-        rm[sw * 12 + 8] = vkey;
-      }
-      named_sync(2, kGroup);
-      const float km = fmaxf(fmaxf(__uint_as_float(rm[l8]), __uint_as_float(rm[12 + l8])),
-                             fmaxf(__uint_as_float(rm[24 + l8]), __uint_as_float(rm[36 + l8])));
-      const uint32_t vk = max(max(rm[8], rm[20]), max(rm[32], rm[44]));
-      const float mnew = fmaxf(m_l, km + bias);
-      const float alpha = m_l == -INFINITY ? 0.f : ex2(m_l - mnew);
-      m_l = mnew;
-      const float off = bias - mnew;
-      const int ev = max(-60, min(60, exp2_ceil(__uint_as_float(vk))));
-      const float vsc = vs * exp2i(23 - ev);
-      // The running sums to this page's max, then C(i-1) at the same scale:
-      // reading the PV accumulator now lets PV(i) issue as soon as its B rows
-      // (below) are written.
-#pragma unroll
-      for (int j = 0; j < GQ; ++j) og[j] *= __shfl_sync(0xffffffffu, alpha, j);
-      if (i > 0) {
-        wait(bPV0 + ((i - 1) & 1), ((i - 1) >> 1) & 1);
-        accumulate_pv(ev_prev, alpha);
-      }
-      ev_prev = ev;
-      uint32_t U[kGQ];
-#pragma unroll
-      for (int j = 0; j < kGQ; ++j) {
-        if (j < GQ) {
-          x[j] = ex2(x[j] + __shfl_sync(0xffffffffu, off, j));  // p_tj
-          U[j] = __float_as_uint(fmaf(x[j], vsc, 8388608.0f)) & 0x00FFFFFFu;
-        } else {
-          U[j] = 0u;
-        }
-      }
-      store_b_row(bpv + (t & 7) * 16 + (t >> 3) * 128, 2048, U);  // PV(i-1) has completed: its B rows are free
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(&bars[bVReady]);
-#pragma unroll
-      for (int j = 0; j < GQ; ++j) {
-        const float aj = __shfl_sync(0xffffffffu, alpha, j);
-        lt[j] = fmaf(lt[j], aj, x[j]);
-        lvt[j] = fmaf(lvt[j], aj, x[j] * vm);
-      }
-    }
-    if (npg > 0) {
-      wait(bPV0 + ((npg - 1) & 1), ((npg - 1) >> 1) & 1);
-      accumulate_pv(ev_prev, 1.0f);
-    }
-    // Item end: sums over the softmax warps, then the partial.
-    float mg[GQ];
-#pragma unroll
-    for (int j = 0; j < GQ; ++j) mg[j] = __shfl_sync(0xffffffffu, m_l, j) * kLn2;  // natural-log units
-    float* red = reinterpret_cast<float*>(smem + S.red);
-    auto group_sum_s = [&](float (&v)[GQ]) {
-#pragma unroll
-      for (int j = 0; j < GQ; ++j) {
-        float xx = v[j];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) xx += __shfl_xor_sync(0xffffffffu, xx, o);
-        v[j] = xx;
-      }
-      named_sync(2, kGroup);
-      if (lane == 0) {
-#pragma unroll
-        for (int j = 0; j < GQ; ++j) red[sw * kGQ + j] = v[j];
-      }
-      named_sync(2, kGroup);
-#pragma unroll
-      for (int j = 0; j < GQ; ++j) v[j] = (red[j] + red[kGQ + j]) + (red[2 * kGQ + j] + red[3 * kGQ + j]);
-    };
-    group_sum_s(lt);
-    group_sum_s(lvt);
-    const int d = (t & ~15) + ((t & 15) >> 2) + 4 * (t & 3);  // PV row t holds channel d(t)
-    const int64_t item = (static_cast<int64_t>(blockIdx.x) * p.n_chunks + blockIdx.z) * p.max_splits + s;
-    float* out = p.ws + item * (GQ * (kD + 2));
-#pragma unroll
-    for (int j = 0; j < GQ; ++j) out[j * kD + d] = og[j] + lvt[j];
-    if (t == 0) {
-#pragma unroll
-      for (int j = 0; j < GQ; ++j) {
-        out[GQ * kD + j] = mg[j];
-        out[GQ * kD + GQ + j] = lt[j];
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();  // every group finished; copies and MMAs drained
-  if (warp == kCtl) {
-    tc_fence_after();
-    tmem_dealloc(tmem, S.tm_cols);
-  }
-}
-
-}  // namespace ws
-
 }  // namespace tc
 
 bool tc_supported(const lf_layout& L, int gq, int pps) {
@@ -1330,8 +725,6 @@ bool tc_supported(const lf_layout& L, int gq, int pps) {
   const tc::TcSmem S = tc::tc_smem(L);
   // The residual split's fp32 rows must end before the query staging.
   if (S.stage0 + resid_smem(tc::kD).total > S.qs) return false;
-  const tc::ws::WsSmem W = tc::ws::ws_smem(L);
-  if (W.stage0 + resid_smem(tc::kD).total > W.qs || W.total > 227 * 1024) return false;
   return S.total <= 227 * 1024;
 }
 
@@ -1352,41 +745,12 @@ static void* tc_kernel_for(int gq) {
   }
 }
 
-template <int GQ>
-static void* ws_kernel_ptr() {
-  return reinterpret_cast<void*>(tc::ws::decode_partial_ws<GQ>);
-}
-static void* ws_kernel_for(int gq) {
-  switch (gq) {
-    case 1: return ws_kernel_ptr<1>();
-    case 2: return ws_kernel_ptr<2>();
-    case 3: return ws_kernel_ptr<3>();
-    case 4: return ws_kernel_ptr<4>();
-    case 5: return ws_kernel_ptr<5>();
-    case 6: return ws_kernel_ptr<6>();
-    case 7: return ws_kernel_ptr<7>();
-    default: return ws_kernel_ptr<8>();
-  }
-}
-
-// The tensor-core kernel the calls use: the single-group kernel, unless the
-// environment variable LF_K2_KERNEL is "ws" (read once), which selects the
-// warp-specialised one for an A/B measurement of the two.
-static bool use_ws() {
-  static const bool ws = [] {
-    const char* e = getenv("LF_K2_KERNEL");
-    return e != nullptr && strcmp(e, "ws") == 0;
-  }();
-  return ws;
-}
-
 // Dynamic shared-memory limit of the GQ-head kernel raised to at least
 // smem_bytes, with the full shared-memory carveout so several CTAs fit on
 // one SM (the occupancy computation assumes both).
 static cudaError_t configure_tc(int gq, int smem_bytes) {
-  return raise_smem_limit(use_ws() ? ws_kernel_for(gq) : tc_kernel_for(gq), smem_bytes, true);
+  return raise_smem_limit(tc_kernel_for(gq), smem_bytes, true);
 }
-static int smem_total(const lf_layout& L) { return use_ws() ? tc::ws::ws_smem(L).total : tc::tc_smem(L).total; }
 
 // Resident CTAs per SM from the kernel's own limits: registers, shared memory
 // (with the per-block reservation), threads and TMEM columns.  The runtime's
@@ -1395,14 +759,12 @@ static int smem_total(const lf_layout& L) { return use_ws() ? tc::ws::ws_smem(L)
 // not used.
 int occupancy_tc(const lf_layout& L, int gq, int pps) {
   (void)pps;  // the stage holds one page's meta row: shared memory does not depend on pps
-  const int total = smem_total(L);
-  const int tm_cols = use_ws() ? tc::ws::ws_smem(L).tm_cols : tc::tc_smem(L).tm_cols;
-  const int threads = use_ws() ? tc::ws::kThreads : tc::kThreads;
-  if (total > 227 * 1024) return 0;
-  void* kern = use_ws() ? ws_kernel_for(gq) : tc_kernel_for(gq);
+  const tc::TcSmem S = tc::tc_smem(L);
+  if (S.total > 227 * 1024) return 0;
+  void* kern = tc_kernel_for(gq);
   cudaFuncAttributes fa;
   int dev = 0, smem_sm = 0, reserved = 0, regs_sm = 0, threads_sm = 0;
-  if (configure_tc(gq, total) != cudaSuccess || cudaFuncGetAttributes(&fa, kern) != cudaSuccess ||
+  if (configure_tc(gq, S.total) != cudaSuccess || cudaFuncGetAttributes(&fa, kern) != cudaSuccess ||
       cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess ||
@@ -1411,12 +773,12 @@ int occupancy_tc(const lf_layout& L, int gq, int pps) {
     cudaGetLastError();
     return -1;
   }
-  const int warps = threads / 32;
+  const int warps = tc::kThreads / 32;
   const int regs_warp = (fa.numRegs * 32 + 255) / 256 * 256;  // allocated per warp in units of 256
   int blocks = regs_sm / (warps * regs_warp);
-  blocks = std::min(blocks, smem_sm / (total + reserved));
-  blocks = std::min(blocks, threads_sm / threads);
-  blocks = std::min(blocks, 512 / tm_cols);
+  blocks = std::min(blocks, smem_sm / (S.total + reserved));
+  blocks = std::min(blocks, threads_sm / tc::kThreads);
+  blocks = std::min(blocks, 512 / S.tm_cols);
   return std::max(blocks, 0);
 }
 
@@ -1424,19 +786,18 @@ int launch_partial_tc(const DecodeParams& p, int resid_dtype, int q_dtype, cudaS
   DecodeParams q = p;
   q.resid_dtype = resid_dtype;
   q.q_dtype = q_dtype;
-  const int total = smem_total(q.L);
-  void* kern = use_ws() ? ws_kernel_for(q.cg) : tc_kernel_for(q.cg);
+  const tc::TcSmem S = tc::tc_smem(q.L);
+  void* kern = tc_kernel_for(q.cg);
   {
-    cudaError_t e = configure_tc(q.cg, total);
+    cudaError_t e = configure_tc(q.cg, S.total);
     if (e != cudaSuccess) {
-      set_error("lf_decode_partial (tcgen05): shared memory %d B: %s", total, cudaGetErrorString(e));
+      set_error("lf_decode_partial (tcgen05): shared memory %d B: %s", S.total, cudaGetErrorString(e));
       return LF_ERR_UNSUPPORTED;
     }
   }
   dim3 grid(q.L.kv_heads * q.batch, q.max_splits, q.n_chunks);
   void* args[] = {&q};
-  cudaError_t e = launch_programmatic(kern, grid, dim3(use_ws() ? tc::ws::kThreads : tc::kThreads), total, stream,
-                                      args);
+  cudaError_t e = launch_programmatic(kern, grid, dim3(tc::kThreads), S.total, stream, args);
   if (e != cudaSuccess) {
     set_error("lf_decode_partial (tcgen05): %s", cudaGetErrorString(e));
     return LF_ERR_LAUNCH;

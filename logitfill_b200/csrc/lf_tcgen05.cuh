@@ -123,18 +123,6 @@ __device__ __forceinline__ void tmem_ld_x32_sync(uint32_t taddr, uint32_t (&r)[3
       : "memory");
 }
 
-// 16 consecutive columns of this thread's lane, waited for in the same asm block.
-__device__ __forceinline__ void tmem_ld_x16_sync(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr)
-      : "memory");
-}
-
 // --------------------------------------------------------------- UMMA ----
 // Shared-memory matrix descriptor, no swizzle: start address, leading-dim
 // byte offset (LBO), stride-dim byte offset (SBO), descriptor version 1.
