@@ -5,9 +5,11 @@
 // head, sequence) work item: four compute warps (thread t owns token t of the
 // current page, TMEM lane t and row t of the PV result) and one control warp.
 //
-// Control warp: lane 0 issues the 1-D bulk copies (a page's row block and
-// meta row per stage) and the MMAs, and nothing else, so that each MMA starts
-// as soon as its operands are ready.
+// Control warp: waits on the barriers with all lanes converged; one elected
+// lane issues the 1-D bulk copies (a page's row block and meta row per stage)
+// and the MMAs, and nothing else, so that each MMA starts as soon as its
+// operands are ready.  Issuing from the converged warp keeps the MMA operands
+// (TMEM base, descriptors) in uniform registers.
 // Compute warps, per page i:
 //   U_K  Key codes -> u8 in TMEM (A of QK, K-major), masked in place (INT2
 //        slot k of a byte as code * 4^k, INT4 as code * 16^k); the B row of QK
@@ -412,7 +414,10 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  // Broadcast from lane 0: the compiler then knows the value is the same in
+  // every lane and keeps it (and the TMEM addresses built from it) in uniform
+  // registers, which tcgen05 operands are read from.
+  const uint32_t tmem = __shfl_sync(0xffffffffu, *tmem_slot, 0);
   const uint64_t kLimit = kWaitLimitNs;
 
   if (warp == 4) {
@@ -422,41 +427,50 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     const uint64_t bqk_desc0 = smem_desc(bqk, 128, S.bqk_sbo);
     const uint64_t apv_desc0 = smem_desc(apv, 128, 2048);
     const uint64_t bpv_desc0 = smem_desc(bpv, 128, 2048);
-    if (lane == 0 && npg > 1) {
-      issue_page(1);
+    if (npg > 1) {  // every lane keeps the issue counts; lane 0 drains on abort
+      if (lane == 0) issue_page(1);
       issued1 = 1;
     }
+    auto cwait = [&](uint64_t* bar, uint32_t parity) {
+      if (mbar_try_wait(bar, parity)) return;
+      if (*abort_s) return;
+      if (!mbar_wait_bounded(bar, parity, kLimit)) *abort_s = 1;
+    };
     for (int i = 0; i < npg; ++i) {
-      if (lane == 0) {
-        if (!mbar_try_wait(&bars[kBarKReady], i & 1) && !*abort_s &&
-            !mbar_wait_bounded(&bars[kBarKReady], i & 1, kLimit))
-          *abort_s = 1;
-        tc_fence_after();
-        for (uint32_t ks = 0; ks < n_ks; ++ks)  // +512 B per K step = +32 in descriptor units
-          mma_u8_ts(tmem + S.tm_qk, tmem + 8 * ks, bqk_desc0 + 32 * ks, kIdescQK, ks > 0 ? 1u : 0u);
+      cwait(&bars[kBarKReady], i & 1);
+      __syncwarp();
+      tc_fence_after();
+      if (elect_one()) {
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)  // +512 B per K step = +32 in descriptor units
+          if (ks < static_cast<int>(n_ks))
+            mma_u8_ts(tmem + S.tm_qk, tmem + 8 * ks, bqk_desc0 + 32 * ks, kIdescQK, ks > 0 ? 1u : 0u);
         mma_commit(&bars[kBarQK]);
-        qk_open = i + 1;
-        // Stage i % 2 has been read by U_K(i), U_V(i) and the FP16 tier of S(i):
-        // it takes page i + 2.
-        if (i + kStages < npg && !*abort_s) {
-          if (!mbar_wait_bounded(&bars[kBarFree], i & 1, kLimit)) {
-            *abort_s = 1;
-          } else {
-            issue_page(i + kStages);
-            if (i & 1) ++issued1; else ++issued0;
-          }
-        }
-        if (!mbar_try_wait(&bars[kBarVReady], i & 1) && !*abort_s &&
-            !mbar_wait_bounded(&bars[kBarVReady], i & 1, kLimit))
+      }
+      __syncwarp();
+      qk_open = i + 1;
+      // Stage i % 2 has been read by U_K(i), U_V(i) and the FP16 tier of S(i):
+      // it takes page i + 2.
+      if (i + kStages < npg && !*abort_s) {
+        const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&bars[kBarFree], i & 1, kLimit));
+        if (!ok) {
           *abort_s = 1;
-        tc_fence_after();
+        } else {
+          if (elect_one()) issue_page(i + kStages);
+          if (i & 1) ++issued1; else ++issued0;
+        }
+      }
+      cwait(&bars[kBarVReady], i & 1);
+      __syncwarp();
+      tc_fence_after();
+      if (elect_one()) {
 #pragma unroll
         for (int ks = 0; ks < kP / 32; ++ks)
           mma_u8_ss(tmem + S.tm_pv, apv_desc0 + 32 * ks, bpv_desc0 + 32 * ks, kIdescPV, ks > 0 ? 1u : 0u);
         mma_commit(&bars[kBarPV]);
-        pv_open = i + 1;
       }
       __syncwarp();
+      pv_open = i + 1;
     }
     if (lane == 0 && *abort_s) {
       // Drain this CTA's copies and MMAs before its shared memory and TMEM go away.
@@ -469,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
     __syncwarp();
   } else {
     // ----------------------------------------------------------- compute warps
-    const uint32_t tm_a = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const uint32_t tm_a = tmem + (static_cast<uint32_t>(__shfl_sync(0xffffffffu, warp, 0) * 32) << 16);
     for (int c = n_slots_of(L) / 4; c < S.a_cols; ++c) tmem_st_x1(tm_a + c, 0u);  // A padding columns
     float og[GQ], lt[GQ], lvt[GQ];
 #pragma unroll
@@ -505,9 +519,17 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       uint32_t col = tm_a;
       uint32_t ns = 0u;
       {
+        // INT2: two words (8 columns) per store.
         const uint32_t* src = rowp + co0;
-#pragma unroll 2
-        for (int w = 0; w < wd0; ++w) {
+        int w = 0;
+#pragma unroll 1
+        for (; w + 2 <= wd0; w += 2) {
+          const uint32_t x = src[w], y = src[w + 1];
+          tmem_st_x8(col + 4 * w, x & kM2, x & (kM2 << 2), x & (kM2 << 4), x & (kM2 << 6), y & kM2, y & (kM2 << 2),
+                     y & (kM2 << 4), y & (kM2 << 6));
+          ns = __dp4a(y, 0x01010101u, __dp4a(x, 0x01010101u, ns));
+        }
+        if (w < wd0) {
           const uint32_t x = src[w];
           tmem_st_x4(col + 4 * w, x & kM2, x & (kM2 << 2), x & (kM2 << 4), x & (kM2 << 6));
           ns = __dp4a(x, 0x01010101u, ns);
@@ -515,9 +537,18 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
         col += 4 * wd0;
       }
       {
+        // INT4: four words (8 columns) per store, then pairs, then one.
         const uint32_t* src = rowp + co1;
-#pragma unroll 2
-        for (int w = 0; w < wd1; ++w) {
+        int w = 0;
+#pragma unroll 1
+        for (; w + 4 <= wd1; w += 4) {
+          const uint32_t x = src[w], y = src[w + 1], z = src[w + 2], u = src[w + 3];
+          tmem_st_x8(col + 2 * w, x & kM4, x & (kM4 << 4), y & kM4, y & (kM4 << 4), z & kM4, z & (kM4 << 4), u & kM4,
+                     u & (kM4 << 4));
+          ns = __dp4a(u, 0x01010101u, __dp4a(z, 0x01010101u, __dp4a(y, 0x01010101u, __dp4a(x, 0x01010101u, ns))));
+        }
+#pragma unroll 1
+        for (; w < wd1; ++w) {
           const uint32_t x = src[w];
           tmem_st_x2(col + 2 * w, x & kM4, x & (kM4 << 4));
           ns = __dp4a(x, 0x01010101u, ns);
@@ -525,9 +556,21 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
         col += 2 * wd1;
       }
       {
+        // INT8: eight words per store, then one at a time.
         const uint32_t* src = rowp + co2;
-#pragma unroll 2
-        for (int w = 0; w < wd2; ++w) {
+        int w = 0;
+#pragma unroll 1
+        for (; w + 8 <= wd2; w += 8) {
+          uint32_t x[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            x[k] = src[w + k];
+            ns = __dp4a(x[k], 0x01010101u, ns);
+          }
+          tmem_st_x8(col + w, x[0], x[1], x[2], x[3], x[4], x[5], x[6], x[7]);
+        }
+#pragma unroll 1
+        for (; w < wd2; ++w) {
           const uint32_t x = src[w];
           tmem_st_x1(col + w, x);
           ns = __dp4a(x, 0x01010101u, ns);

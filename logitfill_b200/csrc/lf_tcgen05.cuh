@@ -38,6 +38,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// One lane of the (converged) warp answers true.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t r;
+  asm volatile("{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\tselp.u32 %0, 1, 0, P;\n\t}" : "=r"(r));
+  return r != 0;
+}
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -105,6 +111,12 @@ __device__ __forceinline__ void tmem_st_x2(uint32_t taddr, uint32_t a, uint32_t 
 __device__ __forceinline__ void tmem_st_x4(uint32_t taddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(a), "r"(b),
                "r"(c), "r"(d));
+}
+// Eight consecutive columns of this thread's lane.
+__device__ __forceinline__ void tmem_st_x8(uint32_t taddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d,
+                                           uint32_t e, uint32_t f, uint32_t g, uint32_t h) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(a), "r"(b), "r"(c), "r"(d), "r"(e), "r"(f), "r"(g), "r"(h));
 }
 // 32 consecutive columns of this thread's lane, waited for in the same asm
 // block so no use of the registers can be scheduled before the load completes.
