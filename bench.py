@@ -21,6 +21,11 @@ Per-GPU work is fixed as N grows (``scaling: weak``): every rank holds its own
 * ``config2`` (N = 1): config 2, 32768-token histories, batch 8, target_bit 3.0
   (the north star's >= 70 % HBM target is stated there), with its own
   ``ms_per_step``, ``roofline`` and ``e2e``;
+* ``config3`` (N = 1): config 3, the page compression path: the 28-layer
+  prefill of a 4096-token prompt per sequence (batch 16) packed through the
+  public API and, separately, its K1 launches alone (HBM roofline fraction);
+  then 256 decode steps, each one CUDA-graph replay of every layer's attention
+  and device-side token commit, with a page flush every 128 tokens;
 * ``config4_kv``: config 4 (64 layers, 40 q / 8 KV heads, batch 64, 16384-token
   histories, target_bit 2.5) sharded by KV head over the N ranks, each layer's
   head-sharded output all-gathered over NCCL inside the timed step (strong
@@ -340,6 +345,141 @@ def time_k1(cache, k, v, T: int, dev) -> dict:
             "bytes_per_launch": moved, "avg_launch_ms": ms, "achieved": moved / (ms * 1e-3) / 1e9}
 
 
+CONFIG3 = dict(name="config3", layers=28, batch=16, n_q=28, n_kv=4, head_dim=128, prompt=4096, decode_steps=256,
+               target_bit=2.5, seed=3)
+
+
+def run_config3(steps: int, warmup: int, dev, peak: float) -> dict:
+    """BASELINE config 3, the page compression path, on one GPU.
+
+    * prefill: every layer's 4096-token bf16 prompt of all 16 sequences packed
+      into 32 pages per sequence and KV head through ``PackedKVCache.commit``
+      (host job lists, one K1 launch per layer), inputs resident in HBM;
+      ``steps`` timed repetitions, each from an empty cache, median kept;
+    * prefill_k1: the same 28 K1 launches alone (jobs already on the device):
+      the kernel's HBM roofline fraction;
+    * decode: 256 decode steps after a fresh prefill, each step a CUDA-graph
+      replay of the 28 layers' attention (K2 + K3) and ``lf_commit_token``
+      (append to the residual page, pack it when it fills), so every sequence
+      flushes a page at steps 128 and 256 inside the timed region."""
+    import ctypes
+
+    import numpy as np
+    import torch
+
+    from logitfill_b200 import _lib
+    from logitfill_b200.packed import PackedKVCache
+    from logitfill_b200.packed.attention import DecodeCall
+    from logitfill_b200.packed.layout import pack_pages
+    from logitfill_b200.synthetic import mean_key_bits, synthetic_kv, synthetic_levels
+
+    cfg = CONFIG3
+    L, B, NQ, H, D, T = cfg["layers"], cfg["batch"], cfg["n_q"], cfg["n_kv"], cfg["head_dim"], cfg["prompt"]
+    n_dec = cfg["decode_steps"]
+    levels = list(synthetic_levels(L, H, D, cfg["target_bit"], seed=cfg["seed"]))
+    cache = PackedKVCache(levels, B, NQ, H, D, device=dev, capacity=T + n_dec + 128)
+    P = cache.page_size
+    kv = [synthetic_kv(B, H, T, D, seed=cfg["seed"] * 1000, layer=l, device=dev) for l in range(L)]
+    moved = 0
+    for l in range(L):
+        lay = cache.layers[l].layout
+        moved += B * (T // P) * H * (2 * P * D * 2 + P * lay.row_words * 4 + lay.meta_halves * 2)
+
+    def prefill():
+        for l in range(L):
+            cache.commit(l, kv[l][0], kv[l][1])
+
+    def timed(fn, reps, before=None):
+        out = []
+        for _ in range(reps):
+            if before is not None:
+                before()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            out.append(a.elapsed_time(b))
+        return float(np.median(out))
+
+    reps = max(3, min(steps, 5))
+    timed(prefill, warmup, before=cache.reset)
+    cache.check_status()
+    ms_prefill = timed(prefill, reps, before=cache.reset)
+    cache.check_status()
+
+    # The K1 launches alone: the same jobs, already on the device.
+    so = _lib.lib()
+    jobs = [(b, p * P, b, p) for b in range(B) for p in range(T // P)]
+    jobs_dev = torch.tensor(jobs, dtype=torch.int32, device=dev)
+    pack_pages(cache.layers[0].layout, cache.layers[0].rows, cache.layers[0].kmeta, kv[0][0], kv[0][1], jobs)
+
+    def k1_all():
+        for l in range(L):
+            layer, (k, v) = cache.layers[l], kv[l]
+            _lib.check(so.lf_pack_pages(
+                ctypes.byref(layer.layout.c), _lib.ptr(k), _lib.ptr(v), _lib.dtype_code(k.dtype), k.stride(0),
+                k.stride(1), k.stride(2), _lib.ptr(jobs_dev), len(jobs), B, _lib.ptr(layer.layout.chan_code),
+                _lib.ptr(layer.rows), _lib.ptr(layer.kmeta), _lib.ptr(cache.status), _lib.stream_handle(dev)),
+                "lf_pack_pages")
+
+    timed(k1_all, warmup)
+    ms_k1 = timed(k1_all, reps)
+    cache.check_status()
+
+    # Decode with page flushes.
+    gen = torch.Generator(device=dev).manual_seed(4321)
+    q = torch.randn(L, B, NQ, D, generator=gen, device=dev).to(torch.bfloat16)
+    kn = torch.randn(L, B, H, D, generator=gen, device=dev).to(torch.bfloat16)
+    vn = torch.randn(L, B, H, D, generator=gen, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    cache.reset()
+    prefill()
+    torch.cuda.synchronize()
+    calls = [DecodeCall(cache, l, q[l], kn[l], vn[l], D ** -0.5, out[l]) for l in range(L)]
+
+    def step():
+        for l in range(L):
+            calls[l].launch()
+            cache.layers[l].commit_token_device(kn[l], vn[l])
+
+    graph = _graph(step)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    cache.check_status()
+    cache.reset()
+    prefill()
+
+    def decode():
+        for _ in range(n_dec):
+            graph.replay()
+
+    ms_dec = timed(decode, 1)
+    cache.check_status()
+    lengths = int(cache.layers[0].dev_hist[0].item()) + int(cache.layers[-1].dev_tail[0].item())
+    del graph
+    return {
+        "workload": f"config3: {L} layers, {NQ} q / {H} kv heads, head_dim {D}, batch {B}, bf16 prefill of a "
+                    f"{T}-token prompt per sequence packed into {T // P} pages per layer, then {n_dec} decode steps "
+                    f"with a page flush every {P} tokens, target_bit {cfg['target_bit']}",
+        "key_mean_bits": mean_key_bits(levels),
+        "prefill": {"tokens_per_s": B * T / (ms_prefill * 1e-3), "ms": ms_prefill, "bytes": moved,
+                    "gbs": moved / (ms_prefill * 1e-3) / 1e9, "frac": moved / (ms_prefill * 1e-3) / 1e9 / peak,
+                    "reps": reps,
+                    "method": "PackedKVCache.commit for every layer (host job lists + one K1 launch per layer), "
+                              "CUDA events, median"},
+        "prefill_k1": {"kernel": "lf_pack_pages (K1)", "bound": "hbm", "launches": L, "ms": ms_k1,
+                       "gbs": moved / (ms_k1 * 1e-3) / 1e9, "frac": moved / (ms_k1 * 1e-3) / 1e9 / peak,
+                       "peak": peak, "unit": "GB/s"},
+        "decode": {"value": B * n_dec / (ms_dec * 1e-3), "unit": "tok/s", "steps": n_dec,
+                   "ms_per_step": ms_dec / n_dec, "flush_steps": n_dec // P, "final_length": lengths,
+                   "method": "CUDA graph of one step (per layer K2 + K3, then lf_commit_token), replayed "
+                             f"{n_dec} times after a fresh prefill, CUDA events"},
+    }
+
+
 def workload_config(cfg: dict, n_gpus: int, shard: str) -> dict:
     per_gpu = cfg["batch"] if shard in ("weak", "kv") else cfg["batch"] // n_gpus
     par = {"weak": f"dp{n_gpus} (sequences sharded, {cfg['batch']} per GPU, no collective)",
@@ -656,6 +796,9 @@ def run_b200(args, cfg) -> None:
             del w2
             gc.collect()
             torch.cuda.empty_cache()
+            extra["config3"] = run_config3(args.steps, args.warmup, dev, main["roofline"]["peak"])
+            gc.collect()
+            torch.cuda.empty_cache()
         steps4 = max(3, min(args.steps, 10))
         shards = ["kv"] + (["batch"] if world > 1 else [])
         for shard in shards:
@@ -785,6 +928,8 @@ def main() -> None:
                     help="pages per K2 work item (default: the occupancy-aware planner)")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the config's sequences per GPU (small cases for profiling)")
+    ap.add_argument("--config3-only", action="store_true",
+                    help="print only the config-3 block (page compression path), one GPU")
     ap.add_argument("--model-decode", action="store_true",
                     help="time the model-level decode loop, eager vs CUDA graph (not the driver's bench line)")
     ap.add_argument("--context", type=int, default=8192, help="prompt length for --model-decode")
@@ -796,7 +941,13 @@ def main() -> None:
         cfg["target_bit"] = args.target_bit
     if args.batch is not None:
         cfg["batch"] = args.batch
-    if args.model_decode:
+    if args.config3_only:
+        import torch
+
+        torch.cuda.set_device(0)
+        peak, _ = measured_peak_hbm()
+        print(json.dumps({"config3": run_config3(args.steps, args.warmup, torch.device("cuda", 0), peak)}), flush=True)
+    elif args.model_decode:
         run_model_decode(args)
     elif args.impl == "reference":
         run_reference(args, cfg)

@@ -59,8 +59,12 @@ class _Layer:
         self.sync_lengths()
 
     def sync_lengths(self) -> None:
-        self.dev_hist.copy_(torch.from_numpy(self.hist_len.astype(np.int32)))
-        self.dev_tail.copy_(torch.from_numpy(self.tail_len.astype(np.int32)))
+        # Pinned, non-blocking uploads: ordered on the stream before every later
+        # kernel, without making the host wait for the kernels already queued.
+        both = torch.from_numpy(np.concatenate([self.hist_len, self.tail_len]).astype(np.int32)).pin_memory()
+        n = self.hist_len.shape[0]
+        self.dev_hist.copy_(both[:n], non_blocking=True)
+        self.dev_tail.copy_(both[n:], non_blocking=True)
 
     def ensure_residual(self, dtype) -> None:
         c = self.cache

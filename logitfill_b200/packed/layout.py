@@ -165,7 +165,9 @@ def pack_pages(layout: LayerLayout, rows: torch.Tensor, kmeta: torch.Tensor, key
     if (jobs_np[:, 2] < 0).any() or (jobs_np[:, 2] >= B).any() or (jobs_np[:, 3] < 0).any() \
             or ((jobs_np[:, 3] + 1) * P > layout.row_cap).any():
         raise ValueError("pack job writes outside the history capacity")
-    jobs_dev = torch.from_numpy(jobs_np).to(key.device, non_blocking=False)
+    # Pinned, non-blocking upload: the host does not wait for the kernels
+    # already queued (the pinned block is not reused before the copy ends).
+    jobs_dev = torch.from_numpy(jobs_np).pin_memory().to(key.device, non_blocking=True)
     so = _lib.lib()
     _lib.check(so.lf_pack_pages(
         ctypes.byref(layout.c), _lib.ptr(key), _lib.ptr(value), _lib.dtype_code(key.dtype),
