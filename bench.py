@@ -21,6 +21,8 @@ Per-GPU work is fixed as N grows (``scaling: weak``): every rank holds its own
 * ``config2`` (N = 1): config 2, 32768-token histories, batch 8, target_bit 3.0
   (the north star's >= 70 % HBM target is stated there), with its own
   ``ms_per_step``, ``roofline`` and ``e2e``;
+* ``config1_chunk16`` (N = 1): config 1's cache with a 16-token query chunk per
+  sequence (chunked prefill / scoring through ``lf_decode_multi``);
 * ``config3`` (N = 1): config 3, the page compression path: the 28-layer
   prefill of a 4096-token prompt per sequence (batch 16) packed through the
   public API and, separately, its K1 launches alone (HBM roofline fraction);
@@ -480,6 +482,43 @@ def run_config3(steps: int, warmup: int, dev, peak: float) -> dict:
     }
 
 
+def run_chunk(w, q_len: int, steps: int, warmup: int, peak: float) -> dict:
+    """A chunk of ``q_len`` query tokens per sequence over ``w``'s cache (a
+    chunked prefill or scoring step): every layer's ``lf_decode_multi`` (K2 over
+    virtual heads = q-heads x query tokens, in chunks of 8 per CTA, then K3),
+    replayed from a CUDA graph.  Each chunk reads the pages again, so the
+    unique history bytes / time understates the bytes the kernels fetch."""
+    import torch
+
+    from logitfill_b200.packed.attention import DecodeCall
+
+    gen = torch.Generator(device=w.dev).manual_seed(99)
+    L, B, NQ, H, D = w.L, w.B, w.NQ, w.H, w.D
+    q = torch.randn(L, B, NQ, q_len, D, generator=gen, device=w.dev).to(torch.bfloat16)
+    kn = torch.randn(L, B, H, q_len, D, generator=gen, device=w.dev).to(torch.bfloat16)
+    vn = torch.randn(L, B, H, q_len, D, generator=gen, device=w.dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    calls = [DecodeCall(w.cache, l, q[l], kn[l], vn[l], D ** -0.5, out[l]) for l in range(L)]
+    for _ in range(warmup):
+        for c in calls:
+            c.launch()
+    torch.cuda.synchronize()
+    w.cache.check_status()
+    g = _graph(lambda: [c.launch() for c in calls])
+    for _ in range(warmup):
+        g.replay()
+    ms = _timed_replays(g, steps, torch.cuda.current_stream(), lambda: None)
+    w.cache.check_status()
+    del g
+    kb, _ = w.bytes_per_step()
+    chunks = -(-(NQ // H) * q_len // 8)
+    return {"q_len": q_len, "value": B * q_len / (ms * 1e-3), "unit": "query tok/s", "ms_per_step": ms,
+            "steps": steps, "virtual_head_chunks_per_kv_head": chunks,
+            "unique_history_gbs": kb * L / (ms * 1e-3) / 1e9,
+            "unique_history_frac": kb * L / (ms * 1e-3) / 1e9 / peak,
+            "method": "CUDA graph of the L lf_decode_multi calls (K2 + K3 each), CUDA events"}
+
+
 def workload_config(cfg: dict, n_gpus: int, shard: str) -> dict:
     per_gpu = cfg["batch"] if shard in ("weak", "kv") else cfg["batch"] // n_gpus
     par = {"weak": f"dp{n_gpus} (sequences sharded, {cfg['batch']} per GPU, no collective)",
@@ -780,6 +819,9 @@ def run_b200(args, cfg) -> None:
     m = measure(w, args.steps, args.warmup, barrier, clocks_index=local)
     main = block(w, m, args.config, traffic_ok=args.target_bit is None and args.batch is None and world == 1
                  and args.shard == "weak" and args.k2 != "simt")
+    chunk = None
+    if not args.no_blocks and args.config == 1 and args.shard == "weak" and world == 1:
+        chunk = run_chunk(w, 16, max(3, min(args.steps, 10)), args.warmup, main["roofline"]["peak"])
     k1 = w.k1
     key_bits = mean_key_bits(w.levels if args.shard != "kv" else [lv.numpy() for lv in w.levels])
     launches = args.steps * w.L * 2
@@ -788,6 +830,8 @@ def run_b200(args, cfg) -> None:
     torch.cuda.empty_cache()
 
     extra = {}
+    if chunk is not None:
+        extra["config1_chunk16"] = chunk
     if not args.no_blocks and args.config == 1 and args.shard == "weak":
         if world == 1:
             w2 = Workload(CONFIGS[2], rank, world, "weak", dev)
