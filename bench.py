@@ -29,9 +29,14 @@ Per-GPU work is fixed as N grows (``scaling: weak``): every rank holds its own
   then 256 decode steps, each one CUDA-graph replay of every layer's attention
   and device-side token commit, with a page flush every 128 tokens;
 * ``config4_kv``: config 4 (64 layers, 40 q / 8 KV heads, batch 64, 16384-token
-  histories, target_bit 2.5) sharded by KV head over the N ranks, each layer's
-  head-sharded output all-gathered over NCCL inside the timed step (strong
-  scaling: the total work is fixed);
+  histories, target_bit 2.5) sharded by KV head over the N ranks (strong
+  scaling: the total work is fixed).  Each layer's split merge stores the
+  rank's output heads into every rank's gathered buffer over NVLink and
+  signals it; a bounded wait per layer completes the gather, inside the timed
+  step;
+* ``config4_kv_nccl`` (N > 1): the same with each layer's output gathered by
+  an NCCL all-gather instead of the fused merge-gather (the collective
+  baseline);
 * ``config4_batch`` (N > 1): config 4 sharded by sequence (strong, no collective).
 
 Timing: W untimed warm-up steps, then K timed steps replayed from a CUDA graph
@@ -519,12 +524,13 @@ def run_chunk(w, q_len: int, steps: int, warmup: int, peak: float) -> dict:
             "method": "CUDA graph of the L lf_decode_multi calls (K2 + K3 each), CUDA events"}
 
 
-def workload_config(cfg: dict, n_gpus: int, shard: str) -> dict:
+def workload_config(cfg: dict, n_gpus: int, shard: str, kv_gather: str = "p2p") -> dict:
     per_gpu = cfg["batch"] if shard in ("weak", "kv") else cfg["batch"] // n_gpus
     par = {"weak": f"dp{n_gpus} (sequences sharded, {cfg['batch']} per GPU, no collective)",
            "batch": f"dp{n_gpus} ({cfg['batch']} sequences split over the GPUs, no collective)",
-           "kv": f"kv{n_gpus} ({cfg['n_kv']} KV heads split over the GPUs, NCCL all-gather of each layer's "
-                 f"output)"}[shard]
+           "kv": f"kv{n_gpus} ({cfg['n_kv']} KV heads split over the GPUs; each layer's output gathered "
+                 + ("by the split merge storing into every GPU's buffer over NVLink (lf_decode_merge_gather) "
+                    "and a bounded wait per layer)" if kv_gather == "p2p" else "with an NCCL all-gather)")}[shard]
     return {
         "workload": f"{cfg['name']}: {cfg['layers']} layers, {cfg['n_q']} q / {cfg['n_kv']} kv heads, "
                     f"head_dim {cfg['head_dim']}, batch {cfg['batch']}"
@@ -544,7 +550,8 @@ class Workload:
     """One rank's share of a config: the packed caches of every layer,
     per-step inputs, outputs and the per-layer decode calls."""
 
-    def __init__(self, cfg: dict, rank: int, world: int, shard: str, dev, pps=None, with_k1=False):
+    def __init__(self, cfg: dict, rank: int, world: int, shard: str, dev, pps=None, with_k1=False,
+                 kv_gather: str = "p2p"):
         import torch
 
         from logitfill_b200.packed import PackedKVCache
@@ -588,8 +595,16 @@ class Workload:
         self.vn = torch.randn(L, B, H, D, generator=gen, device=dev).to(torch.bfloat16)
         self.out = torch.empty(L, B, NQ, D, device=dev, dtype=torch.bfloat16)
         self.gathered = None
+        self.peer = None
+        self.kv_gather = kv_gather
         if shard == "kv" and world > 1:
-            self.gathered = torch.empty(L, world, B, NQ, D, device=dev, dtype=torch.bfloat16)
+            if kv_gather == "p2p":
+                from logitfill_b200.sharding import PeerGather
+
+                self.peer = PeerGather(L, B, NQ, D, torch.bfloat16, dev)
+                self.gathered = self.peer.gathered
+            else:
+                self.gathered = torch.empty(L, world, B, NQ, D, device=dev, dtype=torch.bfloat16)
         self.scaling = D ** -0.5
         self.calls = [DecodeCall(cache, l, self.q[l], self.kn[l], self.vn[l], self.scaling, self.out[l], pps=pps)
                       for l in range(L)]
@@ -601,9 +616,23 @@ class Workload:
         out = self.out if out is None else out
         gathered = self.gathered if gathered is None else gathered
         for l, c in enumerate(calls):
+            if self.peer is not None and calls is self.calls:
+                # K2, then the split merge storing this rank's heads into every
+                # rank's buffer over NVLink, then the bounded wait for the layer.
+                c.launch_partial()
+                self.peer.merge(c, l)
+                self.peer.wait(l)
+                continue
             c.launch()
             if self.shard == "kv" and self.world > 1:
                 gather_heads(out[l], gathered[l])
+
+    def close(self) -> None:
+        """Collective when the outputs are gathered through peer memory."""
+        if self.peer is not None:
+            self.peer.check_status()
+            self.peer.close()
+            self.peer = None
 
     def bytes_per_step(self):
         k2_bytes, total = [], 0
@@ -761,7 +790,7 @@ def block(w: Workload, m: dict, config_id: int, traffic_ok: bool) -> dict:
     out = {
         "value": seqs / (m["ms"] * 1e-3), "unit": "tok/s", "ms_per_step": m["ms"], "n_gpus": world,
         "scaling": "weak" if w.shard == "weak" else "strong",
-        "config": workload_config(cfg, world, w.shard),
+        "config": workload_config(cfg, world, w.shard, w.kv_gather),
         "hbm_gbs": step_gbs * world, "hbm_frac_of_peak_per_gpu": step_gbs / peak,
         "pages_per_split": w.calls[0].pps,
         "roofline": {"kernel": "lf_decode_partial (K2)", "bound": "hbm", "achieved": achieved, "peak": peak,
@@ -844,12 +873,13 @@ def run_b200(args, cfg) -> None:
             gc.collect()
             torch.cuda.empty_cache()
         steps4 = max(3, min(args.steps, 10))
-        shards = ["kv"] + (["batch"] if world > 1 else [])
-        for shard in shards:
-            w4 = Workload(CONFIGS[4], rank, world, shard, dev)
+        shards = [("kv", "p2p")] + ([("kv", "nccl"), ("batch", None)] if world > 1 else [])
+        for shard, gather in shards:
+            w4 = Workload(CONFIGS[4], rank, world, shard, dev, kv_gather=gather or "p2p")
             b4 = block(w4, measure(w4, steps4, args.warmup, barrier, e2e=False), 4, traffic_ok=False)
             b4["steps"] = steps4
-            extra[f"config4_{shard}"] = b4
+            extra["config4_kv_nccl" if gather == "nccl" else f"config4_{shard}"] = b4
+            w4.close()
             del w4
             gc.collect()
             torch.cuda.empty_cache()

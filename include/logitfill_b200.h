@@ -46,7 +46,8 @@ enum lf_status {
   LF_ERR_UNSUPPORTED = 2,      /* geometry this build does not implement           */
   LF_ERR_LAUNCH = 3,           /* the CUDA launch failed (see lf_last_error)       */
   LF_ERR_DEVICE_TIMEOUT = 4,   /* a bounded device-side wait gave up               */
-  LF_ERR_OUT_OF_RANGE = 5      /* a device-side bounds check rejected a job        */
+  LF_ERR_OUT_OF_RANGE = 5,     /* a device-side bounds check rejected a job        */
+  LF_ERR_CUDA = 6              /* a CUDA runtime call failed (see lf_last_error)   */
 };
 
 enum lf_dtype { LF_F32 = 0, LF_F16 = 1, LF_BF16 = 2 };
@@ -278,6 +279,48 @@ LF_API int lf_selftest_wait(int32_t* status, int64_t limit_ns, int arrive, lf_st
  */
 LF_API int lf_selftest_divide(const float* x, const float* lo, const float* scale, int64_t n, int bits,
                               float* quotient, uint32_t* code, lf_stream_t stream);
+
+/*
+ * KV-head sharding over NVLink: the split merge fused with the output
+ * all-gather.  The reference decodes all KV heads on one device
+ * (reference.py:45-47 expands them with repeat_kv, kernel.cu:234 launches one
+ * CTA per q-head); when the KV heads are split over N GPUs, rank r owns heads
+ * [r H/N, (r+1) H/N) and every layer's output must reach every rank.
+ *
+ * Buffers shared between the ranks' processes come from lf_ipc_alloc (device
+ * memory, zero-filled) and travel as 64-byte CUDA IPC handles (lf_ipc_handle,
+ * lf_ipc_open with peer access enabled, lf_ipc_close; lf_ipc_free on the
+ * owner after every peer has closed it).
+ *
+ * lf_decode_merge_gather is lf_decode_merge for one query token per sequence
+ * (n_q / kv_heads <= 8 q-heads per KV head; same workspace, same result bit
+ * for bit), storing this rank's output [batch, n_q, head_dim] (n_q = the
+ * rank's q-heads) as block `rank` of layer `layer` of every rank's gathered
+ * buffer [layers][world][batch][n_q][head_dim] (dtype out_dtype): peer_out
+ * holds the world buffer addresses (device array of uint64).  Each CTA then
+ * adds 1 to uint32 counter `layer` of every rank's flag array (peer_flags,
+ * device array of uint64), after making its stores visible to all GPUs.
+ * lf_gather_signals(batch, n_q, world) is the number of adds a rank receives
+ * per layer.
+ *
+ * lf_gather_wait launches one thread on `stream` that waits until counter
+ * `layer` of this rank's flags reaches `expected`, then subtracts `expected`,
+ * so the counter serves the next step.  It gives up after limit_ns and
+ * writes LF_ERR_DEVICE_TIMEOUT to *status (device int32, may be NULL).
+ * Kernels after it on the stream see every rank's block of that layer.
+ */
+LF_API int lf_ipc_alloc(size_t bytes, void** ptr);
+LF_API int lf_ipc_free(void* ptr);
+LF_API int lf_ipc_handle(const void* ptr, void* handle);
+LF_API int lf_ipc_open(const void* handle, void** ptr);
+LF_API int lf_ipc_close(void* ptr);
+LF_API int lf_decode_merge_gather(const float* workspace, const int32_t* hist_tokens, int batch, int kv_heads,
+                                  int n_q, int head_dim, int page_size, int pages_per_split, int max_splits,
+                                  const uint64_t* peer_out, const uint64_t* peer_flags, int layer, int rank,
+                                  int world, int out_dtype, lf_stream_t stream);
+LF_API int lf_gather_signals(int batch, int n_q, int world);
+LF_API int lf_gather_wait(uint32_t* flags, int layer, uint32_t expected, uint64_t limit_ns, int32_t* status,
+                          lf_stream_t stream);
 
 /* Human-readable text of a status code; detail of the last failure on this thread. */
 LF_API const char* lf_status_string(int status);

@@ -11,14 +11,16 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "liblogitfill_b200.so"
 
-LF_OK, LF_ERR_INVALID_ARGUMENT, LF_ERR_UNSUPPORTED, LF_ERR_LAUNCH, LF_ERR_DEVICE_TIMEOUT, LF_ERR_OUT_OF_RANGE = range(6)
+(LF_OK, LF_ERR_INVALID_ARGUMENT, LF_ERR_UNSUPPORTED, LF_ERR_LAUNCH, LF_ERR_DEVICE_TIMEOUT, LF_ERR_OUT_OF_RANGE,
+ LF_ERR_CUDA) = range(7)
 LF_F32, LF_F16, LF_BF16 = 0, 1, 2
 
 EXPORTS = (
     "lf_layout_init", "lf_pack_pages", "lf_dequantize", "lf_decode_workspace_bytes",
     "lf_decode_max_splits", "lf_decode_occupancy", "lf_decode_partial", "lf_decode_noalloc", "lf_decode_merge",
     "lf_decode", "lf_decode_multi", "lf_decode_max_splits_multi", "lf_commit_token", "lf_selftest_wait", "lf_selftest_divide",
-    "lf_status_string", "lf_last_error",
+    "lf_ipc_alloc", "lf_ipc_free", "lf_ipc_handle", "lf_ipc_open", "lf_ipc_close", "lf_decode_merge_gather",
+    "lf_gather_signals", "lf_gather_wait", "lf_status_string", "lf_last_error",
 )
 
 
@@ -74,6 +76,15 @@ def lib() -> ctypes.CDLL:
                                     P, P, P]),
         "lf_selftest_wait": (c_int, [P, c_int64, c_int, P]),
         "lf_selftest_divide": (c_int, [P, P, P, c_int64, c_int, P, P, P]),
+        "lf_ipc_alloc": (c_int, [c_size_t, P]),
+        "lf_ipc_free": (c_int, [P]),
+        "lf_ipc_handle": (c_int, [P, P]),
+        "lf_ipc_open": (c_int, [P, P]),
+        "lf_ipc_close": (c_int, [P]),
+        "lf_decode_merge_gather": (c_int, [P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, P, c_int,
+                                           c_int, c_int, c_int, P]),
+        "lf_gather_signals": (c_int, [c_int, c_int, c_int]),
+        "lf_gather_wait": (c_int, [P, c_int, ctypes.c_uint32, ctypes.c_uint64, P, P]),
         "lf_status_string": (c_char_p, [c_int]),
         "lf_last_error": (c_char_p, []),
     }

@@ -148,6 +148,7 @@ extern "C" const char* lf_status_string(int status) {
     case LF_ERR_LAUNCH: return "CUDA launch failed";
     case LF_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
     case LF_ERR_OUT_OF_RANGE: return "device-side bounds check rejected a job";
+    case LF_ERR_CUDA: return "CUDA runtime call failed";
     default: return "unknown status";
   }
 }

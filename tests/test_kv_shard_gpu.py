@@ -2,12 +2,16 @@
 
 Two NCCL ranks (child processes, one GPU each) hold 4 of the 8 KV heads of a
 config-4-shaped layer (40 q / 8 KV heads, GQA 5) with their 20 query heads,
-run K2 + K3 on them and all-gather the head-sharded outputs
-(``logitfill_b200.sharding.gather_heads``).  Rank 0 also decodes the whole
-layer on its GPU; the reassembled output must equal it (the same kernels run
-on the same heads with the same split plan; max-abs 1e-6 allowed for the
-wider tier padding of the full layer).  Skipped on a box with fewer than two
-GPUs.  NVLS is off for the collective (NCCL_NVLS_ENABLE=0).
+run K2 + K3 on them and gather the head-sharded outputs, either with an NCCL
+all-gather (``logitfill_b200.sharding.gather_heads``) or through peer memory
+(``PeerGather``: the split merge stores each rank's heads into both ranks'
+buffers over NVLink, then a bounded wait per layer; run for two steps so the
+layer counter must have been taken back in between).  Rank 0 also decodes the
+whole layer on its GPU; the reassembled output must equal it (the same kernels
+run on the same heads with the same split plan; max-abs 1e-6 allowed for the
+wider tier padding of the full layer), and the two gathers must agree bit for
+bit.  Skipped on a box with fewer than two GPUs.  NVLS is off for the
+collective (NCCL_NVLS_ENABLE=0); no multicast object is created.
 """
 from __future__ import annotations
 
@@ -54,6 +58,35 @@ def _decode(levels, lengths, k, v, q, kn, vn, dims, dev, pps=4):
     return out
 
 
+def _peer_gather(levels, lengths, k, v, q, kn, vn, dims, dev, pps=4, steps=2):
+    """The rank's layer decoded with K2, then gathered by the fused split
+    merge through peer memory; the gathered ``[world, B, n_q/world, D]`` of
+    every step."""
+    from logitfill_b200.packed import PackedKVCache
+    from logitfill_b200.packed.attention import DecodeCall
+    from logitfill_b200.sharding import PeerGather
+
+    B, H, NQ, D, T = dims
+    cache = PackedKVCache([levels], B, NQ, H, D, device=dev, capacity=T + 128)
+    cache.prefill(0, k, v, lengths)
+    out = torch.empty(B, NQ, D, dtype=torch.float32, device=dev)
+    call = DecodeCall(cache, 0, q, kn, vn, D ** -0.5, out, pps=pps)
+    peer = PeerGather(1, B, NQ, D, torch.float32, dev, limit_ns=5_000_000_000)
+    got = []
+    try:
+        for _ in range(steps):
+            call.launch_partial()
+            peer.merge(call, 0)
+            peer.wait(0)
+            torch.cuda.synchronize(dev)
+            cache.check_status()
+            peer.check_status()
+            got.append(peer.gathered[0].clone())
+    finally:
+        peer.close()
+    return got
+
+
 def _worker(rank: int, world: int, port: int, out) -> None:
     import datetime
 
@@ -76,12 +109,16 @@ def _worker(rank: int, world: int, port: int, out) -> None:
         gathered = torch.empty((world,) + tuple(local.shape), dtype=local.dtype, device=dev)
         gather_heads(local, gathered)
         full_sharded = assemble_heads(gathered)
+        p2p = _peer_gather(levels[h0:h1], lengths, k[:, h0:h1].contiguous(), v[:, h0:h1].contiguous(),
+                           q[:, q0:q1].contiguous(), kn[:, h0:h1].contiguous(), vn[:, h0:h1].contiguous(),
+                           (B, h1 - h0, q1 - q0, D, T), dev)
+        same = all(bool(torch.equal(assemble_heads(g), full_sharded)) for g in p2p)
         if rank == 0:
             full = _decode(levels, lengths, k, v, q, kn, vn, dims, dev)
             diff = float((full_sharded - full).abs().max())
-            out.put((rank, diff, bool(torch.equal(full_sharded, full))))
+            out.put((rank, diff, same))
         else:
-            out.put((rank, 0.0, True))
+            out.put((rank, 0.0, same))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -99,5 +136,6 @@ def test_kv_sharded_two_gpus_equals_one_gpu():
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    (_, diff, exact), _ = results
+    (_, diff, same0), (_, _, same1) = results
     assert diff <= 1e-6, diff
+    assert same0 and same1, "the NVLink merge-gather differs from the NCCL all-gather"
