@@ -12,6 +12,10 @@ run on the same heads with the same split plan; max-abs 1e-6 allowed for the
 wider tier padding of the full layer), and the two gathers must agree bit for
 bit.  Skipped on a box with fewer than two GPUs.  NVLS is off for the
 collective (NCCL_NVLS_ENABLE=0); no multicast object is created.
+
+Failure detection without a fault: rank 1 then leaves one layer unmerged (it
+stays alive and in step); rank 0's wait for that layer gives up after 0.1 s
+with LF_ERR_DEVICE_TIMEOUT in its status word and its context stays usable.
 """
 from __future__ import annotations
 
@@ -87,6 +91,34 @@ def _peer_gather(levels, lengths, k, v, q, kn, vn, dims, dev, pps=4, steps=2):
     return got
 
 
+def _silent_rank(levels, lengths, k, v, q, kn, vn, dims, dev, rank: int) -> int:
+    """Rank 1 decodes but never merges or signals the layer; rank 0's bounded
+    wait (0.1 s) must give up.  Returns rank 0's status code (0 on rank 1)."""
+    from logitfill_b200.packed import PackedKVCache
+    from logitfill_b200.packed.attention import DecodeCall
+    from logitfill_b200.sharding import PeerGather
+
+    B, H, NQ, D, T = dims
+    cache = PackedKVCache([levels], B, NQ, H, D, device=dev, capacity=T + 128)
+    cache.prefill(0, k, v, lengths)
+    out = torch.empty(B, NQ, D, dtype=torch.float32, device=dev)
+    call = DecodeCall(cache, 0, q, kn, vn, D ** -0.5, out, pps=4)
+    peer = PeerGather(1, B, NQ, D, torch.float32, dev, limit_ns=100_000_000)
+    code = 0
+    try:
+        call.launch_partial()
+        if rank == 0:
+            peer.merge(call, 0)
+            peer.wait(0)
+        torch.cuda.synchronize(dev)
+        code = int(peer.status.item())
+        peer.status.zero_()
+        assert int(torch.arange(10, device=dev).sum().item()) == 45  # the context is still usable
+    finally:
+        peer.close()
+    return code
+
+
 def _worker(rank: int, world: int, port: int, out) -> None:
     import datetime
 
@@ -113,12 +145,15 @@ def _worker(rank: int, world: int, port: int, out) -> None:
                            q[:, q0:q1].contiguous(), kn[:, h0:h1].contiguous(), vn[:, h0:h1].contiguous(),
                            (B, h1 - h0, q1 - q0, D, T), dev)
         same = all(bool(torch.equal(assemble_heads(g), full_sharded)) for g in p2p)
+        silent = _silent_rank(levels[h0:h1], lengths, k[:, h0:h1].contiguous(), v[:, h0:h1].contiguous(),
+                              q[:, q0:q1].contiguous(), kn[:, h0:h1].contiguous(), vn[:, h0:h1].contiguous(),
+                              (B, h1 - h0, q1 - q0, D, T), dev, rank)
         if rank == 0:
             full = _decode(levels, lengths, k, v, q, kn, vn, dims, dev)
             diff = float((full_sharded - full).abs().max())
-            out.put((rank, diff, same))
+            out.put((rank, diff, same, silent))
         else:
-            out.put((rank, 0.0, same))
+            out.put((rank, 0.0, same, silent))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -136,6 +171,9 @@ def test_kv_sharded_two_gpus_equals_one_gpu():
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    (_, diff, same0), (_, _, same1) = results
+    (_, diff, same0, silent0), (_, _, same1, _) = results
     assert diff <= 1e-6, diff
     assert same0 and same1, "the NVLink merge-gather differs from the NCCL all-gather"
+    from logitfill_b200._lib import LF_ERR_DEVICE_TIMEOUT
+
+    assert silent0 == LF_ERR_DEVICE_TIMEOUT, silent0  # the wait for a rank that never signalled gave up
