@@ -245,7 +245,7 @@ decode_partial_simt(DecodeParams p) {
 // values are read as float2.
 constexpr int kMergeWarps = 4;
 
-template <typename OT>
+template <typename OT, bool kFew>
 __global__ void __launch_bounds__(kMergeWarps * 32)
 decode_merge_kernel(const float* __restrict__ ws, const int32_t* __restrict__ hist_tokens, int batch,
                     int kv_heads, int n_q, int q_len, int cg, int D, int P, int pps, int max_splits,
@@ -312,7 +312,38 @@ decode_merge_kernel(const float* __restrict__ ws, const int32_t* __restrict__ hi
       }
     }
   };
-  if (n_s <= 32) {
+  if (kFew) {
+    // At most 16 splits and head_dim 128 (the host's choice of this
+    // instantiation): the values are loaded together with the statistics (one
+    // round of loads instead of two), then summed in split order.  A separate
+    // instantiation, so the general path keeps its smaller register footprint.
+    float2 v0[16], v1[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      if (u < n_s) {
+        const float* row = vals + static_cast<int64_t>(u) * item;
+        v0[u] = *reinterpret_cast<const float2*>(row + d0);
+        v1[u] = *reinterpret_cast<const float2*>(row + d1);
+      }
+    }
+    const float ms = lane < n_s ? mstat[lane * item] : -INFINITY;
+    const float ls = lane < n_s ? mstat[lane * item + cg] : 0.f;
+    float M = ms;
+#pragma unroll
+    for (int sh = 16; sh > 0; sh >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sh));
+    const float wl = ms == -INFINITY ? 0.f : expf(ms - M);
+    Lsum = wl * ls;
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      if (u < n_s) {
+        const float w = __shfl_sync(0xffffffffu, wl, u);
+        a0 = fmaf(w, v0[u].x, a0);
+        a1 = fmaf(w, v0[u].y, a1);
+        a2 = fmaf(w, v1[u].x, a2);
+        a3 = fmaf(w, v1[u].y, a3);
+      }
+    }
+  } else if (n_s <= 32) {
     // Every split's statistics in one lane, read once.
     const float ms = lane < n_s ? mstat[lane * item] : -INFINITY;
     const float ls = lane < n_s ? mstat[lane * item + cg] : 0.f;
@@ -402,14 +433,24 @@ static int launch_merge(const float* workspace, const int32_t* hist_tokens, int 
                         int out_dtype, int64_t out_seq_stride, int64_t out_head_stride, int64_t out_tok_stride,
                         cudaStream_t s) {
   int cg = chunk_heads(n_q / kv_heads, q_len);
+  const bool few = max_splits <= 16 && head_dim == 128;  // every item has at most 16 splits
   const int64_t tasks = static_cast<int64_t>(batch) * n_q * q_len;
   const dim3 grid(static_cast<unsigned>((tasks + kMergeWarps - 1) / kMergeWarps));
   const dim3 block(kMergeWarps * 32);
   const void* kern = nullptr;
   switch (out_dtype) {
-    case LF_F32: kern = reinterpret_cast<const void*>(decode_merge_kernel<float>); break;
-    case LF_F16: kern = reinterpret_cast<const void*>(decode_merge_kernel<__half>); break;
-    case LF_BF16: kern = reinterpret_cast<const void*>(decode_merge_kernel<__nv_bfloat16>); break;
+    case LF_F32:
+      kern = few ? reinterpret_cast<const void*>(decode_merge_kernel<float, true>)
+                 : reinterpret_cast<const void*>(decode_merge_kernel<float, false>);
+      break;
+    case LF_F16:
+      kern = few ? reinterpret_cast<const void*>(decode_merge_kernel<__half, true>)
+                 : reinterpret_cast<const void*>(decode_merge_kernel<__half, false>);
+      break;
+    case LF_BF16:
+      kern = few ? reinterpret_cast<const void*>(decode_merge_kernel<__nv_bfloat16, true>)
+                 : reinterpret_cast<const void*>(decode_merge_kernel<__nv_bfloat16, false>);
+      break;
     default:
       set_error("lf_decode_merge: out dtype %d", out_dtype);
       return LF_ERR_INVALID_ARGUMENT;
