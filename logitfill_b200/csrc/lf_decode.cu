@@ -245,7 +245,7 @@ decode_partial_simt(DecodeParams p) {
 // values are read as float2.
 constexpr int kMergeWarps = 4;
 
-template <typename OT, bool kFew>
+template <typename OT, int kFew>
 __global__ void __launch_bounds__(kMergeWarps * 32)
 decode_merge_kernel(const float* __restrict__ ws, const int32_t* __restrict__ hist_tokens, int batch,
                     int kv_heads, int n_q, int q_len, int cg, int D, int P, int pps, int max_splits,
@@ -312,14 +312,14 @@ decode_merge_kernel(const float* __restrict__ ws, const int32_t* __restrict__ hi
       }
     }
   };
-  if (kFew) {
-    // At most 16 splits and head_dim 128 (the host's choice of this
+  if (kFew > 0) {
+    // At most kFew splits and head_dim 128 (the host's choice of this
     // instantiation): the values are loaded together with the statistics (one
     // round of loads instead of two), then summed in split order.  A separate
     // instantiation, so the general path keeps its smaller register footprint.
-    float2 v0[16], v1[16];
+    float2 v0[kFew > 0 ? kFew : 1], v1[kFew > 0 ? kFew : 1];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) {
+    for (int u = 0; u < kFew; ++u) {
       if (u < n_s) {
         const float* row = vals + static_cast<int64_t>(u) * item;
         v0[u] = *reinterpret_cast<const float2*>(row + d0);
@@ -334,7 +334,7 @@ decode_merge_kernel(const float* __restrict__ ws, const int32_t* __restrict__ hi
     const float wl = ms == -INFINITY ? 0.f : expf(ms - M);
     Lsum = wl * ls;
 #pragma unroll
-    for (int u = 0; u < 16; ++u) {
+    for (int u = 0; u < kFew; ++u) {
       if (u < n_s) {
         const float w = __shfl_sync(0xffffffffu, wl, u);
         a0 = fmaf(w, v0[u].x, a0);
@@ -433,23 +433,27 @@ static int launch_merge(const float* workspace, const int32_t* hist_tokens, int 
                         int out_dtype, int64_t out_seq_stride, int64_t out_head_stride, int64_t out_tok_stride,
                         cudaStream_t s) {
   int cg = chunk_heads(n_q / kv_heads, q_len);
-  const bool few = max_splits <= 16 && head_dim == 128;  // every item has at most 16 splits
+  // Every item has at most 16 (32) splits: the one-round-of-loads instantiation.
+  const int few = head_dim != 128 ? 0 : max_splits <= 16 ? 16 : max_splits <= 32 ? 32 : 0;
   const int64_t tasks = static_cast<int64_t>(batch) * n_q * q_len;
   const dim3 grid(static_cast<unsigned>((tasks + kMergeWarps - 1) / kMergeWarps));
   const dim3 block(kMergeWarps * 32);
   const void* kern = nullptr;
   switch (out_dtype) {
     case LF_F32:
-      kern = few ? reinterpret_cast<const void*>(decode_merge_kernel<float, true>)
-                 : reinterpret_cast<const void*>(decode_merge_kernel<float, false>);
+      kern = few == 16   ? reinterpret_cast<const void*>(decode_merge_kernel<float, 16>)
+             : few == 32 ? reinterpret_cast<const void*>(decode_merge_kernel<float, 32>)
+                         : reinterpret_cast<const void*>(decode_merge_kernel<float, 0>);
       break;
     case LF_F16:
-      kern = few ? reinterpret_cast<const void*>(decode_merge_kernel<__half, true>)
-                 : reinterpret_cast<const void*>(decode_merge_kernel<__half, false>);
+      kern = few == 16   ? reinterpret_cast<const void*>(decode_merge_kernel<__half, 16>)
+             : few == 32 ? reinterpret_cast<const void*>(decode_merge_kernel<__half, 32>)
+                         : reinterpret_cast<const void*>(decode_merge_kernel<__half, 0>);
       break;
     case LF_BF16:
-      kern = few ? reinterpret_cast<const void*>(decode_merge_kernel<__nv_bfloat16, true>)
-                 : reinterpret_cast<const void*>(decode_merge_kernel<__nv_bfloat16, false>);
+      kern = few == 16   ? reinterpret_cast<const void*>(decode_merge_kernel<__nv_bfloat16, 16>)
+             : few == 32 ? reinterpret_cast<const void*>(decode_merge_kernel<__nv_bfloat16, 32>)
+                         : reinterpret_cast<const void*>(decode_merge_kernel<__nv_bfloat16, 0>);
       break;
     default:
       set_error("lf_decode_merge: out dtype %d", out_dtype);
