@@ -30,7 +30,11 @@ def plan_pages_per_split(pages: int, pairs: int, resid_items: int, sms: int, occ
     head chunk) histories of ``pages`` pages each, ``resid_items`` residual
     items in all, ``sms`` SMs and ``occupancy(pps)`` the K2 CTAs per SM (<= 0:
     pps not launchable).  Returns the pps of least (waves of page items) x
-    (pps + 1.5), see ``pages_per_split``."""
+    (pps + 1.5), see ``pages_per_split``.  One refinement, when the residual
+    items fit beside the page items (a quarter of the slots at most): if all
+    full-length items fit in one wave and only the pairs' shorter last items
+    overflow, the overflow runs in the slots the first wave's short items free,
+    so the cost is max(pps + 1.5, 2 (rem + 1.5)) with rem their length."""
     if pages <= 1:
         return 1
     best, best_cost = 1, None
@@ -39,9 +43,13 @@ def plan_pages_per_split(pages: int, pairs: int, resid_items: int, sms: int, occ
         if occ <= 0:
             continue
         ctas = pairs * (-(-pages // pps))
-        per_wave = sms * (occ if 4 * resid_items <= sms * occ else min(occ, 3))
+        resid_fit = 4 * resid_items <= sms * occ
+        per_wave = sms * (occ if resid_fit else min(occ, 3))
         waves = max(1, math.ceil(ctas / per_wave - 0.02))
         cost = waves * (pps + 1.5)
+        full, rem = pages // pps, pages % pps
+        if resid_fit and waves > 1 and rem and pairs * full <= per_wave and ctas - per_wave <= pairs:
+            cost = max(pps + 1.5, 2 * (rem + 1.5))
         if best_cost is None or cost < best_cost - 1e-9:
             best, best_cost = pps, cost
     return best
