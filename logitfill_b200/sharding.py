@@ -91,7 +91,8 @@ class PeerGather:
     (this rank's block stored into every rank's buffer, then one signal per
     CTA to every rank), :meth:`wait` the bounded wait for that layer's
     signals from all ranks.  Collective: every rank constructs it, and
-    :meth:`close` is collective too."""
+    :meth:`close` is collective too.  ``gathered`` is a view of memory that
+    :meth:`close` frees: copy what must outlive it."""
 
     def __init__(self, layers: int, batch: int, n_q_local: int, head_dim: int, dtype, device, group=None,
                  limit_ns: int = 2_000_000_000):
