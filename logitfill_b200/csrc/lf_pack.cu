@@ -420,27 +420,47 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
 
   // 3. Codes and words, kPackParts threads per token row and role (every
   // kPackParts-th word each): the first kPackRole threads the Key tier words
-  // and (last part of a row) the fp16 words (FP16 Key tier, Value scale and
-  // min), the others the Value code words.  Lanes are consecutive rows, so a
-  // warp reads one column of 32 rows (32 banks).  Each word goes to the row
-  // staged in `out`.
+  // [0, ksplit) and (last part of a row) the fp16 words (FP16 Key tier, Value
+  // scale and min), the others the Value code words and, on the pair-wise
+  // Value path, the Key words [ksplit, nk).  ksplit balances the two roles (a
+  // Key code costs about twice a Value code: a record and a gathered element
+  // each).  Lanes are consecutive rows, so a warp reads one column of 32 rows
+  // (32 banks).  Each word goes to the row staged in `out`.
+  const int nk0 = L.words[0], nk1 = L.words[1], nk = nk0 + nk1 + L.words[2];
+  const bool v_pairs = D % 16 == 0 && L.v_group % 16 == 0;
+  int ksplit = nk;
+  if (v_pairs) {
+    const int cost_k = 2 * (16 * nk0 + 8 * nk1 + 4 * L.words[2]);
+    const int target = (cost_k + 16 * L.vcode_words) / 2;
+    int acc = 0;
+    ksplit = 0;
+    while (ksplit < nk) {
+      const int c = 2 * (ksplit < nk0 ? 16 : ksplit < nk0 + nk1 ? 8 : 4);
+      if (acc + c > target) break;
+      acc += c;
+      ++ksplit;
+    }
+  }
+  // Key word w of row t.
+  auto key_word_at = [&](int t, int w) {
+    const unsigned char* row = xk + t * sw4;
+    const SlotRec* rec = kslot + (t / kg) * S.nslot;
+    uint32_t* orow = out + t * R;
+    if (w < nk0) {
+      orow[L.code_off[0] + w] = key_word<T, 2>(row, rec + 16 * w);
+    } else if (w < nk0 + nk1) {
+      orow[L.code_off[1] + w - nk0] = key_word<T, 4>(row, rec + S.tbase1 + 8 * (w - nk0));
+    } else {
+      orow[L.code_off[2] + w - nk0 - nk1] = key_word<T, 8>(row, rec + S.tbase2 + 4 * (w - nk0 - nk1));
+    }
+  };
   if (tid < kPackRole) {
     const int part = tid / kPackRows;
-    const int nk0 = L.words[0], nk1 = L.words[1], nk = nk0 + nk1 + L.words[2];
     const int half_part = kPackParts - 1;  // the part that also writes the fp16 words
     for (int t = tid % kPackRows; t < P; t += kPackRows) {
       const unsigned char* row = xk + t * sw4;
-      const SlotRec* rec = kslot + (t / kg) * S.nslot;
       uint32_t* orow = out + t * R;
-      for (int w = part; w < nk; w += kPackParts) {
-        if (w < nk0) {
-          orow[L.code_off[0] + w] = key_word<T, 2>(row, rec + 16 * w);
-        } else if (w < nk0 + nk1) {
-          orow[L.code_off[1] + w - nk0] = key_word<T, 4>(row, rec + S.tbase1 + 8 * (w - nk0));
-        } else {
-          orow[L.code_off[2] + w - nk0 - nk1] = key_word<T, 8>(row, rec + S.tbase2 + 4 * (w - nk0 - nk1));
-        }
-      }
+      for (int w = part; w < ksplit; w += kPackParts) key_word_at(t, w);
       if (part != half_part) continue;
       const int w3 = L.width[3];
       for (int w = L.half_off; w < R; ++w) {
@@ -491,6 +511,7 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
           ++gi;
         }
       }
+      for (int w = ksplit + part; w < nk; w += kPackParts) key_word_at(t, w);
     }
   } else {
     const int vg = L.v_group;
