@@ -87,6 +87,39 @@ __device__ __forceinline__ uint32_t pack_code(float x, float lo, float scale, fl
   return min(r, qmax);
 }
 
+constexpr uint32_t kMagicBits = 0x4B400000u;  // bit pattern of 1.5 * 2^23
+
+// Two codes, each as pack_code forms it, with packed fp32x2 arithmetic
+// (sm_100a): every lane of {sub, mul, fma, add}.rn.f32x2 rounds as the scalar
+// instruction does.  Takes nscale = -scale: the residual fma(q0, -scale, d)
+// equals fma(-q0, scale, d).  Returns each lane's magic-number sum bit pattern
+// clamped to kMagicBits + qmax, i.e. code + kMagicBits; a caller that adds
+// several shifted codes takes the shifted kMagicBits off once.
+__device__ __forceinline__ uint2 pack_bits2(float2 x, float2 lo, float2 nscale, float2 rcp, uint32_t qmax) {
+  uint32_t a, b;
+  asm("{\n\t.reg .b64 X, L, N, C, M, D, Q, R;\n\t"
+      "mov.b64 X, {%2, %3};\n\t"
+      "mov.b64 L, {%4, %5};\n\t"
+      "mov.b64 N, {%6, %7};\n\t"
+      "mov.b64 C, {%8, %9};\n\t"
+      "mov.b64 M, {%10, %10};\n\t"
+      "sub.rn.f32x2 D, X, L;\n\t"
+      "mul.rn.f32x2 Q, D, C;\n\t"
+      "fma.rn.f32x2 R, Q, N, D;\n\t"
+      "fma.rn.f32x2 Q, R, C, Q;\n\t"
+      "add.rn.f32x2 Q, Q, M;\n\t"
+      "mov.b64 {%0, %1}, Q;\n\t}"
+      : "=r"(a), "=r"(b)
+      : "r"(__float_as_uint(x.x)), "r"(__float_as_uint(x.y)), "r"(__float_as_uint(lo.x)),
+        "r"(__float_as_uint(lo.y)), "r"(__float_as_uint(nscale.x)), "r"(__float_as_uint(nscale.y)),
+        "r"(__float_as_uint(rcp.x)), "r"(__float_as_uint(rcp.y)), "r"(kMagicBits));
+  return make_uint2(min(a, kMagicBits + qmax), min(b, kMagicBits + qmax));
+}
+__device__ __forceinline__ uint2 pack_code2(float2 x, float2 lo, float2 nscale, float2 rcp, uint32_t qmax) {
+  const uint2 r = pack_bits2(x, lo, nscale, rcp, qmax);
+  return make_uint2(r.x - kMagicBits, r.y - kMagicBits);
+}
+
 template <typename F>
 __device__ __forceinline__ void dispatch_noop(F) {}
 

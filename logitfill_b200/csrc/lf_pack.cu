@@ -56,7 +56,7 @@ __host__ __device__ inline PackSmem pack_smem(const lf_layout& L, int esz) {
   s.xv = off; off += round16(P * s.sw * 4);
   s.chan = off; off += round16(D * 4);
   s.slotmap = off; off += round16(4 * D * 4);
-  s.kslot = off; off += G * (s.nslot > 0 ? s.nslot : 1) * 16;
+  s.kslot = off; off += G * (s.nslot > 0 ? s.nslot : 2) * 16;
   s.vstat = off; off += P * NV * 16;
   s.h16 = off; off += round16((L.width[3] > 0 ? L.width[3] : 1) * 4);
   s.out = off; off += round16(P * L.row_words * 4);
@@ -65,13 +65,16 @@ __host__ __device__ inline PackSmem pack_smem(const lf_layout& L, int esz) {
   return s;
 }
 
-// Per-slot record of a Key tier slot (group g, tier slot): scale, RN(1/scale),
-// min, and the byte offset of the slot's channel in a staged row.  A padding
-// slot (past the head's channel count, or past the tier width) reads the zero
-// word of the row with scale 1, min 0: its code is 0 (layout.py:95-97).
-struct __align__(16) SlotRec {
-  float scale, rcp, lo;
-  int off;
+// Records of two adjacent Key tier slots (group g, tier slots 2i and 2i+1),
+// lane e for slot 2i + e, laid out so each field pair is one fp32x2 operand:
+// -scale, RN(1/scale), min, and the byte offset of the slot's channel in a
+// staged row.  A padding slot (past the head's channel count, or past the
+// tier width) reads the zero word of the row with scale 1, min 0: its code
+// is 0 (layout.py:95-97).  Every tier starts at an even slot.
+struct __align__(16) SlotPair {
+  float nscale[2], rcp[2];
+  float lo[2];
+  int off[2];
 };
 
 template <typename T>
@@ -171,19 +174,27 @@ __device__ __forceinline__ float2 load_pair<float>(const unsigned char* p) {
   return make_float2(*reinterpret_cast<const float*>(p), *reinterpret_cast<const float*>(p + 4));
 }
 
-// A Key word of token row `row`: BITS-bit codes of the slots rec[0 .. 32 / BITS).
+// A Key word of token row `row`: BITS-bit codes of the slots of the pairs
+// rec[0 .. 16 / BITS), two codes per packed fp32x2 evaluation.
 template <typename T, int BITS>
-__device__ __forceinline__ uint32_t key_word(const unsigned char* row, const SlotRec* rec) {
+__device__ __forceinline__ uint32_t key_word(const unsigned char* row, const SlotPair* rec) {
   constexpr int kPer = 32 / BITS;
   constexpr uint32_t kQmax = (1u << BITS) - 1u;
-  uint32_t word = 0;
+  uint32_t word = 0, bias = 0;
 #pragma unroll
-  for (int k = 0; k < kPer; ++k) {
-    const SlotRec r = rec[k];
-    // the fields are disjoint: adding is OR-ing (one shift-add)
-    word += pack_code(load_elem<T>(row + r.off), r.lo, r.scale, r.rcp, kQmax) << (k * BITS);
+  for (int k = 0; k < kPer; k += 2) {
+    const float4 a = *reinterpret_cast<const float4*>(rec[k / 2].nscale);  // -scale x2, rcp x2
+    const int4 b = *reinterpret_cast<const int4*>(rec[k / 2].lo);          // min x2, offset x2
+    const float2 x = make_float2(load_elem<T>(row + b.z), load_elem<T>(row + b.w));
+    const uint2 c = pack_bits2(x, make_float2(__int_as_float(b.x), __int_as_float(b.y)), make_float2(a.x, a.y),
+                               make_float2(a.z, a.w), kQmax);
+    // the fields are disjoint: adding is OR-ing (one shift-add); each sum
+    // carries kMagicBits, taken off once at the end (mod 2^32)
+    word += c.x << (k * BITS);
+    word += c.y << ((k + 1) * BITS);
+    bias += (kMagicBits << (k * BITS)) + (kMagicBits << ((k + 1) * BITS));
   }
-  return word;
+  return word - bias;
 }
 
 template <typename T>
@@ -198,7 +209,7 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
   unsigned char* xv = smem + S.xv;
   int* chan = reinterpret_cast<int*>(smem + S.chan);        // chan_code of the head
   int* slotmap = reinterpret_cast<int*>(smem + S.slotmap);  // [tier][slot] -> channel or -1
-  SlotRec* kslot = reinterpret_cast<SlotRec*>(smem + S.kslot);
+  SlotPair* kslot = reinterpret_cast<SlotPair*>(smem + S.kslot);
   float4* vstat = reinterpret_cast<float4*>(smem + S.vstat);  // [token][v group]: scale, rcp, min
   int* h16 = reinterpret_cast<int*>(smem + S.h16);          // FP16 slot -> byte offset in a row
   uint32_t* out = reinterpret_cast<uint32_t*>(smem + S.out);
@@ -299,7 +310,8 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
       is_scale |= (e >= L.scale_off[b] && e < L.scale_off[b] + L.width[b]);
     meta[i] = is_scale ? 0x3C00 : 0;
   }
-  for (int i = tid; i < G * S.nslot; i += kPackThreads) kslot[i] = SlotRec{1.0f, 1.0f, 0.0f, S.pad_off};
+  for (int i = tid; i < G * S.nslot / 2; i += kPackThreads)
+    kslot[i] = SlotPair{{-1.0f, -1.0f}, {1.0f, 1.0f}, {0.0f, 0.0f}, {S.pad_off, S.pad_off}};
   __syncthreads();
   for (int c = tid; c < D; c += kPackThreads) {
     const int code = chan[c];
@@ -343,7 +355,12 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
           if (tier < 0 || tier > 2 || local >= L.width[tier]) continue;
           const float sc = asym_scale(hi[e], lo[e], 2 << tier);
           const int base = tier == 0 ? 0 : tier == 1 ? S.tbase1 : S.tbase2;
-          kslot[g * S.nslot + base + local] = SlotRec{sc, __frcp_rn(sc), lo[e], (c0 + e) * static_cast<int>(sizeof(T))};
+          const int si = g * S.nslot + base + local;
+          SlotPair& sp = kslot[si >> 1];
+          sp.nscale[si & 1] = -sc;
+          sp.rcp[si & 1] = __frcp_rn(sc);
+          sp.lo[si & 1] = lo[e];
+          sp.off[si & 1] = (c0 + e) * static_cast<int>(sizeof(T));
           meta[g * M + L.scale_off[tier] + local] = float_to_half_bits(sc);
           meta[g * M + L.min_off[tier] + local] = float_to_half_bits(lo[e]);
         }
@@ -444,14 +461,14 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
   // Key word w of row t.
   auto key_word_at = [&](int t, int w) {
     const unsigned char* row = xk + t * sw4;
-    const SlotRec* rec = kslot + (t / kg) * S.nslot;
+    const SlotPair* rec = kslot + (t / kg) * (S.nslot / 2);
     uint32_t* orow = out + t * R;
     if (w < nk0) {
-      orow[L.code_off[0] + w] = key_word<T, 2>(row, rec + 16 * w);
+      orow[L.code_off[0] + w] = key_word<T, 2>(row, rec + 8 * w);
     } else if (w < nk0 + nk1) {
-      orow[L.code_off[1] + w - nk0] = key_word<T, 4>(row, rec + S.tbase1 + 8 * (w - nk0));
+      orow[L.code_off[1] + w - nk0] = key_word<T, 4>(row, rec + S.tbase1 / 2 + 4 * (w - nk0));
     } else {
-      orow[L.code_off[2] + w - nk0 - nk1] = key_word<T, 8>(row, rec + S.tbase2 + 4 * (w - nk0 - nk1));
+      orow[L.code_off[2] + w - nk0 - nk1] = key_word<T, 8>(row, rec + S.tbase2 / 2 + 2 * (w - nk0 - nk1));
     }
   };
   if (tid < kPackRole) {
@@ -496,15 +513,17 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
       }
       for (int w = part; w < L.vcode_words; w += kPackParts) {
         const float4 st = vstat[t * NV + gi];
+        const float2 lo2 = make_float2(st.z, st.z), ns2 = make_float2(-st.x, -st.x), rc2 = make_float2(st.y, st.y);
         const unsigned char* src = row + 16 * w * static_cast<int>(sizeof(T));
-        uint32_t word = 0;
+        uint32_t word = 0, bias = 0;
 #pragma unroll
         for (int k = 0; k < 16; k += 2) {
-          const float2 x = load_pair<T>(src + k * static_cast<int>(sizeof(T)));
-          word += pack_code(x.x, st.z, st.x, st.y, 3u) << (2 * k);
-          word += pack_code(x.y, st.z, st.x, st.y, 3u) << (2 * k + 2);
+          const uint2 c = pack_bits2(load_pair<T>(src + k * static_cast<int>(sizeof(T))), lo2, ns2, rc2, 3u);
+          word += c.x << (2 * k);
+          word += c.y << (2 * k + 2);
+          bias += (kMagicBits << (2 * k)) + (kMagicBits << (2 * k + 2));
         }
-        orow[w] = word;
+        orow[w] = word - bias;
         wg += kPackParts;
         while (wg >= wpg) {
           wg -= wpg;

@@ -33,17 +33,28 @@ extern "C" int lf_selftest_wait(int32_t* status, int64_t limit_ns, int arrive, l
 // Self-test of K1's per-element division: for each (x, lo, scale) triple the
 // quotient (x - lo) / scale and the code exactly as pack_pages_kernel forms
 // them (IEEE subtract, Markstein division with rcp = RN(1 / scale), round
-// half to even by the magic-number add, clamp to [0, 2^bits - 1]).
+// half to even by the magic-number add, clamp to [0, 2^bits - 1]).  The code
+// is formed both ways K1 forms codes, one element (pack_code) and a pair of
+// elements in packed fp32x2 arithmetic (pack_code2, element i with its
+// neighbour i ^ 1 in the other lane); an element whose two codes differ gets
+// the code 0xFFFFFFFF, which no reference code equals.
 namespace lf {
 
 __global__ void selftest_divide_kernel(const float* __restrict__ x, const float* __restrict__ lo,
                                        const float* __restrict__ scale, int64_t n, int bits,
                                        float* __restrict__ quot, uint32_t* __restrict__ code) {
+  const uint32_t qmax = (1u << bits) - 1u;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t j = (i ^ 1) < n ? (i ^ 1) : i;
     const float s = scale[i], rcp = __frcp_rn(s);
+    const float sj = scale[j], rcpj = __frcp_rn(sj);
     quot[i] = asym_quotient_rcp(__fsub_rn(x[i], lo[i]), s, rcp);
-    code[i] = pack_code(x[i], lo[i], s, rcp, (1u << bits) - 1u);
+    const uint32_t ci = pack_code(x[i], lo[i], s, rcp, qmax);
+    const uint32_t cj = pack_code(x[j], lo[j], sj, rcpj, qmax);
+    const uint2 c2 = pack_code2(make_float2(x[i], x[j]), make_float2(lo[i], lo[j]), make_float2(-s, -sj),
+                                make_float2(rcp, rcpj), qmax);
+    code[i] = (c2.x == ci && c2.y == cj) ? ci : 0xFFFFFFFFu;
   }
 }
 

@@ -5,9 +5,10 @@ K1 forms every code as clamp(round_half_even((x - lo) / scale), 0, 2^b - 1)
 (layout.py:12-18) but divides by Markstein's method (RN(1/scale), one
 product, an exact FMA residual and one corrective FMA) instead of an IEEE
 division.  ``lf_selftest_divide`` runs that exact device routine on given
-(x, lo, scale) triples; this test compares its quotients and codes with
-numpy's float32 IEEE subtract and divide (round to nearest even) on seeded
-sweeps:
+(x, lo, scale) triples, in both forms K1 uses: one element at a time, and two
+elements in packed fp32x2 arithmetic (an element whose two codes differ
+comes back as -1).  This test compares its quotients and codes with numpy's
+float32 IEEE subtract and divide (round to nearest even) on seeded sweeps:
 
 * operands as K1 sees them: bf16 x and lo, scale = clamp(RN((hi - lo) / qmax),
   1e-5, 1e5) for 2-, 4- and 8-bit tiers;
