@@ -194,6 +194,18 @@ __device__ __forceinline__ int exp2_ceil(float x) {
 // 2^e as a float, e in [-126, 127].
 __device__ __forceinline__ float exp2i(int e) { return __int_as_float((e + 127) << 23); }
 
+// Per-q-head float arithmetic two q-heads at a time: pair(j) for heads j,
+// j + 1 (packed fp32x2 instructions, sm_100a, each lane rounded as the
+// scalar instruction, so the results are bit-identical) and one(N - 1) for
+// an odd last head.
+template <int N, typename F2, typename F1>
+__device__ __forceinline__ void by_pairs(F2 pair, F1 one) {
+#pragma unroll
+  for (int j = 0; j + 1 < N; j += 2) pair(j);
+  if (N & 1) one(N - 1);
+}
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+
 // Barrier slots in shared memory.
 enum { kBarFull = 0, kBarKReady = kStages, kBarVReady, kBarQK, kBarPV, kBarFree, kNumBars };
 static_assert(kNumBars <= kNumBarsMax, "barrier slots");
@@ -646,8 +658,13 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
         const float4 qa = *reinterpret_cast<const float4*>(q16_s + c * kGQ);
         const float4 qb = *reinterpret_cast<const float4*>(q16_s + c * kGQ + 4);
         const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-#pragma unroll
-        for (int j = 0; j < GQ; ++j) s16[j] = fmaf(qv[j], kv, s16[j]);
+        by_pairs<GQ>(
+            [&](int j) {
+              const float2 r = __ffma2_rn(f2(qv[j], qv[j + 1]), f2(kv, kv), f2(s16[j], s16[j + 1]));
+              s16[j] = r.x;
+              s16[j + 1] = r.y;
+            },
+            [&](int j) { s16[j] = fmaf(qv[j], kv, s16[j]); });
       }
       const float vs = half_bits_to_float(row16[w3]);
       const float vm = half_bits_to_float(row16[w3 + 1]);
@@ -658,16 +675,27 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       tc_fence_after();
       uint32_t a[32];
       tmem_ld_x32_sync(tm_a + S.tm_qk, a);
-      float x[GQ];
+      float x[GQ], xh[GQ];
       float key[GQ];
 #pragma unroll
       for (int j = 0; j < GQ; ++j) {
         // acc_l = column 4 j + l; limbs 0-1 and 2-3 joined exactly in 32 bits.
         const uint32_t lo = a[4 * j] + (a[4 * j + 1] << 8);
         const int hi = static_cast<int>(a[4 * j + 2]) + ((static_cast<int>(a[4 * j + 3]) - off64) << 8);
-        x[j] = fmaf(static_cast<float>(hi), f16, fmaf(static_cast<float>(lo), f, s16[j]));
-        key[j] = warp_max_f32(x[j]);
+        x[j] = static_cast<float>(lo);
+        xh[j] = static_cast<float>(hi);
       }
+      // score = hi * 2^16 f + (lo * f + FP16 tier part)
+      by_pairs<GQ>(
+          [&](int j) {
+            const float2 r = __ffma2_rn(f2(xh[j], xh[j + 1]), f2(f16, f16),
+                                        __ffma2_rn(f2(x[j], x[j + 1]), f2(f, f), f2(s16[j], s16[j + 1])));
+            x[j] = r.x;
+            x[j + 1] = r.y;
+          },
+          [&](int j) { x[j] = fmaf(xh[j], f16, fmaf(x[j], f, s16[j])); });
+#pragma unroll
+      for (int j = 0; j < GQ; ++j) key[j] = warp_max_f32(x[j]);
       const uint32_t vkey = __reduce_max_sync(0xffffffffu, __float_as_uint(vs));
       uint32_t* rm = red_m + st * 48;
       if (lane == 0) {
@@ -691,35 +719,60 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       const float vsc = vs * exp2i(23 - ev);
       uint32_t U[kGQ];
 #pragma unroll
-      for (int j = 0; j < kGQ; ++j) {
-        if (j < GQ) {
-          x[j] = ex2(x[j] + __shfl_sync(0xffffffffu, off, j));  // p_tj
-          // Y = rint(p * vs * 2^(23 - Ev)) in [0, 2^23]: the low 24 bits of the
-          // fp32 sum 2^23 + Y are Y (2^24 itself has low bits 2^23).
-          U[j] = __float_as_uint(fmaf(x[j], vsc, 8388608.0f)) & 0x00FFFFFFu;
-        } else {
-          U[j] = 0u;
-        }
-      }
+      for (int j = 0; j < GQ; ++j) x[j] = ex2(x[j] + __shfl_sync(0xffffffffu, off, j));  // p_tj
+      // Y = rint(p * vs * 2^(23 - Ev)) in [0, 2^23]: the low 24 bits of the
+      // fp32 sum 2^23 + Y are Y (2^24 itself has low bits 2^23).
+      by_pairs<GQ>(
+          [&](int j) {
+            const float2 r = __ffma2_rn(f2(x[j], x[j + 1]), f2(vsc, vsc), f2(8388608.0f, 8388608.0f));
+            U[j] = __float_as_uint(r.x) & 0x00FFFFFFu;
+            U[j + 1] = __float_as_uint(r.y) & 0x00FFFFFFu;
+          },
+          [&](int j) { U[j] = __float_as_uint(fmaf(x[j], vsc, 8388608.0f)) & 0x00FFFFFFu; });
+#pragma unroll
+      for (int j = GQ; j < kGQ; ++j) U[j] = 0u;
       store_b_row(bpv + (tid & 7) * 16 + (tid >> 3) * 128, 2048, U);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&bars[kBarVReady]);
       // The running sums are not read by PV: rescaled and extended after the arrive.
       if (__any_sync(0xffffffffu, l8 < GQ && alpha != 1.f)) {
+        float al[GQ];
 #pragma unroll
-        for (int j = 0; j < GQ; ++j) {
-          const float aj = __shfl_sync(0xffffffffu, alpha, j);
-          og[j] *= aj;
-          lt[j] *= aj;
-          lvt[j] *= aj;
-        }
+        for (int j = 0; j < GQ; ++j) al[j] = __shfl_sync(0xffffffffu, alpha, j);
+        by_pairs<GQ>(
+            [&](int j) {
+              const float2 aj = f2(al[j], al[j + 1]);
+              const float2 o2 = __fmul2_rn(f2(og[j], og[j + 1]), aj);
+              const float2 t2 = __fmul2_rn(f2(lt[j], lt[j + 1]), aj);
+              const float2 v2 = __fmul2_rn(f2(lvt[j], lvt[j + 1]), aj);
+              og[j] = o2.x;
+              og[j + 1] = o2.y;
+              lt[j] = t2.x;
+              lt[j + 1] = t2.y;
+              lvt[j] = v2.x;
+              lvt[j + 1] = v2.y;
+            },
+            [&](int j) {
+              og[j] *= al[j];
+              lt[j] *= al[j];
+              lvt[j] *= al[j];
+            });
       }
-#pragma unroll
-      for (int j = 0; j < GQ; ++j) {
-        lt[j] += x[j];
-        lvt[j] = fmaf(x[j], vm, lvt[j]);
-      }
+      by_pairs<GQ>(
+          [&](int j) {
+            const float2 p2 = f2(x[j], x[j + 1]);
+            const float2 t2 = __fadd2_rn(f2(lt[j], lt[j + 1]), p2);
+            const float2 v2 = __ffma2_rn(p2, f2(vm, vm), f2(lvt[j], lvt[j + 1]));
+            lt[j] = t2.x;
+            lt[j + 1] = t2.y;
+            lvt[j] = v2.x;
+            lvt[j + 1] = v2.y;
+          },
+          [&](int j) {
+            lt[j] += x[j];
+            lvt[j] = fmaf(x[j], vm, lvt[j]);
+          });
       // U_K(i+1) while PV(i) runs.
       if (i + 1 < npg) {
         wait(&bars[kBarFull + (st ^ 1)], ((i + 1) >> 1) & 1);
@@ -730,11 +783,22 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
       tc_fence_after();
       tmem_ld_x32_sync(tm_a + S.tm_pv, a);
       const float sc = exp2i(ev - 23 - 2 * rk);
+      {
+        float vl[GQ], vh[GQ];
 #pragma unroll
-      for (int j = 0; j < GQ; ++j) {
-        const uint32_t lo = a[4 * j] + (a[4 * j + 1] << 8);
-        const float v = fmaf(static_cast<float>(a[4 * j + 2]), 65536.f, static_cast<float>(lo));
-        og[j] = fmaf(v, sc, og[j]);
+        for (int j = 0; j < GQ; ++j) {
+          vl[j] = static_cast<float>(a[4 * j] + (a[4 * j + 1] << 8));
+          vh[j] = static_cast<float>(a[4 * j + 2]);
+        }
+        // og += (limb2 * 2^16 + limbs 0-1) * scale
+        by_pairs<GQ>(
+            [&](int j) {
+              const float2 v2 = __ffma2_rn(f2(vh[j], vh[j + 1]), f2(65536.f, 65536.f), f2(vl[j], vl[j + 1]));
+              const float2 o2 = __ffma2_rn(v2, f2(sc, sc), f2(og[j], og[j + 1]));
+              og[j] = o2.x;
+              og[j + 1] = o2.y;
+            },
+            [&](int j) { og[j] = fmaf(fmaf(vh[j], 65536.f, vl[j]), sc, og[j]); });
       }
       // U_V(i+1): the Value tile is free once PV(i) has completed.
       if (i + 1 < npg) unpack_v(i + 1);
