@@ -120,6 +120,14 @@ __device__ __forceinline__ uint2 pack_code2(float2 x, float2 lo, float2 nscale, 
   return make_uint2(r.x - kMagicBits, r.y - kMagicBits);
 }
 
+// (x, y) = (fma(w, v.x, x), fma(w, v.y, y)) as one packed fp32x2 FMA; each
+// lane rounds as fmaf does, so the sums equal the scalar ones bit for bit.
+__device__ __forceinline__ void fma2_acc(float w, float2 v, float& x, float& y) {
+  const float2 r = __ffma2_rn(make_float2(w, w), v, make_float2(x, y));
+  x = r.x;
+  y = r.y;
+}
+
 template <typename F>
 __device__ __forceinline__ void dispatch_noop(F) {}
 

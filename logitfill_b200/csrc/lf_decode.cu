@@ -291,10 +291,8 @@ decode_merge_kernel(const float* __restrict__ ws, const int32_t* __restrict__ hi
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const float w = __shfl_sync(0xffffffffu, wl, k + u);
-        a0 = fmaf(w, v0[u].x, a0);
-        a1 = fmaf(w, v0[u].y, a1);
-        a2 = fmaf(w, v1[u].x, a2);
-        a3 = fmaf(w, v1[u].y, a3);
+        fma2_acc(w, v0[u], a0, a1);
+        fma2_acc(w, v1[u], a2, a3);
       }
     }
     for (; k < cnt; ++k) {
@@ -302,13 +300,11 @@ decode_merge_kernel(const float* __restrict__ ws, const int32_t* __restrict__ hi
       const float* row = vals + static_cast<int64_t>(s0 + k) * item;
       if (d0 < D) {
         const float2 v = *reinterpret_cast<const float2*>(row + d0);
-        a0 = fmaf(w, v.x, a0);
-        a1 = fmaf(w, v.y, a1);
+        fma2_acc(w, v, a0, a1);
       }
       if (d1 < D) {
         const float2 v = *reinterpret_cast<const float2*>(row + d1);
-        a2 = fmaf(w, v.x, a2);
-        a3 = fmaf(w, v.y, a3);
+        fma2_acc(w, v, a2, a3);
       }
     }
   };
@@ -337,10 +333,8 @@ decode_merge_kernel(const float* __restrict__ ws, const int32_t* __restrict__ hi
     for (int u = 0; u < kFew; ++u) {
       if (u < n_s) {
         const float w = __shfl_sync(0xffffffffu, wl, u);
-        a0 = fmaf(w, v0[u].x, a0);
-        a1 = fmaf(w, v0[u].y, a1);
-        a2 = fmaf(w, v1[u].x, a2);
-        a3 = fmaf(w, v1[u].y, a3);
+        fma2_acc(w, v0[u], a0, a1);
+        fma2_acc(w, v1[u], a2, a3);
       }
     }
   } else if (n_s <= 32) {

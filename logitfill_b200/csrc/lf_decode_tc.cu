@@ -150,6 +150,18 @@ __device__ __forceinline__ void store_b_row(unsigned char* dst, int sbo, const u
   *reinterpret_cast<uint4*>(dst + sbo) = make_uint4(U[4], U[5], U[6], U[7]);
 }
 
+// Per-q-head float arithmetic two q-heads at a time: pair(j) for heads j,
+// j + 1 (packed fp32x2 instructions, sm_100a, each lane rounded as the
+// scalar instruction, so the results are bit-identical) and one(N - 1) for
+// an odd last head.
+template <int N, typename F2, typename F1>
+__device__ __forceinline__ void by_pairs(F2 pair, F1 one) {
+#pragma unroll
+  for (int j = 0; j + 1 < N; j += 2) pair(j);
+  if (N & 1) one(N - 1);
+}
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+
 // Warp reduce-scatter of 8 sums: returns the warp total of v[j] for
 // j = 4*bit4(lane) + 2*bit3(lane) + bit2(lane).
 __device__ __forceinline__ float warp_sum8_scatter(const float (&v)[kGQ], int lane) {
@@ -194,18 +206,6 @@ __device__ __forceinline__ int exp2_ceil(float x) {
 // 2^e as a float, e in [-126, 127].
 __device__ __forceinline__ float exp2i(int e) { return __int_as_float((e + 127) << 23); }
 
-// Per-q-head float arithmetic two q-heads at a time: pair(j) for heads j,
-// j + 1 (packed fp32x2 instructions, sm_100a, each lane rounded as the
-// scalar instruction, so the results are bit-identical) and one(N - 1) for
-// an odd last head.
-template <int N, typename F2, typename F1>
-__device__ __forceinline__ void by_pairs(F2 pair, F1 one) {
-#pragma unroll
-  for (int j = 0; j + 1 < N; j += 2) pair(j);
-  if (N & 1) one(N - 1);
-}
-__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
-
 // Barrier slots in shared memory.
 enum { kBarFull = 0, kBarKReady = kStages, kBarVReady, kBarQK, kBarPV, kBarFree, kNumBars };
 static_assert(kNumBars <= kNumBarsMax, "barrier slots");
@@ -218,23 +218,33 @@ template <int GQ>
 __device__ __forceinline__ void qk_b_row(unsigned char* bqk, int sbo, int pp, const float (&qv)[kGQ], float sc,
                                          float mn, float (&bias)[kGQ]) {
   uint32_t U[kGQ];
+  float y[kGQ];
+  by_pairs<GQ>(
+      [&](int j) {
+        const float2 q2 = f2(qv[j], qv[j + 1]);
+        const float2 y2 = __fmul2_rn(q2, f2(sc, sc));
+        const float2 b2 = __ffma2_rn(q2, f2(mn, mn), f2(bias[j], bias[j + 1]));
+        y[j] = y2.x;
+        y[j + 1] = y2.y;
+        bias[j] = b2.x;
+        bias[j + 1] = b2.y;
+      },
+      [&](int j) {
+        y[j] = qv[j] * sc;
+        bias[j] = fmaf(qv[j], mn, bias[j]);
+      });
 #pragma unroll
-  for (int j = 0; j < kGQ; ++j) {
-    if (j < GQ) {
-      U[j] = static_cast<uint32_t>(__float2int_rn(qv[j] * sc) + (1 << 30));
-      bias[j] = fmaf(qv[j], mn, bias[j]);
-    } else {
-      U[j] = 1u << 30;  // X = 0
-    }
-  }
+  for (int j = 0; j < kGQ; ++j)
+    U[j] = j < GQ ? static_cast<uint32_t>(__float2int_rn(y[j]) + (1 << 30)) : 1u << 30;  // X = 0 past GQ
   store_b_row(bqk + (pp & 7) * 16 + (pp >> 3) * 128, sbo, U);
 }
 
 // Two q-heads (2 hp, 2 hp + 1) of the B row of QK at K position pp: the
 // same words as qk_b_row, one 8-byte store (columns 8 hp .. 8 hp + 7).
 __device__ __forceinline__ void hi_b_row_pair(unsigned char* bqk, int sbo, int pp, int hp, float2 qv, float sc) {
-  const uint32_t ua = static_cast<uint32_t>(__float2int_rn(qv.x * sc) + (1 << 30));
-  const uint32_t ub = static_cast<uint32_t>(__float2int_rn(qv.y * sc) + (1 << 30));
+  const float2 y = __fmul2_rn(qv, f2(sc, sc));
+  const uint32_t ua = static_cast<uint32_t>(__float2int_rn(y.x) + (1 << 30));
+  const uint32_t ub = static_cast<uint32_t>(__float2int_rn(y.y) + (1 << 30));
   unsigned char* dst = bqk + (pp & 7) * 16 + (pp >> 3) * 128 + (hp >= 2 ? sbo : 0) + 8 * (hp & 1);
   *reinterpret_cast<uint2*>(dst) = make_uint2(ua, ub);
 }
@@ -604,7 +614,8 @@ __global__ void __launch_bounds__(kThreads, 4) decode_partial_tc(DecodeParams p)
           const float sc2 = o >= 0 ? half_bits_to_float(meta[pos_scale(o)]) * fsc : 0.f;
           const float mn2 = o >= 0 ? half_bits_to_float(meta[pos_min(o)]) * exp2i(pos_lg(o)) : 0.f;
           hi_b_row_pair(bqk, S.bqk_sbo, pp, hp, qv, sc2);
-          const float b0 = qv.x * mn2, b1 = qv.y * mn2;
+          const float2 b01 = __fmul2_rn(qv, f2(mn2, mn2));
+          const float b0 = b01.x, b1 = b01.y;
 #pragma unroll
           for (int j = 0; j < kGQ; ++j)
             if (j < GQ) bias[j] += (j >> 1) == hp ? ((j & 1) ? b1 : b0) : 0.f;

@@ -78,13 +78,11 @@ merge_gather_kernel(const float* __restrict__ ws, const int32_t* __restrict__ hi
         const float* row = vals + static_cast<int64_t>(s0 + k) * item;
         if (d0 < D) {
           const float2 v = *reinterpret_cast<const float2*>(row + d0);
-          a0 = fmaf(w, v.x, a0);
-          a1 = fmaf(w, v.y, a1);
+          fma2_acc(w, v, a0, a1);
         }
         if (d1 < D) {
           const float2 v = *reinterpret_cast<const float2*>(row + d1);
-          a2 = fmaf(w, v.x, a2);
-          a3 = fmaf(w, v.y, a3);
+          fma2_acc(w, v, a2, a3);
         }
       }
     }
