@@ -199,7 +199,7 @@ __device__ __forceinline__ uint32_t key_word(const unsigned char* row, const Slo
 
 template <typename T>
 __global__ void __launch_bounds__(kPackThreads, 2)
-pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict__ src_v,
+pack_pages_kernel(const __grid_constant__ lf_layout L, const T* __restrict__ src_k, const T* __restrict__ src_v,
                   int64_t s_seq, int64_t s_head, int64_t s_tok, const int32_t* __restrict__ jobs,
                   int dst_batch, const int32_t* __restrict__ chan_code, int32_t* __restrict__ rows,
                   uint16_t* __restrict__ kmeta, int32_t* status) {
@@ -458,18 +458,18 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
       ++ksplit;
     }
   }
-  // Key word w of row t.
-  auto key_word_at = [&](int t, int w) {
+  // Key words [w0, w1) of row t (this thread's part, every kPackParts-th
+  // word), one loop per tier so each runs with its code width fixed.
+  auto key_words = [&](int t, int w0, int w1) {
     const unsigned char* row = xk + t * sw4;
     const SlotPair* rec = kslot + (t / kg) * (S.nslot / 2);
     uint32_t* orow = out + t * R;
-    if (w < nk0) {
-      orow[L.code_off[0] + w] = key_word<T, 2>(row, rec + 8 * w);
-    } else if (w < nk0 + nk1) {
+    int w = w0;
+    for (const int e = min(w1, nk0); w < e; w += kPackParts) orow[L.code_off[0] + w] = key_word<T, 2>(row, rec + 8 * w);
+    for (const int e = min(w1, nk0 + nk1); w < e; w += kPackParts)
       orow[L.code_off[1] + w - nk0] = key_word<T, 4>(row, rec + S.tbase1 / 2 + 4 * (w - nk0));
-    } else {
+    for (; w < w1; w += kPackParts)
       orow[L.code_off[2] + w - nk0 - nk1] = key_word<T, 8>(row, rec + S.tbase2 / 2 + 2 * (w - nk0 - nk1));
-    }
   };
   if (tid < kPackRole) {
     const int part = tid / kPackRows;
@@ -477,7 +477,7 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
     for (int t = tid % kPackRows; t < P; t += kPackRows) {
       const unsigned char* row = xk + t * sw4;
       uint32_t* orow = out + t * R;
-      for (int w = part; w < ksplit; w += kPackParts) key_word_at(t, w);
+      key_words(t, part, ksplit);
       if (part != half_part) continue;
       const int w3 = L.width[3];
       for (int w = L.half_off; w < R; ++w) {
@@ -530,7 +530,7 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
           ++gi;
         }
       }
-      for (int w = ksplit + part; w < nk; w += kPackParts) key_word_at(t, w);
+      key_words(t, ksplit + part, nk);
     }
   } else {
     const int vg = L.v_group;
@@ -574,7 +574,7 @@ pack_pages_kernel(lf_layout L, const T* __restrict__ src_k, const T* __restrict_
   for (int i = tid; i < G * M; i += kPackThreads) out_meta[i] = meta[i];
 }
 
-__global__ void dequantize_kernel(lf_layout L, const int32_t* __restrict__ rows,
+__global__ void dequantize_kernel(const __grid_constant__ lf_layout L, const int32_t* __restrict__ rows,
                                   const uint16_t* __restrict__ kmeta,
                                   const int32_t* __restrict__ chan_code, int seq, int64_t tokens,
                                   float* __restrict__ out_k, float* __restrict__ out_v) {
