@@ -237,6 +237,24 @@ pack_pages_kernel(const __grid_constant__ lf_layout L, const T* __restrict__ src
   constexpr int kVec = 16 / sizeof(T);
   const bool vec = (reinterpret_cast<uintptr_t>(ksrc) % 16 == 0) && (reinterpret_cast<uintptr_t>(vsrc) % 16 == 0) &&
                    (s_tok * static_cast<int64_t>(sizeof(T))) % 16 == 0 && D % kVec == 0;
+  // The head's channel codes are loaded first and stored after the staging,
+  // and the tables that need no input are filled while the page's loads are
+  // in flight.
+  const int chv = tid < D ? chan_code[h * D + tid] : 0;
+  auto init_tables = [&]() {
+    for (int i = tid; i < 4 * D; i += kPackThreads) slotmap[i] = -1;
+    for (int i = tid; i < G * M; i += kPackThreads) {
+      const int e = i % M;
+      // Padding channels of a tier keep scale 1.0 and min 0 (layout.py:84-85).
+      bool is_scale = false;
+      for (int b = 0; b < 3; ++b)
+        is_scale |= (e >= L.scale_off[b] && e < L.scale_off[b] + L.width[b]);
+      meta[i] = is_scale ? 0x3C00 : 0;
+    }
+    for (int i = tid; i < G * S.nslot / 2; i += kPackThreads)
+      kslot[i] = SlotPair{{-1.0f, -1.0f}, {1.0f, 1.0f}, {0.0f, 0.0f}, {S.pad_off, S.pad_off}};
+  };
+  bool tables_done = false;
   if (vec && kPackThreads % (D / kVec) == 0) {
     // Each thread keeps one 16-byte column of the rows: no division per vector.
     const int vpr = D / kVec, rstep = kPackThreads / vpr;
@@ -251,6 +269,10 @@ pack_pages_kernel(const __grid_constant__ lf_layout L, const T* __restrict__ src
           a[r] = __ldcs(reinterpret_cast<const uint4*>(ksrc + t * s_tok + ec));
           c[r] = __ldcs(reinterpret_cast<const uint4*>(vsrc + t * s_tok + ec));
         }
+      }
+      if (!tables_done) {
+        init_tables();
+        tables_done = true;
       }
 #pragma unroll
       for (int r = 0; r < kBatch; ++r) {
@@ -300,18 +322,9 @@ pack_pages_kernel(const __grid_constant__ lf_layout L, const T* __restrict__ src
       }
     }
   }
-  for (int c = tid; c < D; c += kPackThreads) chan[c] = chan_code[h * D + c];
-  for (int i = tid; i < 4 * D; i += kPackThreads) slotmap[i] = -1;
-  for (int i = tid; i < G * M; i += kPackThreads) {
-    const int e = i % M;
-    // Padding channels of a tier keep scale 1.0 and min 0 (layout.py:84-85).
-    bool is_scale = false;
-    for (int b = 0; b < 3; ++b)
-      is_scale |= (e >= L.scale_off[b] && e < L.scale_off[b] + L.width[b]);
-    meta[i] = is_scale ? 0x3C00 : 0;
-  }
-  for (int i = tid; i < G * S.nslot / 2; i += kPackThreads)
-    kslot[i] = SlotPair{{-1.0f, -1.0f}, {1.0f, 1.0f}, {0.0f, 0.0f}, {S.pad_off, S.pad_off}};
+  if (!tables_done) init_tables();
+  if (tid < D) chan[tid] = chv;
+  for (int c = tid + kPackThreads; c < D; c += kPackThreads) chan[c] = chan_code[h * D + c];
   __syncthreads();
   for (int c = tid; c < D; c += kPackThreads) {
     const int code = chan[c];
@@ -346,24 +359,30 @@ pack_pages_kernel(const __grid_constant__ lf_layout L, const T* __restrict__ src
       const int g = task / ((D + cw - 1) / cw), c0 = (task - g * ((D + cw - 1) / cw)) * cw;
       float hi[2], lo[2];
       key_stats<T>(xk, sw, g, kg, c0, split, part, hi, lo);
-      if (part == 0) {
+      // Slot record and meta entries of channel c0 + e.
+      auto record = [&](int e, float hv, float lv) {
+        if (e >= cw || c0 + e >= D) return;
+        const int code = chan[c0 + e];
+        const int tier = code >> 16, local = code & 0xFFFF;
+        if (tier < 0 || tier > 2 || local >= L.width[tier]) return;
+        const float sc = asym_scale(hv, lv, 2 << tier);
+        const int base = tier == 0 ? 0 : tier == 1 ? S.tbase1 : S.tbase2;
+        const int si = g * S.nslot + base + local;
+        SlotPair& sp = kslot[si >> 1];
+        sp.nscale[si & 1] = -sc;
+        sp.rcp[si & 1] = __frcp_rn(sc);
+        sp.lo[si & 1] = lv;
+        sp.off[si & 1] = (c0 + e) * static_cast<int>(sizeof(T));
+        meta[g * M + L.scale_off[tier] + local] = float_to_half_bits(sc);
+        meta[g * M + L.min_off[tier] + local] = float_to_half_bits(lv);
+      };
+      if (split > 1) {
+        // Every lane of the split holds both channels' statistics: parts 0
+        // and 1 each take one channel's record, in one converged pass.
+        if (part < 2) record(part, part ? hi[1] : hi[0], part ? lo[1] : lo[0]);
+      } else {
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          if (e >= cw || c0 + e >= D) continue;
-          const int code = chan[c0 + e];
-          const int tier = code >> 16, local = code & 0xFFFF;
-          if (tier < 0 || tier > 2 || local >= L.width[tier]) continue;
-          const float sc = asym_scale(hi[e], lo[e], 2 << tier);
-          const int base = tier == 0 ? 0 : tier == 1 ? S.tbase1 : S.tbase2;
-          const int si = g * S.nslot + base + local;
-          SlotPair& sp = kslot[si >> 1];
-          sp.nscale[si & 1] = -sc;
-          sp.rcp[si & 1] = __frcp_rn(sc);
-          sp.lo[si & 1] = lo[e];
-          sp.off[si & 1] = (c0 + e) * static_cast<int>(sizeof(T));
-          meta[g * M + L.scale_off[tier] + local] = float_to_half_bits(sc);
-          meta[g * M + L.min_off[tier] + local] = float_to_half_bits(lo[e]);
-        }
+        for (int e = 0; e < 2; ++e) record(e, hi[e], lo[e]);
       }
     }
   } else {
