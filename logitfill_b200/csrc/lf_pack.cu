@@ -33,7 +33,7 @@ constexpr int kPackSkip = -1;                 // src_seq of a job that packs not
 // word longer than the row, so every row ends in a zero word (`pad_off`,
 // the element a padding slot reads).
 struct PackSmem {
-  int xk, xv, chan, slotmap, kslot, vstat, h16, out, meta, total;
+  int xk, xv, chan, slotmap, kslot, vstat, h16, out, meta, kmax, total;
   int sw;      // staged row stride, 32-bit words
   int pad_off; // byte offset of the zero word in a staged row
   int nslot;   // Key tier slots the row words hold: 16 words0 + 8 words1 + 4 words2
@@ -61,6 +61,7 @@ __host__ __device__ inline PackSmem pack_smem(const lf_layout& L, int esz) {
   s.h16 = off; off += round16((L.width[3] > 0 ? L.width[3] : 1) * 4);
   s.out = off; off += round16(P * L.row_words * 4);
   s.meta = off; off += round16(G * L.meta_halves * 2);
+  s.kmax = off; off += round16(G * 4);
   s.total = off;
   return s;
 }
@@ -214,6 +215,9 @@ pack_pages_kernel(const __grid_constant__ lf_layout L, const T* __restrict__ src
   int* h16 = reinterpret_cast<int*>(smem + S.h16);          // FP16 slot -> byte offset in a row
   uint32_t* out = reinterpret_cast<uint32_t*>(smem + S.out);
   uint16_t* meta = reinterpret_cast<uint16_t*>(smem + S.meta);
+  // Per group: the largest stored INT2/INT4/INT8 Key scale as fp16 bits
+  // (positive fp16 values order as their bit patterns), raised by every record.
+  unsigned int* kmax_s = reinterpret_cast<unsigned int*>(smem + S.kmax);
 
   const int job = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   const int P = L.page_size, D = L.head_dim, R = L.row_words, M = L.meta_halves;
@@ -253,6 +257,7 @@ pack_pages_kernel(const __grid_constant__ lf_layout L, const T* __restrict__ src
     }
     for (int i = tid; i < G * S.nslot / 2; i += kPackThreads)
       kslot[i] = SlotPair{{-1.0f, -1.0f}, {1.0f, 1.0f}, {0.0f, 0.0f}, {S.pad_off, S.pad_off}};
+    for (int g = tid; g < G; g += kPackThreads) kmax_s[g] = 0u;
   };
   bool tables_done = false;
   if (vec && kPackThreads % (D / kVec) == 0) {
@@ -373,8 +378,10 @@ pack_pages_kernel(const __grid_constant__ lf_layout L, const T* __restrict__ src
         sp.rcp[si & 1] = __frcp_rn(sc);
         sp.lo[si & 1] = lv;
         sp.off[si & 1] = (c0 + e) * static_cast<int>(sizeof(T));
-        meta[g * M + L.scale_off[tier] + local] = float_to_half_bits(sc);
+        const uint16_t sb = float_to_half_bits(sc);
+        meta[g * M + L.scale_off[tier] + local] = sb;
         meta[g * M + L.min_off[tier] + local] = float_to_half_bits(lv);
+        atomicMax(kmax_s + g, static_cast<unsigned int>(sb));
       };
       if (split > 1) {
         // Every lane of the split holds both channels' statistics: parts 0
@@ -443,16 +450,8 @@ pack_pages_kernel(const __grid_constant__ lf_layout L, const T* __restrict__ src
   }
   __syncthreads();
   // Largest stored Key scale of each group over the head's INT2/INT4/INT8
-  // channels (positive fp16 values order as their bit patterns): one warp per
-  // group, lanes over the slots, then a warp maximum.
-  for (int g = tid >> 5; g < G; g += kPackThreads / 32) {
-    uint32_t mx = 0;
-    for (int b = 0; b < 3; ++b)
-      for (int slot = tid & 31; slot < L.width[b]; slot += 32)
-        if (slotmap[b * D + slot] >= 0) mx = max(mx, static_cast<uint32_t>(meta[g * M + L.scale_off[b] + slot]));
-    mx = __reduce_max_sync(0xffffffffu, mx);
-    if ((tid & 31) == 0) meta[g * M + L.kmax_off] = static_cast<uint16_t>(mx);
-  }
+  // channels, gathered by the records' atomic maxima (0 with no such channel).
+  for (int g = tid; g < G; g += kPackThreads) meta[g * M + L.kmax_off] = static_cast<uint16_t>(kmax_s[g]);
 
   // 3. Codes and words, kPackParts threads per token row and role (every
   // kPackParts-th word each): the first kPackRole threads the Key tier words
