@@ -106,50 +106,54 @@ template <> struct Pair<__half> {
 };
 
 // Key statistics of channels c0 .. c0+n-1 (n = 2 for a 16-bit pair, 1 otherwise)
-// of group g over tokens [g kg, (g+1) kg), split over `split` consecutive
-// lanes of full warps: part h takes the stretch of span = kg / split tokens
-// starting at g kg + h span, beginning rot = (32 / split) h tokens in and
-// wrapping around (span >= 32 when split > 1), so the parts of one warp read
-// different banks.  Every lane of the split returns the combined max / min.
-template <typename T>
-__device__ __forceinline__ void key_stats(const unsigned char* xk, int sw, int g, int kg, int c0, int split, int h,
+// of group g over tokens [g kg, (g+1) kg), split over SPLIT consecutive lanes
+// of full warps.  With SPLIT > 1 (kg a multiple of 32), part h takes tokens
+// 32 b + (32 / SPLIT) h + i of every 32-token block b, i < 32 / SPLIT: at each
+// step the parts of one warp are 32 / SPLIT rows apart, so (rows being an odd
+// number of words) they read different banks, and every part runs the same
+// loop.  Every lane of the split returns the combined max / min.
+template <typename T, int SPLIT>
+__device__ __forceinline__ void key_stats(const unsigned char* xk, int sw, int g, int kg, int c0, int h,
                                           float (&hi)[2], float (&lo)[2]) {
-  const int span = kg / split, rot = (32 / split) * h;
-  const int t0 = g * kg + h * span;
+  constexpr int kSub = 32 / SPLIT;
   const int stride = sw * 4;
+  const int t0 = g * kg + (SPLIT > 1 ? kSub * h : 0);
+  // visit(offset): the element of token t0 + offset
+  auto scan = [&](auto visit) {
+    if (SPLIT > 1) {
+      for (int b = 0; b < kg; b += 32) {
+#pragma unroll
+        for (int i = 0; i < kSub; ++i) visit(b + i);
+      }
+    } else {
+#pragma unroll 8
+      for (int j = 0; j < kg; ++j) visit(j);
+    }
+  };
   if constexpr (sizeof(T) == 2) {
     using PR = Pair<T>;
     typename PR::V mx = PR::lowest(), mn = PR::highest();
     const unsigned char* col = xk + c0 * 2 + t0 * stride;
-    auto scan = [&](int j0, int j1) {
-#pragma unroll 8
-      for (int j = j0; j < j1; ++j) {
-        const typename PR::V v = *reinterpret_cast<const typename PR::V*>(col + j * stride);
-        mx = PR::max(mx, v);
-        mn = PR::min(mn, v);
-      }
-    };
-    scan(rot, span);
-    scan(0, rot);
+    scan([&](int j) {
+      const typename PR::V v = *reinterpret_cast<const typename PR::V*>(col + j * stride);
+      mx = PR::max(mx, v);
+      mn = PR::min(mn, v);
+    });
     hi[0] = PR::lo(mx); hi[1] = PR::hi(mx);
     lo[0] = PR::lo(mn); lo[1] = PR::hi(mn);
   } else {
     float mx = -INFINITY, mn = INFINITY;
     const unsigned char* col = xk + c0 * 4 + t0 * stride;
-    auto scan = [&](int j0, int j1) {
-#pragma unroll 8
-      for (int j = j0; j < j1; ++j) {
-        const float v = *reinterpret_cast<const float*>(col + j * stride);
-        mx = fmaxf(mx, v);
-        mn = fminf(mn, v);
-      }
-    };
-    scan(rot, span);
-    scan(0, rot);
+    scan([&](int j) {
+      const float v = *reinterpret_cast<const float*>(col + j * stride);
+      mx = fmaxf(mx, v);
+      mn = fminf(mn, v);
+    });
     hi[0] = hi[1] = mx;
     lo[0] = lo[1] = mn;
   }
-  for (int o = 1; o < split; o <<= 1) {
+#pragma unroll
+  for (int o = 1; o < SPLIT; o <<= 1) {
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       hi[e] = fmaxf(hi[e], __shfl_xor_sync(0xffffffffu, hi[e], o));
@@ -354,7 +358,7 @@ pack_pages_kernel(const __grid_constant__ lf_layout L, const T* __restrict__ src
     // part at least 32 tokens.
     int split = 1;
     for (int s2 = 4; s2 > 1; s2 >>= 1) {
-      if (tasks * s2 <= kPackRole && (tasks * s2) % 32 == 0 && kg % s2 == 0 && kg / s2 >= 32) {
+      if (tasks * s2 <= kPackRole && (tasks * s2) % 32 == 0 && kg % 32 == 0 && kg / s2 >= 32) {
         split = s2;
         break;
       }
@@ -363,7 +367,9 @@ pack_pages_kernel(const __grid_constant__ lf_layout L, const T* __restrict__ src
       const int task = i / split, part = i - task * split;
       const int g = task / ((D + cw - 1) / cw), c0 = (task - g * ((D + cw - 1) / cw)) * cw;
       float hi[2], lo[2];
-      key_stats<T>(xk, sw, g, kg, c0, split, part, hi, lo);
+      if (split == 4) key_stats<T, 4>(xk, sw, g, kg, c0, part, hi, lo);
+      else if (split == 2) key_stats<T, 2>(xk, sw, g, kg, c0, part, hi, lo);
+      else key_stats<T, 1>(xk, sw, g, kg, c0, part, hi, lo);
       // Slot record and meta entries of channel c0 + e.
       auto record = [&](int e, float hv, float lv) {
         if (e >= cw || c0 + e >= D) return;
@@ -471,7 +477,7 @@ pack_pages_kernel(const __grid_constant__ lf_layout L, const T* __restrict__ src
     ksplit = 0;
     while (ksplit < nk) {
       const int c = 2 * (ksplit < nk0 ? 16 : ksplit < nk0 + nk1 ? 8 : 4);
-      if (acc + c > target) break;
+      if (acc + c / 2 > target) break;  // the word goes where more than half of it falls
       acc += c;
       ++ksplit;
     }
