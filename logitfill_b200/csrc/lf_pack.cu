@@ -33,7 +33,7 @@ constexpr int kPackSkip = -1;                 // src_seq of a job that packs not
 // word longer than the row, so every row ends in a zero word (`pad_off`,
 // the element a padding slot reads).
 struct PackSmem {
-  int xk, xv, chan, slotmap, kslot, vstat, h16, out, meta, kmax, total;
+  int xk, xv, chan, kslot, vstat, h16, out, meta, kmax, total;
   int sw;      // staged row stride, 32-bit words
   int pad_off; // byte offset of the zero word in a staged row
   int nslot;   // Key tier slots the row words hold: 16 words0 + 8 words1 + 4 words2
@@ -55,7 +55,6 @@ __host__ __device__ inline PackSmem pack_smem(const lf_layout& L, int esz) {
   s.xk = off; off += round16(P * s.sw * 4);
   s.xv = off; off += round16(P * s.sw * 4);
   s.chan = off; off += round16(D * 4);
-  s.slotmap = off; off += round16(4 * D * 4);
   s.kslot = off; off += G * (s.nslot > 0 ? s.nslot : 2) * 16;
   s.vstat = off; off += P * NV * 16;
   s.h16 = off; off += round16((L.width[3] > 0 ? L.width[3] : 1) * 4);
@@ -213,7 +212,6 @@ pack_pages_kernel(const __grid_constant__ lf_layout L, const T* __restrict__ src
   unsigned char* xk = smem + S.xk;
   unsigned char* xv = smem + S.xv;
   int* chan = reinterpret_cast<int*>(smem + S.chan);        // chan_code of the head
-  int* slotmap = reinterpret_cast<int*>(smem + S.slotmap);  // [tier][slot] -> channel or -1
   SlotPair* kslot = reinterpret_cast<SlotPair*>(smem + S.kslot);
   float4* vstat = reinterpret_cast<float4*>(smem + S.vstat);  // [token][v group]: scale, rcp, min
   int* h16 = reinterpret_cast<int*>(smem + S.h16);          // FP16 slot -> byte offset in a row
@@ -250,7 +248,7 @@ pack_pages_kernel(const __grid_constant__ lf_layout L, const T* __restrict__ src
   // in flight.
   const int chv = tid < D ? chan_code[h * D + tid] : 0;
   auto init_tables = [&]() {
-    for (int i = tid; i < 4 * D; i += kPackThreads) slotmap[i] = -1;
+    for (int i = tid; i < L.width[3]; i += kPackThreads) h16[i] = S.pad_off;  // padding slots read 0
     for (int i = tid; i < G * M; i += kPackThreads) {
       const int e = i % M;
       // Padding channels of a tier keep scale 1.0 and min 0 (layout.py:84-85).
@@ -335,16 +333,12 @@ pack_pages_kernel(const __grid_constant__ lf_layout L, const T* __restrict__ src
   if (tid < D) chan[tid] = chv;
   for (int c = tid + kPackThreads; c < D; c += kPackThreads) chan[c] = chan_code[h * D + c];
   __syncthreads();
+  // FP16 tier slot -> byte offset of its channel in a staged row (read by the
+  // code phase, after the statistics' barrier).
   for (int c = tid; c < D; c += kPackThreads) {
     const int code = chan[c];
-    const int tier = code >> 16, local = code & 0xFFFF;
-    if (tier >= 0 && tier < 4 && local < L.width[tier]) slotmap[tier * D + local] = c;
-  }
-  for (int i = tid; i < L.width[3]; i += kPackThreads) h16[i] = S.pad_off;
-  __syncthreads();
-  for (int i = tid; i < L.width[3]; i += kPackThreads) {
-    const int c = slotmap[3 * D + i];
-    if (c >= 0) h16[i] = c * static_cast<int>(sizeof(T));
+    const int local = code & 0xFFFF;
+    if ((code >> 16) == 3 && local < L.width[3]) h16[local] = c * static_cast<int>(sizeof(T));
   }
 
   // 2. Statistics.  Threads 0..127: Key channel (pairs of 16-bit elements)
